@@ -1,0 +1,186 @@
+/* nc_cuda.h -- the C ABI of libnc_cuda.so, the B200 (sm_100a) backend for nanocompile's
+ * Qwen2 decode step.
+ *
+ * Two layers, both plain C: pointers, sizes, int32 status codes.
+ *
+ *  1. Fused-group entry points.  nanocompile's generated C exports one function per
+ *     fused kernel with the signature  int32_t nc_kN(void **p, const int64_t *s)
+ *     (nanocompile/codegen_c.py:3-10, nanocompile/loopir.py:329-336): p[0] is the
+ *     output, p[1..] the operands, s the symbol values, 0 = OK.  The functions below
+ *     keep that convention -- p[] holds DEVICE pointers, s[] the sizes -- and add the
+ *     CUDA stream to launch on (NULL = the default stream).  One per fused group kind
+ *     of an int8-vnni Qwen2 step (nanocompile/fusion.py:417-731).
+ *
+ *  2. The model runtime, the CUDA twin of nanocompile/runtime.py:167-318
+ *     (CompiledGraph: compile once, then call per step): one device arena holding the
+ *     weights, the KV cache of every sequence slot and the activations; a step is a
+ *     fixed sequence of fused kernels, captured once as a CUDA graph and replayed.
+ *
+ * Every function returns 0 on success or a nonzero NC_* code; nc_last_error() gives
+ * the message of the last failure on the calling thread.  No function calls back into
+ * the caller.  One host thread should drive one model at a time.
+ */
+#ifndef NC_CUDA_H
+#define NC_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    NC_OK = 0,
+    NC_ERR_KERNEL = 1,      /* a kernel rejected its input (gather index out of range), as
+                               the reference's kernel status 1 (nanocompile/runtime.py:298-318) */
+    NC_ERR_ARGUMENT = 2,    /* bad sizes, names, capacity exceeded */
+    NC_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+    NC_ERR_STATE = 4,       /* call out of order (e.g. step before every weight is uploaded) */
+};
+
+/* The message of the last failure on this thread; returns its full length. */
+int32_t nc_last_error(char *buf, int64_t size);
+
+/* Library / device plumbing (device memory for the fused-group entry points). */
+int32_t nc_device_count(int32_t *count);
+int32_t nc_set_device(int32_t device);
+int32_t nc_device_alloc(int64_t bytes, void **ptr);
+int32_t nc_device_free(void *ptr);
+int32_t nc_copy_to_device(void *dst, const void *src, int64_t bytes);
+int32_t nc_copy_to_host(void *dst, const void *src, int64_t bytes);
+int32_t nc_device_synchronize(void);
+
+/* ---- 1. fused groups (device pointers; s[] sizes; stream may be NULL) -------------------- */
+
+/* gather (nanocompile/fusion.py:713-731, call 0): rows of the embedding table by token id.
+ * p: [0] out f32[rows, hidden]  [1] ids i64[rows]  [2] table f32[vocab, hidden]
+ *    [3] error word i64[2] (device; [0] = 1 + first bad row, [1] = its id; zero it first)
+ * s: rows, vocab, hidden */
+int32_t nc_gather_rows(void **p, const int64_t *s, void *stream);
+
+/* row kernel rms_norm (nanocompile/nn.py:34-38 -> fusion.py:631-650, calls 1/25/40), in the
+ * reference's order (in-order float32 sum of squares), fused with block-32 activation
+ * quantization (nanocompile/quantize.py:102-124, calls 2-7).
+ * p: [0] normed f32[rows, n] (nullable)  [1] x f32[rows, n]  [2] weight f32[n]
+ *    [3] xq i8[rows, n] (nullable: no quantization)  [4] xs f32[rows, n/32]  [5] offset f32[rows]
+ *    [6] block sums i32[rows, n/32] (nullable)
+ * s: rows, n, eps as float32 bits */
+int32_t nc_rms_norm_quantize(void **p, const int64_t *s, void *stream);
+
+/* block-32 activation quantization alone (calls 18-23, 33-38).
+ * p: [0] xq i8[rows, k]  [1] x f32[rows, k]  [2] xs f32[rows, k/32]  [3] offset f32[rows]
+ *    [4] block sums i32[rows, k/32] (nullable)
+ * s: rows, k */
+int32_t nc_quantize_blocks(void **p, const int64_t *s, void *stream);
+
+/* matmul_i8_vnni with its epilogue (nanocompile/lower.py:363-397, fusion.py:677-711; calls
+ * 8/12/16/24/32/39), bit-exact: 32 float32 accumulators per output, one per 4-byte Dp4 lane,
+ * FMA'd by the block scale in the reference's k order, combined in its order.
+ * Weights are the reference's int8 values offset by 128 (w ^ 0x80, as unsigned bytes; see
+ * nc_pack_int8_weights).
+ * p: [0] out f32[rows, n]  [1] xq i8[rows, k]  [2] xs f32[rows, k/32]  [3] offset f32[rows]
+ *    [4] w u8[n, k]  [5] scales f32[n]  [6] epilogue operand (bias f32[n] / residual
+ *    f32[rows, n] / second weight u8[n, k] for SwiGLU)  [7] second scales f32[n] (SwiGLU)
+ * s: rows, n, k, epilogue (0 none, 1 bias, 2 residual, 3 silu(y0) * y1) */
+int32_t nc_matmul_i8_vnni(void **p, const int64_t *s, void *stream);
+
+/* float32 matmul with epilogue (nanocompile/lower.py:255-274, fusion.py:652-675):
+ * acc = acc + x[k] * w[n, k] in index order, no FMA.
+ * p: [0] out f32[rows, n]  [1] x f32[rows, k]  [2] w f32[n, k]  [3] epilogue operand
+ *    (bias / residual / second weight)
+ * s: rows, n, k, epilogue (as above) */
+int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream);
+
+/* The tied LM head (call 41) fused with greedy argmax (nanocompile/models/qwen2.py:364,
+ * first maximum wins): logits = x @ embed.T in index order per row, then the argmax of
+ * each row.  Scratch holds one (value, index) pair per (row, CTA): nc_lm_head_scratch_bytes.
+ * p: [0] logits f32[rows, vocab] (nullable)  [1] x f32[rows, hidden]  [2] embed f32[vocab, hidden]
+ *    [3] tokens i64[rows] (nullable)  [4] scratch (device, >= nc_lm_head_scratch_bytes)
+ * s: rows, vocab, hidden */
+int32_t nc_lm_head_argmax(void **p, const int64_t *s, void *stream);
+int64_t nc_lm_head_scratch_bytes(int64_t rows, int64_t vocab);
+
+/* Decode attention over a KV cache (calls 14-17 with RoPE calls 9-13 fused in): for one new
+ * token per row, bias is already in qkv; RoPE q and k, append k/v to the cache at the row's
+ * position, scores in index order, softmax (NaN-propagating max, in-order sum of expf),
+ * probabilities @ V in index order.
+ * p: [0] ctx f32[rows, heads*d]  [1] qkv f32[rows, (heads+2*kv)*d] (biased projections)
+ *    [2] cache f32 (layout: slot, {K,V}, kv, capacity, d -- this layer's)  [3] cos f32[cap, d/2]
+ *    [4] sin f32[cap, d/2]  [5] slot i32[rows]  [6] pos i32[rows]
+ * s: rows, heads, kv_heads, d, capacity, slot stride (floats), append (1 = write k/v),
+ *    attention scale as float32 bits */
+int32_t nc_attention(void **p, const int64_t *s, void *stream);
+
+/* int8 weights as the kernels read them: u8 = int8 + 128 (one XOR per byte). */
+int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t bytes);
+
+/* glibc's expf, bit for bit, evaluated on the device (test hook for the softmax / SiLU math).
+ * p: [0] out f32[n]  [1] x f32[n];  s: n */
+int32_t nc_expf_exact(void **p, const int64_t *s, void *stream);
+
+/* ---- 2. the model runtime ---------------------------------------------------------------- */
+
+typedef struct nc_model nc_model;
+
+typedef struct {
+    int64_t vocab, hidden, inter, layers, heads, kv_heads, head_dim;
+    float eps;            /* float32(rms_norm_eps) */
+    float attn_scale;     /* float32(head_dim ** -0.5) */
+    int32_t quant;        /* 0 = float32 projections, 1 = int8-vnni */
+    int32_t max_rows;     /* token rows per step (prompt length, or sequences in a batch) */
+    int32_t slots;        /* KV-cache sequence slots */
+    int32_t capacity;     /* KV positions per slot */
+    int32_t device;       /* CUDA device ordinal */
+} nc_qwen2_config;
+
+/* Allocates the arena on cfg->device.  inv_freq: float32[head_dim/2], RoPE's rates
+ * (nanocompile/nn.py:69-75); cos/sin tables of every position are made from it here with
+ * the C library's cosf/sinf, the same functions the reference's generated C calls. */
+int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_freq, nc_model **out);
+int32_t nc_qwen2_destroy(nc_model *model);
+int64_t nc_qwen2_arena_bytes(const nc_model *model);
+
+/* Upload one weight by its checkpoint name (int8 ones as "<name>@int8" / "<name>@scales",
+ * nanocompile/quantize.py:47-52).  Returns NC_ERR_ARGUMENT for an unknown name or size. */
+int32_t nc_qwen2_upload(nc_model *model, const char *name, const void *host, int64_t bytes);
+int32_t nc_qwen2_missing_weights(const nc_model *model, int32_t *count);
+
+/* KV cache of one slot: positions [start, start+count) of every layer, host arrays
+ * [layers, kv_heads, count, head_dim]. */
+int32_t nc_qwen2_kv_write(nc_model *model, int32_t slot, int64_t start, int64_t count,
+                          const float *keys, const float *values);
+int32_t nc_qwen2_kv_read(nc_model *model, int32_t slot, int64_t start, int64_t count,
+                         float *keys, float *values);
+
+/* One step on `rows` token rows: row r is token ids[r] of sequence slot[r] at position
+ * pos[r] (its KV history is positions 0..pos[r]-1 of that slot).  Rows of one slot must be
+ * consecutive positions in order (a prompt); a slot may also appear once (decode).
+ * Logits are produced for the `logit_rows` rows listed in logit_row[] (host), into
+ * logits (host, nullable) [logit_rows, vocab], with the argmax of each into tokens (host,
+ * nullable).  Returns NC_ERR_KERNEL for an id outside 0..vocab-1; *bad_row (nullable)
+ * gets the first such row. */
+int32_t nc_qwen2_step(nc_model *model, int32_t rows, const int64_t *ids, const int32_t *slot,
+                      const int32_t *pos, int32_t logit_rows, const int32_t *logit_row,
+                      float *logits, int64_t *tokens, int32_t *bad_row);
+
+/* Greedy decode of `batch` sequences, one new token each per step, for `steps` steps: row b
+ * starts from token first[b] at position start[b] of slot[b].  Each step is one replay of a
+ * captured CUDA graph; the argmax feeds the next step on the device.  tokens (host)
+ * [steps, batch]; logits (host, nullable) [batch, vocab] of the last step.
+ * Per-step streaming: with per_step != 0 every step copies its tokens to the host and
+ * synchronizes (the host-visible path); otherwise one copy at the end. */
+int32_t nc_qwen2_decode(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
+                        const int32_t *start, int32_t steps, int32_t per_step, int64_t *tokens,
+                        float *logits);
+
+/* Timing hook for benchmarks: runs `steps` replays of the captured decode graph for the
+ * current device-side state, timed with CUDA events on the model's stream; *ms gets the
+ * elapsed milliseconds.  Also reports the average duration of the LM-head kernel and the
+ * i8 GEMV of the last replay window (nullable). */
+int32_t nc_qwen2_decode_timed(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
+                              const int32_t *start, int32_t steps, float *ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

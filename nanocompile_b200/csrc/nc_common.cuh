@@ -1,0 +1,133 @@
+// nc_common.cuh -- device helpers shared by the kernels.
+//
+// Everything here computes exactly what nanocompile's generated C computes (that code is
+// compiled with -ffp-contract=off, nanocompile/codegen_c.py:50).  This file is compiled with
+// -fmad=false, and the order-sensitive arithmetic is spelled with explicit round-to-nearest
+// intrinsics so no contraction or reassociation can change a bit.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nc {
+
+constexpr int QBLOCK = 32;     // nanocompile/quantize.py:43, activation scale block
+constexpr int CHUNK = 128;     // nanocompile/lower.py:360 VNNI_STRIDE: four 32-byte groups
+
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+
+// ---- glibc's expf ------------------------------------------------------------------------
+// The softmax and SiLU of the reference call the C library's expf.  glibc (2.28+) computes it
+// with the table-driven method of ARM's optimized-routines: x * 32/ln2 = k + r, then
+// exp(x) = 2^(k/32) * p(r) with a cubic p, all in double, rounded once to float.  This is a
+// restatement of that method (the table is 2^(i/32) from its definition, with the exponent
+// bits of i/32 folded out); the remainder is a fused multiply-subtract as in glibc's FMA
+// build.  Every float input in (-103.9, 88.7) gives glibc's bits (checked on the CPU for all
+// 2.24e9 of them, and on the device by the tests).
+__device__ __constant__ uint64_t kExpTab[32] = {
+    0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL,
+    0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL,
+    0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL,
+    0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL,
+    0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL,
+    0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL,
+    0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL,
+    0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL};
+
+__device__ __forceinline__ float expf_exact(float x, const uint64_t *tab) {
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ff;
+    if (abstop >= 0x42b) {                          // |x| >= 88, inf or nan
+        if (ux == 0xff800000u) return 0.0f;          // exp(-inf)
+        if (abstop >= 0x7f8) return x + x;           // +inf, nan
+        if (x > 0x1.62e42ep6f) return __uint_as_float(0x7f800000u);
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double inv_ln2_32 = 0x1.71547652b82fep+0 * 32;
+    const double shift = 0x1.8p+52;
+    const double c0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;
+    const double c1 = 0x1.ebfce50fac4f3p-3 / 32 / 32;
+    const double c2 = 0x1.62e42ff0c52d6p-1 / 32;
+    const double xd = (double)x;
+    const double z = __dmul_rn(inv_ln2_32, xd);
+    double kd = __dadd_rn(z, shift);
+    const uint64_t ki = (uint64_t)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(inv_ln2_32, xd, -kd);
+    const uint64_t t = tab[ki & 31] + (ki << 47);
+    const double s = __longlong_as_double((long long)t);
+    const double p = __fma_rn(c0, r, c1);
+    double y = __fma_rn(c2, r, 1.0);
+    y = __fma_rn(p, __dmul_rn(r, r), y);
+    return __double2float_rn(__dmul_rn(y, s));
+}
+
+// ---- int8 lanes ---------------------------------------------------------------------------
+// nanocompile/codegen_c.py:85-89 nc_dp4: sum over 4 bytes of (w + 128) * x.  The weights are
+// stored already offset (u8 = w ^ 0x80), so one dp4a.u32.s32 gives the lane.  Seeding the
+// accumulator with the bits of 1.5 * 2^23 makes the result the float 12582912 + v exactly
+// (|v| <= 4 * 255 * 127 < 2^22), so int -> float is one exact subtraction, not a conversion.
+__device__ __forceinline__ float dp4_lane(uint32_t w_u8x4, uint32_t x_s8x4) {
+    int32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(w_u8x4), "r"(x_s8x4), "r"(0x4B400000));
+    return __fsub_rn(__int_as_float(d), 12582912.0f);
+}
+
+// ---- reductions -------------------------------------------------------------------------
+// The reference's max: acc = (acc < v || v != v) ? v : acc (nanocompile/fusion.py:603-610).
+// Any NaN wins; otherwise the maximum, independent of order (only +-0 compare equal with
+// different bits, and both give the same downstream result).
+__device__ __forceinline__ float nan_max(float acc, float v) { return (acc < v || v != v) ? v : acc; }
+
+__device__ __forceinline__ float warp_nan_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = nan_max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// nanocompile/lower.py:298-317 _combine: (acc0+acc1)+(acc2+acc3) lane by lane, then lanes j
+// and j+4, then two hadds.
+__device__ __forceinline__ float combine32(const float *acc) {
+    float h[8];
+#pragma unroll
+    for (int kh = 0; kh < 8; ++kh) h[kh] = fadd(fadd(acc[kh], acc[8 + kh]), fadd(acc[16 + kh], acc[24 + kh]));
+    return fadd(fadd(fadd(h[0], h[4]), fadd(h[1], h[5])), fadd(fadd(h[2], h[6]), fadd(h[3], h[7])));
+}
+
+// nanocompile/nn.py:41-55: silu(g) * u with e = expf(-|g|), sigma = (g >= 0 ? 1 : e) / (1 + e).
+__device__ __forceinline__ float swiglu(float g, float u, const uint64_t *tab) {
+    const bool nonneg = 0.0f <= g;
+    const float e = expf_exact(nonneg ? -g : g, tab);
+    const float sig = fdiv(nonneg ? 1.0f : e, fadd(e, 1.0f));
+    return fmul(fmul(g, sig), u);
+}
+
+// One 32-value block of block-32 quantization by one warp, lane = position in the block
+// (nanocompile/quantize.py:102-124): returns the scale; *q the lane's int8 and *bsum the
+// block's int32 sum.
+__device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bsum) {
+    const float a = (0.0f <= v) ? v : -v;
+    const float mag = warp_nan_max(a);
+    const float scale = (mag <= 0.0f) ? 1.0f : fdiv(mag, 127.0f);
+    float t = roundf(fdiv(v, scale));
+    t = (t <= 127.0f) ? t : 127.0f;
+    t = (-127.0f <= t) ? t : -127.0f;
+    const int8_t qi = (int8_t)t;
+    *q = qi;
+    *bsum = warp_sum_int((int)qi);
+    return scale;
+}
+
+// ---- epilogues ----------------------------------------------------------------------------
+enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3 };
+
+}  // namespace nc

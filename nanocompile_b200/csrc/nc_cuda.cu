@@ -1,0 +1,828 @@
+// nc_cuda.cu -- libnc_cuda.so: the C ABI of include/nc_cuda.h.
+//
+// The model runtime is the CUDA twin of nanocompile/runtime.py's CompiledGraph
+// (nanocompile/runtime.py:167-318): built once per model, then called per step.  The
+// reference plans an arena per call and crosses the FFI once per fused kernel
+// (runtime.py:281-299); here one device arena is laid out at creation, every step is the
+// same fixed sequence of fused kernels reading its sizes from device memory, and decode
+// steps replay one captured CUDA graph.
+#include "../../include/nc_cuda.h"
+#include "nc_kernels.cuh"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <set>
+#include <string>
+#include <vector>
+
+using namespace nc;
+
+// ---- errors ---------------------------------------------------------------------------------
+static thread_local std::string g_error;
+
+static int32_t fail(int32_t code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                       \
+    do {                                                                                     \
+        cudaError_t e_ = (expr);                                                             \
+        if (e_ != cudaSuccess)                                                               \
+            return fail(NC_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), \
+                        __FILE__, __LINE__);                                                 \
+    } while (0)
+
+#define NC_TRY(expr)                  \
+    do {                              \
+        int32_t s_ = (expr);          \
+        if (s_ != NC_OK) return s_;   \
+    } while (0)
+
+extern "C" int32_t nc_last_error(char *buf, int64_t size) {
+    if (buf && size > 0) {
+        std::snprintf(buf, (size_t)size, "%s", g_error.c_str());
+    }
+    return (int32_t)g_error.size();
+}
+
+extern "C" int32_t nc_device_count(int32_t *count) {
+    int n = 0;
+    CUDA_TRY(cudaGetDeviceCount(&n));
+    *count = n;
+    return NC_OK;
+}
+extern "C" int32_t nc_set_device(int32_t device) {
+    CUDA_TRY(cudaSetDevice(device));
+    return NC_OK;
+}
+extern "C" int32_t nc_device_alloc(int64_t bytes, void **ptr) {
+    CUDA_TRY(cudaMalloc(ptr, (size_t)(bytes > 0 ? bytes : 1)));
+    return NC_OK;
+}
+extern "C" int32_t nc_device_free(void *ptr) {
+    CUDA_TRY(cudaFree(ptr));
+    return NC_OK;
+}
+extern "C" int32_t nc_copy_to_device(void *dst, const void *src, int64_t bytes) {
+    CUDA_TRY(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyHostToDevice));
+    return NC_OK;
+}
+extern "C" int32_t nc_copy_to_host(void *dst, const void *src, int64_t bytes) {
+    CUDA_TRY(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost));
+    return NC_OK;
+}
+extern "C" int32_t nc_device_synchronize(void) {
+    CUDA_TRY(cudaDeviceSynchronize());
+    return NC_OK;
+}
+
+// ---- kernel launchers (shared by the fused-group ABI and the model) -------------------------
+namespace {
+
+template <typename K>
+cudaError_t allow_smem(K kernel, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+int32_t check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(NC_ERR_CUDA, "launching %s: %s", what, cudaGetErrorString(e));
+    return NC_OK;
+}
+
+int32_t launch_norm(cudaStream_t st, float *normed, const float *x, const float *w, int8_t *xq, float *xs,
+                    float *off, int32_t *bsums, const int32_t *row_map, int rows, int n, float eps) {
+    if (rows <= 0) return NC_OK;
+    if (n > 8192 || (xq && n % QBLOCK)) return fail(NC_ERR_ARGUMENT, "rms_norm width %d unsupported", n);
+    const size_t smem = sizeof(float) * 2 * (size_t)n;
+    CUDA_TRY(allow_smem(norm_quant_kernel, smem));
+    norm_quant_kernel<<<rows, NORM_THREADS, smem, st>>>(normed, x, w, xq, xs, off, bsums, row_map, n, eps);
+    return check_launch("norm_quant_kernel");
+}
+
+int32_t launch_quant(cudaStream_t st, int8_t *xq, const float *x, float *xs, float *off, int32_t *bsums,
+                     int rows, int k) {
+    if (rows <= 0) return NC_OK;
+    if (k % QBLOCK || k > 8192) return fail(NC_ERR_ARGUMENT, "quantize width %d unsupported", k);
+    quantize_kernel<<<rows, NORM_THREADS, 0, st>>>(xq, x, xs, off, bsums, k);
+    return check_launch("quantize_kernel");
+}
+
+template <int LPR, int TOK, int UNROLL>
+int32_t launch_i8_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
+    constexpr int WARPS = 4, RPW = 32 / LPR;
+    const int grid = (a.n + WARPS * RPW - 1) / (WARPS * RPW);
+    switch (epi) {
+        case EPI_NONE: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_NONE><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_BIAS: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_BIAS><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_RESIDUAL: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_RESIDUAL><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_SWIGLU: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_SWIGLU><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+    return check_launch("gemv_i8_kernel");
+}
+
+int32_t launch_i8(cudaStream_t st, const GemvI8Args &a, int epi) {
+    if (a.m <= 0 || a.n <= 0) return NC_OK;
+    if (a.k % QBLOCK) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a whole number of 32-blocks", a.k);
+    const bool long_k = a.k > 1024;
+    if (a.m == 1) {
+        return long_k ? launch_i8_epi<32, 1, 16>(st, a, epi) : launch_i8_epi<8, 1, 8>(st, a, epi);
+    }
+    return long_k ? launch_i8_epi<32, 4, 16>(st, a, epi) : launch_i8_epi<8, 4, 8>(st, a, epi);
+}
+
+template <int TOK, int EPI, bool ARGMAX>
+int32_t launch_f32_t(cudaStream_t st, const GemvF32Args &a) {
+    constexpr int NW = EPI == EPI_SWIGLU ? 2 : 1;
+    const size_t smem = sizeof(float4) * F32_STAGES * (NW * F32_ROWS * (F32_TILE / 4) + TOK * (F32_TILE / 4));
+    auto kernel = gemv_f32_kernel<TOK, EPI, ARGMAX>;
+    CUDA_TRY(allow_smem(kernel, smem));
+    const int grid = (a.n + F32_ROWS - 1) / F32_ROWS;
+    kernel<<<grid, F32_ROWS, smem, st>>>(a);
+    return check_launch("gemv_f32_kernel");
+}
+
+template <int TOK>
+int32_t launch_f32_tok(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) {
+    if (argmax) return launch_f32_t<TOK, EPI_NONE, true>(st, a);
+    switch (epi) {
+        case EPI_NONE: return launch_f32_t<TOK, EPI_NONE, false>(st, a);
+        case EPI_BIAS: return launch_f32_t<TOK, EPI_BIAS, false>(st, a);
+        case EPI_RESIDUAL: return launch_f32_t<TOK, EPI_RESIDUAL, false>(st, a);
+        case EPI_SWIGLU: return launch_f32_t<TOK, EPI_SWIGLU, false>(st, a);
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+}
+
+int32_t launch_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) {
+    if (a.m <= 0 || a.n <= 0) return NC_OK;
+    if (a.k % F32_TILE) return fail(NC_ERR_ARGUMENT, "float32 width %d is not a multiple of %d", a.k, F32_TILE);
+    if (argmax && epi != EPI_NONE) return fail(NC_ERR_ARGUMENT, "argmax takes no epilogue");
+    return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<8>(st, a, epi, argmax);
+}
+
+size_t attention_smem(int group, int d, int cap) {
+    return sizeof(float) * ((size_t)(group + 2) * d + 2 * (size_t)group + (size_t)group * cap);
+}
+
+int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
+    if (rows <= 0) return NC_OK;
+    const int group = a.heads / a.kv;
+    if (group > 8 || a.heads % a.kv || a.d % 4) return fail(NC_ERR_ARGUMENT, "attention shape unsupported");
+    const size_t smem = attention_smem(group, a.d, a.cap);
+    if (smem > 220 * 1024) return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
+    CUDA_TRY(allow_smem(attention_kernel, smem));
+    attention_kernel<<<rows * a.kv, ATTN_THREADS, smem, st>>>(a);
+    return check_launch("attention_kernel");
+}
+
+float f32_from_bits(int64_t bits) {
+    uint32_t u = (uint32_t)bits;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+}  // namespace
+
+// ---- 1. fused-group entry points -------------------------------------------------------------
+
+extern "C" int32_t nc_gather_rows(void **p, const int64_t *s, void *stream) {
+    const int rows = (int)s[0];
+    if (rows <= 0) return NC_OK;
+    gather_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>((float *)p[0], (const int64_t *)p[1], (const float *)p[2],
+                                                          (unsigned long long *)p[3], s[1], (int)s[2]);
+    return check_launch("gather_kernel");
+}
+
+extern "C" int32_t nc_rms_norm_quantize(void **p, const int64_t *s, void *stream) {
+    return launch_norm((cudaStream_t)stream, (float *)p[0], (const float *)p[1], (const float *)p[2], (int8_t *)p[3],
+                       (float *)p[4], (float *)p[5], (int32_t *)p[6], nullptr, (int)s[0], (int)s[1],
+                       f32_from_bits(s[2]));
+}
+
+extern "C" int32_t nc_quantize_blocks(void **p, const int64_t *s, void *stream) {
+    return launch_quant((cudaStream_t)stream, (int8_t *)p[0], (const float *)p[1], (float *)p[2], (float *)p[3],
+                        (int32_t *)p[4], (int)s[0], (int)s[1]);
+}
+
+extern "C" int32_t nc_matmul_i8_vnni(void **p, const int64_t *s, void *stream) {
+    GemvI8Args a{};
+    a.out = (float *)p[0];
+    a.xq = (const int8_t *)p[1];
+    a.xs = (const float *)p[2];
+    a.offset = (const float *)p[3];
+    a.w = (const uint8_t *)p[4];
+    a.scales = (const float *)p[5];
+    a.m = (int)s[0];
+    a.n = (int)s[1];
+    a.k = (int)s[2];
+    const int epi = (int)s[3];
+    if (epi == EPI_BIAS) a.bias = (const float *)p[6];
+    if (epi == EPI_RESIDUAL) a.residual = (const float *)p[6];
+    if (epi == EPI_SWIGLU) {
+        a.w2 = (const uint8_t *)p[6];
+        a.scales2 = (const float *)p[7];
+    }
+    return launch_i8((cudaStream_t)stream, a, epi);
+}
+
+extern "C" int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream) {
+    GemvF32Args a{};
+    a.out = (float *)p[0];
+    a.x = (const float *)p[1];
+    a.w = (const float *)p[2];
+    a.m = (int)s[0];
+    a.n = (int)s[1];
+    a.k = (int)s[2];
+    const int epi = (int)s[3];
+    if (epi == EPI_BIAS) a.bias = (const float *)p[3];
+    if (epi == EPI_RESIDUAL) a.residual = (const float *)p[3];
+    if (epi == EPI_SWIGLU) a.w2 = (const float *)p[3];
+    return launch_f32((cudaStream_t)stream, a, epi, false);
+}
+
+extern "C" int64_t nc_lm_head_scratch_bytes(int64_t rows, int64_t vocab) {
+    const int64_t ctas = (vocab + F32_ROWS - 1) / F32_ROWS;
+    return 256 + rows * ctas * (int64_t)(sizeof(float) + sizeof(int32_t));
+}
+
+extern "C" int32_t nc_lm_head_argmax(void **p, const int64_t *s, void *stream) {
+    GemvF32Args a{};
+    a.out = (float *)p[0];
+    a.x = (const float *)p[1];
+    a.w = (const float *)p[2];
+    a.tokens = (int64_t *)p[3];
+    a.m = (int)s[0];
+    a.n = (int)s[1];
+    a.k = (int)s[2];
+    const int64_t ctas = (a.n + F32_ROWS - 1) / F32_ROWS;
+    char *scratch = (char *)p[4];
+    a.counter = (unsigned int *)scratch;
+    a.part_val = (float *)(scratch + 256);
+    a.part_idx = (int32_t *)(scratch + 256 + a.m * ctas * sizeof(float));
+    if (!a.tokens) return launch_f32((cudaStream_t)stream, a, EPI_NONE, false);
+    return launch_f32((cudaStream_t)stream, a, EPI_NONE, true);
+}
+
+extern "C" int32_t nc_attention(void **p, const int64_t *s, void *stream) {
+    AttnArgs a{};
+    a.ctx = (float *)p[0];
+    a.qkv = (const float *)p[1];
+    a.cache = (float *)p[2];
+    a.cos_tab = (const float *)p[3];
+    a.sin_tab = (const float *)p[4];
+    a.slot = (const int32_t *)p[5];
+    a.pos = (const int32_t *)p[6];
+    const int rows = (int)s[0];
+    a.heads = (int)s[1];
+    a.kv = (int)s[2];
+    a.d = (int)s[3];
+    a.cap = (int)s[4];
+    a.slot_stride = s[5];
+    a.mode = s[6] ? 0 : 2;
+    a.scale = f32_from_bits(s[7]);
+    return launch_attention((cudaStream_t)stream, a, rows);
+}
+
+extern "C" int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t bytes) {
+    CUDA_TRY(cudaMemcpy(dst_device, src_host, (size_t)bytes, cudaMemcpyHostToDevice));
+    xor80_kernel<<<1024, 256>>>((uint8_t *)dst_device, bytes);
+    NC_TRY(check_launch("xor80_kernel"));
+    CUDA_TRY(cudaDeviceSynchronize());
+    return NC_OK;
+}
+
+extern "C" int32_t nc_expf_exact(void **p, const int64_t *s, void *stream) {
+    if (s[0] <= 0) return NC_OK;
+    expf_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>((float *)p[0], (const float *)p[1], s[0]);
+    return check_launch("expf_kernel");
+}
+
+// ---- 2. the model runtime ----------------------------------------------------------------------
+
+struct WeightSlot {
+    char *dst;
+    int64_t bytes;
+    bool int8;      // stored as int8 + 128
+};
+
+struct nc_model {
+    nc_qwen2_config c{};
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    char *arena = nullptr;
+    int64_t arena_bytes = 0;
+    std::map<std::string, WeightSlot> weights;
+    std::set<std::string> uploaded;
+
+    // weights
+    float *embed = nullptr, *final_norm = nullptr, *cos_tab = nullptr, *sin_tab = nullptr;
+    struct Layer {
+        float *in_norm, *post_norm, *bqkv;
+        uint8_t *wqkv, *wo, *wg, *wu, *wd;    // int8 mode
+        float *sqkv, *so, *sg, *su, *sd;
+        float *fqkv, *fo, *fg, *fu, *fd;      // float32 mode
+    };
+    std::vector<Layer> layers;
+    float *kv = nullptr;            // [slot][layer][2][kv][cap][d]
+    int64_t slot_stride = 0, layer_stride = 0;
+
+    // activations and step state
+    float *x = nullptr, *normed = nullptr, *xs = nullptr, *off = nullptr, *qkv = nullptr, *ctx = nullptr,
+          *hbuf = nullptr, *logits = nullptr, *part_val = nullptr;
+    int8_t *xq = nullptr;
+    int32_t *part_idx = nullptr, *slot = nullptr, *pos = nullptr, *logit_row = nullptr, *step = nullptr;
+    int64_t *ids = nullptr, *tokens = nullptr, *history = nullptr;
+    unsigned long long *err = nullptr;
+    unsigned int *counter = nullptr;
+    int history_steps = 0;
+
+    std::map<int, cudaGraphExec_t> decode_graphs;   // by batch size
+};
+
+namespace {
+
+int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Arena layout: a bump allocator over one cudaMalloc, 256-byte aligned pieces.
+struct Layout {
+    int64_t top = 0;
+    std::vector<std::pair<void **, int64_t>> pieces;
+    template <typename T>
+    void add(T **ptr, int64_t bytes) {
+        pieces.push_back({(void **)ptr, top});
+        top = align_up(top + std::max<int64_t>(bytes, 1), 256);
+    }
+};
+
+int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
+    const nc_qwen2_config &c = m->c;
+    cudaStream_t st = m->stream;
+    const int H = (int)c.hidden, I = (int)c.inter, d = (int)c.head_dim;
+    const int Hq = (int)(c.heads * d), Nqkv = (int)((c.heads + 2 * c.kv_heads) * d);
+    const bool q8 = c.quant != 0;
+
+    CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
+    gather_kernel<<<rows, 256, 0, st>>>(m->x, m->ids, m->embed, m->err, c.vocab, H);
+    NC_TRY(check_launch("gather_kernel"));
+
+    for (int l = 0; l < (int)c.layers; ++l) {
+        const nc_model::Layer &L = m->layers[l];
+        // input norm (+ quantize) -> q/k/v projections with their biases
+        NC_TRY(launch_norm(st, q8 ? nullptr : m->normed, m->x, L.in_norm, q8 ? m->xq : nullptr, m->xs, m->off,
+                           nullptr, nullptr, rows, H, c.eps));
+        if (q8) {
+            GemvI8Args a{};
+            a.out = m->qkv; a.xq = m->xq; a.xs = m->xs; a.offset = m->off; a.w = L.wqkv; a.scales = L.sqkv;
+            a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
+            NC_TRY(launch_i8(st, a, EPI_BIAS));
+        } else {
+            GemvF32Args a{};
+            a.out = m->qkv; a.x = m->normed; a.w = L.fqkv; a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
+            NC_TRY(launch_f32(st, a, EPI_BIAS, false));
+        }
+        // RoPE, cache append, attention
+        AttnArgs at{};
+        at.ctx = m->ctx; at.qkv = m->qkv; at.cache = m->kv + (int64_t)l * m->layer_stride;
+        at.cos_tab = m->cos_tab; at.sin_tab = m->sin_tab; at.slot = m->slot; at.pos = m->pos;
+        at.slot_stride = m->slot_stride; at.heads = (int)c.heads; at.kv = (int)c.kv_heads; at.d = d;
+        at.cap = c.capacity; at.scale = c.attn_scale;
+        if (fused) {
+            at.mode = 0;
+            NC_TRY(launch_attention(st, at, rows));
+        } else {
+            at.mode = 1;
+            NC_TRY(launch_attention(st, at, rows));
+            at.mode = 2;
+            NC_TRY(launch_attention(st, at, rows));
+        }
+        // o_proj with the residual add
+        if (q8) {
+            NC_TRY(launch_quant(st, m->xq, m->ctx, m->xs, m->off, nullptr, rows, Hq));
+            GemvI8Args a{};
+            a.out = m->x; a.xq = m->xq; a.xs = m->xs; a.offset = m->off; a.w = L.wo; a.scales = L.so;
+            a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
+            NC_TRY(launch_i8(st, a, EPI_RESIDUAL));
+        } else {
+            GemvF32Args a{};
+            a.out = m->x; a.x = m->ctx; a.w = L.fo; a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
+            NC_TRY(launch_f32(st, a, EPI_RESIDUAL, false));
+        }
+        // post-attention norm -> gate/up with SiLU * up -> down with the residual add
+        NC_TRY(launch_norm(st, q8 ? nullptr : m->normed, m->x, L.post_norm, q8 ? m->xq : nullptr, m->xs, m->off,
+                           nullptr, nullptr, rows, H, c.eps));
+        if (q8) {
+            GemvI8Args a{};
+            a.out = m->hbuf; a.xq = m->xq; a.xs = m->xs; a.offset = m->off; a.w = L.wg; a.scales = L.sg;
+            a.w2 = L.wu; a.scales2 = L.su; a.m = rows; a.n = I; a.k = H;
+            NC_TRY(launch_i8(st, a, EPI_SWIGLU));
+            NC_TRY(launch_quant(st, m->xq, m->hbuf, m->xs, m->off, nullptr, rows, I));
+            GemvI8Args b{};
+            b.out = m->x; b.xq = m->xq; b.xs = m->xs; b.offset = m->off; b.w = L.wd; b.scales = L.sd;
+            b.residual = m->x; b.m = rows; b.n = H; b.k = I;
+            NC_TRY(launch_i8(st, b, EPI_RESIDUAL));
+        } else {
+            GemvF32Args a{};
+            a.out = m->hbuf; a.x = m->normed; a.w = L.fg; a.w2 = L.fu; a.m = rows; a.n = I; a.k = H;
+            NC_TRY(launch_f32(st, a, EPI_SWIGLU, false));
+            GemvF32Args b{};
+            b.out = m->x; b.x = m->hbuf; b.w = L.fd; b.residual = m->x; b.m = rows; b.n = H; b.k = I;
+            NC_TRY(launch_f32(st, b, EPI_RESIDUAL, false));
+        }
+    }
+    // final norm of the rows that need logits, then the tied LM head with the argmax
+    NC_TRY(launch_norm(st, m->normed, m->x, m->final_norm, nullptr, nullptr, nullptr, nullptr, m->logit_row,
+                       logit_rows, H, c.eps));
+    GemvF32Args a{};
+    a.out = m->logits; a.x = m->normed; a.w = m->embed; a.m = logit_rows; a.n = (int)c.vocab; a.k = H;
+    a.part_val = m->part_val; a.part_idx = m->part_idx; a.counter = m->counter; a.tokens = m->tokens;
+    NC_TRY(launch_f32(st, a, EPI_NONE, true));
+    return NC_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_freq, nc_model **out) {
+    if (!cfg || !out || !inv_freq) return fail(NC_ERR_ARGUMENT, "null argument");
+    const nc_qwen2_config c = *cfg;
+    if (c.hidden <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads || c.head_dim % 4 ||
+        c.heads / c.kv_heads > 8 || c.max_rows <= 0 || c.max_rows > 1024 || c.slots <= 0 || c.capacity <= 0)
+        return fail(NC_ERR_ARGUMENT, "unsupported model shape");
+    if (c.hidden % 32 || c.inter % 32 || (c.heads * c.head_dim) % 32)
+        return fail(NC_ERR_ARGUMENT, "widths must be whole 32-blocks");
+    if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024)
+        return fail(NC_ERR_ARGUMENT, "capacity %d exceeds the attention kernel's shared memory", c.capacity);
+
+    auto m = std::make_unique<nc_model>();
+    m->c = c;
+    m->dev = c.device;
+    CUDA_TRY(cudaSetDevice(c.device));
+    CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+
+    const int64_t H = c.hidden, I = c.inter, d = c.head_dim, V = c.vocab, R = c.max_rows;
+    const int64_t Hq = c.heads * d, Nqkv = (c.heads + 2 * c.kv_heads) * d, half = d / 2;
+    const int64_t kmax = std::max(H, std::max(I, Hq));
+    Layout lay;
+    lay.add(&m->embed, V * H * 4);
+    lay.add(&m->final_norm, H * 4);
+    lay.add(&m->cos_tab, (int64_t)c.capacity * half * 4);
+    lay.add(&m->sin_tab, (int64_t)c.capacity * half * 4);
+    m->layers.resize(c.layers);
+    for (auto &L : m->layers) {
+        std::memset(&L, 0, sizeof L);
+        lay.add(&L.in_norm, H * 4);
+        lay.add(&L.post_norm, H * 4);
+        lay.add(&L.bqkv, Nqkv * 4);
+        if (c.quant) {
+            lay.add(&L.wqkv, Nqkv * H);
+            lay.add(&L.sqkv, Nqkv * 4);
+            lay.add(&L.wo, H * Hq);
+            lay.add(&L.so, H * 4);
+            lay.add(&L.wg, I * H);
+            lay.add(&L.sg, I * 4);
+            lay.add(&L.wu, I * H);
+            lay.add(&L.su, I * 4);
+            lay.add(&L.wd, H * I);
+            lay.add(&L.sd, H * 4);
+        } else {
+            lay.add(&L.fqkv, Nqkv * H * 4);
+            lay.add(&L.fo, H * Hq * 4);
+            lay.add(&L.fg, I * H * 4);
+            lay.add(&L.fu, I * H * 4);
+            lay.add(&L.fd, H * I * 4);
+        }
+    }
+    m->layer_stride = 2 * c.kv_heads * (int64_t)c.capacity * d;
+    m->slot_stride = c.layers * m->layer_stride;
+    lay.add(&m->kv, (int64_t)c.slots * m->slot_stride * 4);
+    lay.add(&m->x, R * H * 4);
+    lay.add(&m->normed, R * H * 4);
+    lay.add(&m->xq, R * kmax);
+    lay.add(&m->xs, R * (kmax / 32) * 4);
+    lay.add(&m->off, R * 4);
+    lay.add(&m->qkv, R * Nqkv * 4);
+    lay.add(&m->ctx, R * Hq * 4);
+    lay.add(&m->hbuf, R * I * 4);
+    lay.add(&m->logits, R * V * 4);
+    const int64_t ctas = (V + F32_ROWS - 1) / F32_ROWS;
+    lay.add(&m->part_val, R * ctas * 4);
+    lay.add(&m->part_idx, R * ctas * 4);
+    lay.add(&m->ids, R * 8);
+    lay.add(&m->tokens, R * 8);
+    lay.add(&m->slot, R * 4);
+    lay.add(&m->pos, R * 4);
+    lay.add(&m->logit_row, R * 4);
+    lay.add(&m->step, 4);
+    lay.add(&m->err, 8);
+    lay.add(&m->counter, 4);
+    m->history_steps = 8192;
+    lay.add(&m->history, (int64_t)m->history_steps * R * 8);
+
+    m->arena_bytes = lay.top;
+    void *base = nullptr;
+    CUDA_TRY(cudaMalloc(&base, (size_t)lay.top));
+    m->arena = (char *)base;
+    for (auto &pc : lay.pieces) *pc.first = m->arena + pc.second;
+    CUDA_TRY(cudaMemsetAsync(m->arena, 0, (size_t)lay.top, m->stream));
+
+    // RoPE tables: angle = float(position) * inv_freq[i] (nanocompile/nn.py:78-94), evaluated with
+    // the C library's cosf/sinf -- the functions the reference's generated C calls for them.
+    std::vector<float> ct((size_t)c.capacity * half), stt((size_t)c.capacity * half);
+    for (int64_t p = 0; p < c.capacity; ++p)
+        for (int64_t i = 0; i < half; ++i) {
+            volatile float angle = (float)p * inv_freq[i];
+            ct[p * half + i] = cosf(angle);
+            stt[p * half + i] = sinf(angle);
+        }
+    CUDA_TRY(cudaMemcpyAsync(m->cos_tab, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice, m->stream));
+    CUDA_TRY(cudaMemcpyAsync(m->sin_tab, stt.data(), stt.size() * 4, cudaMemcpyHostToDevice, m->stream));
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+
+    // the upload registry: checkpoint name -> destination
+    auto reg = [&](const std::string &name, void *dst, int64_t bytes, bool int8) {
+        m->weights[name] = WeightSlot{(char *)dst, bytes, int8};
+    };
+    reg("model.embed_tokens.weight", m->embed, V * H * 4, false);
+    reg("model.norm.weight", m->final_norm, H * 4, false);
+    for (int64_t l = 0; l < c.layers; ++l) {
+        auto &L = m->layers[l];
+        const std::string p = "model.layers." + std::to_string(l);
+        reg(p + ".input_layernorm.weight", L.in_norm, H * 4, false);
+        reg(p + ".post_attention_layernorm.weight", L.post_norm, H * 4, false);
+        const int64_t rows[3] = {Hq, c.kv_heads * d, c.kv_heads * d};
+        const char *names[3] = {"q_proj", "k_proj", "v_proj"};
+        int64_t r0 = 0;
+        for (int i = 0; i < 3; ++i) {
+            const std::string base_name = p + ".self_attn." + names[i];
+            reg(base_name + ".bias", L.bqkv + r0, rows[i] * 4, false);
+            if (c.quant) {
+                reg(base_name + ".weight@int8", L.wqkv + r0 * H, rows[i] * H, true);
+                reg(base_name + ".weight@scales", L.sqkv + r0, rows[i] * 4, false);
+            } else {
+                reg(base_name + ".weight", L.fqkv + r0 * H, rows[i] * H * 4, false);
+            }
+            r0 += rows[i];
+        }
+        struct P { const char *name; uint8_t *w8; float *s; float *f; int64_t n, k; };
+        const P projs[4] = {{"self_attn.o_proj", L.wo, L.so, L.fo, H, Hq},
+                            {"mlp.gate_proj", L.wg, L.sg, L.fg, I, H},
+                            {"mlp.up_proj", L.wu, L.su, L.fu, I, H},
+                            {"mlp.down_proj", L.wd, L.sd, L.fd, H, I}};
+        for (const P &pr : projs) {
+            const std::string base_name = p + "." + pr.name + ".weight";
+            if (c.quant) {
+                reg(base_name + "@int8", pr.w8, pr.n * pr.k, true);
+                reg(base_name + "@scales", pr.s, pr.n * 4, false);
+            } else {
+                reg(base_name, pr.f, pr.n * pr.k * 4, false);
+            }
+        }
+    }
+    *out = m.release();
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_destroy(nc_model *m) {
+    if (!m) return NC_OK;
+    cudaSetDevice(m->dev);
+    for (auto &g : m->decode_graphs) cudaGraphExecDestroy(g.second);
+    if (m->arena) cudaFree(m->arena);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return NC_OK;
+}
+
+extern "C" int64_t nc_qwen2_arena_bytes(const nc_model *m) { return m ? m->arena_bytes : 0; }
+
+extern "C" int32_t nc_qwen2_upload(nc_model *m, const char *name, const void *host, int64_t bytes) {
+    if (!m || !name || !host) return fail(NC_ERR_ARGUMENT, "null argument");
+    auto it = m->weights.find(name);
+    if (it == m->weights.end()) return fail(NC_ERR_ARGUMENT, "no weight named %s", name);
+    if (it->second.bytes != bytes)
+        return fail(NC_ERR_ARGUMENT, "weight %s has %lld bytes, expected %lld", name, (long long)bytes,
+                    (long long)it->second.bytes);
+    CUDA_TRY(cudaSetDevice(m->dev));
+    CUDA_TRY(cudaMemcpyAsync(it->second.dst, host, (size_t)bytes, cudaMemcpyHostToDevice, m->stream));
+    if (it->second.int8) {
+        xor80_kernel<<<592, 256, 0, m->stream>>>((uint8_t *)it->second.dst, bytes);
+        NC_TRY(check_launch("xor80_kernel"));
+    }
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->uploaded.insert(name);
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_missing_weights(const nc_model *m, int32_t *count) {
+    int32_t n = 0;
+    std::string first;
+    for (auto &w : m->weights)
+        if (!m->uploaded.count(w.first)) {
+            if (!n) first = w.first;
+            ++n;
+        }
+    *count = n;
+    if (n) g_error = "missing weights, first " + first;
+    return NC_OK;
+}
+
+static int32_t check_ready(nc_model *m) {
+    if (m->uploaded.size() != m->weights.size()) {
+        int32_t n;
+        nc_qwen2_missing_weights(m, &n);
+        return fail(NC_ERR_STATE, "%s (%d missing)", g_error.c_str(), n);
+    }
+    return NC_OK;
+}
+
+static int32_t kv_copy(nc_model *m, int32_t slot, int64_t start, int64_t count, float *keys, float *values,
+                       bool to_device) {
+    const nc_qwen2_config &c = m->c;
+    if (slot < 0 || slot >= c.slots || start < 0 || count < 0 || start + count > c.capacity)
+        return fail(NC_ERR_ARGUMENT, "KV range slot %d [%lld, %lld) outside the cache", slot, (long long)start,
+                    (long long)(start + count));
+    if (count == 0) return NC_OK;
+    CUDA_TRY(cudaSetDevice(m->dev));
+    const int64_t d = c.head_dim;
+    for (int64_t l = 0; l < c.layers; ++l)
+        for (int64_t kvi = 0; kvi < 2; ++kvi)
+            for (int64_t g = 0; g < c.kv_heads; ++g) {
+                float *dev = m->kv + slot * m->slot_stride + l * m->layer_stride + (kvi * c.kv_heads + g) * c.capacity * d +
+                             start * d;
+                float *host = (kvi ? values : keys) + ((l * c.kv_heads + g) * count) * d;
+                if (to_device)
+                    CUDA_TRY(cudaMemcpyAsync(dev, host, count * d * 4, cudaMemcpyHostToDevice, m->stream));
+                else
+                    CUDA_TRY(cudaMemcpyAsync(host, dev, count * d * 4, cudaMemcpyDeviceToHost, m->stream));
+            }
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_kv_write(nc_model *m, int32_t slot, int64_t start, int64_t count, const float *keys,
+                                     const float *values) {
+    return kv_copy(m, slot, start, count, (float *)keys, (float *)values, true);
+}
+
+extern "C" int32_t nc_qwen2_kv_read(nc_model *m, int32_t slot, int64_t start, int64_t count, float *keys,
+                                    float *values) {
+    return kv_copy(m, slot, start, count, keys, values, false);
+}
+
+static int32_t check_rows(nc_model *m, int32_t rows, const int32_t *slot, const int32_t *pos, bool *fused) {
+    const nc_qwen2_config &c = m->c;
+    if (rows <= 0 || rows > c.max_rows) return fail(NC_ERR_ARGUMENT, "%d rows, the model takes 1..%d", rows, c.max_rows);
+    std::set<int32_t> seen;
+    *fused = true;
+    for (int r = 0; r < rows; ++r) {
+        if (slot[r] < 0 || slot[r] >= c.slots) return fail(NC_ERR_ARGUMENT, "row %d: slot %d out of range", r, slot[r]);
+        if (pos[r] < 0 || pos[r] >= c.capacity)
+            return fail(NC_ERR_ARGUMENT, "row %d: position %d outside the cache capacity %d", r, pos[r], c.capacity);
+        if (!seen.insert(slot[r]).second) {
+            *fused = false;
+            if (r == 0 || slot[r - 1] != slot[r] || pos[r - 1] + 1 != pos[r])
+                return fail(NC_ERR_ARGUMENT, "rows of slot %d must be consecutive positions", slot[r]);
+        }
+    }
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, const int32_t *slot,
+                                 const int32_t *pos, int32_t logit_rows, const int32_t *logit_row, float *logits,
+                                 int64_t *tokens, int32_t *bad_row) {
+    if (!m || !ids || !slot || !pos) return fail(NC_ERR_ARGUMENT, "null argument");
+    NC_TRY(check_ready(m));
+    bool fused;
+    NC_TRY(check_rows(m, rows, slot, pos, &fused));
+    if (logit_rows < 0 || logit_rows > rows) return fail(NC_ERR_ARGUMENT, "bad logit row count");
+    for (int i = 0; i < logit_rows; ++i)
+        if (logit_row[i] < 0 || logit_row[i] >= rows) return fail(NC_ERR_ARGUMENT, "bad logit row");
+    CUDA_TRY(cudaSetDevice(m->dev));
+    cudaStream_t st = m->stream;
+    CUDA_TRY(cudaMemcpyAsync(m->ids, ids, rows * 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->slot, slot, rows * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->pos, pos, rows * 4, cudaMemcpyHostToDevice, st));
+    if (logit_rows) CUDA_TRY(cudaMemcpyAsync(m->logit_row, logit_row, logit_rows * 4, cudaMemcpyHostToDevice, st));
+    NC_TRY(enqueue_step(m, rows, logit_rows, fused));
+    unsigned long long err = 0;
+    CUDA_TRY(cudaMemcpyAsync(&err, m->err, 8, cudaMemcpyDeviceToHost, st));
+    if (logits && logit_rows)
+        CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)logit_rows * m->c.vocab * 4, cudaMemcpyDeviceToHost, st));
+    if (tokens && logit_rows) CUDA_TRY(cudaMemcpyAsync(tokens, m->tokens, logit_rows * 8, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    if (err != ~0ull) {
+        if (bad_row) *bad_row = (int32_t)err;
+        return fail(NC_ERR_KERNEL, "gather index %lld is outside 0..%lld", (long long)ids[err],
+                    (long long)(m->c.vocab - 1));
+    }
+    return NC_OK;
+}
+
+static int32_t decode_graph(nc_model *m, int batch, cudaGraphExec_t *out) {
+    auto it = m->decode_graphs.find(batch);
+    if (it != m->decode_graphs.end()) {
+        *out = it->second;
+        return NC_OK;
+    }
+    cudaGraph_t graph;
+    CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int32_t s = enqueue_step(m, batch, batch, true);
+    if (s == NC_OK) {
+        advance_kernel<<<1, 1024, 0, m->stream>>>(m->ids, m->pos, m->tokens, m->history, m->step, batch);
+        s = check_launch("advance_kernel");
+    }
+    cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    if (s != NC_OK) return s;
+    if (e != cudaSuccess) return fail(NC_ERR_CUDA, "capture: %s", cudaGetErrorString(e));
+    cudaGraphExec_t exec;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return fail(NC_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
+    m->decode_graphs[batch] = exec;
+    *out = exec;
+    return NC_OK;
+}
+
+static int32_t decode_setup(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
+                            const int32_t *start, int32_t steps, cudaGraphExec_t *graph) {
+    if (!m || !slot || !first || !start) return fail(NC_ERR_ARGUMENT, "null argument");
+    NC_TRY(check_ready(m));
+    if (batch <= 0 || batch > m->c.max_rows || batch > 1024)
+        return fail(NC_ERR_ARGUMENT, "batch %d outside 1..%d", batch, m->c.max_rows);
+    if (steps < 0 || steps > m->history_steps)
+        return fail(NC_ERR_ARGUMENT, "%d steps, at most %d per call", steps, m->history_steps);
+    bool fused;
+    NC_TRY(check_rows(m, batch, slot, start, &fused));
+    if (!fused) return fail(NC_ERR_ARGUMENT, "decode rows must be distinct slots");
+    for (int b = 0; b < batch; ++b) {
+        if (first[b] < 0 || first[b] >= m->c.vocab)
+            return fail(NC_ERR_KERNEL, "gather index %lld is outside 0..%lld", (long long)first[b],
+                        (long long)(m->c.vocab - 1));
+        if ((int64_t)start[b] + steps > m->c.capacity)
+            return fail(NC_ERR_ARGUMENT, "row %d: %d steps from position %d pass the capacity %d", b, steps, start[b],
+                        m->c.capacity);
+    }
+    CUDA_TRY(cudaSetDevice(m->dev));
+    cudaStream_t st = m->stream;
+    std::vector<int32_t> rows(batch);
+    for (int b = 0; b < batch; ++b) rows[b] = b;
+    CUDA_TRY(cudaMemcpyAsync(m->ids, first, batch * 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->slot, slot, batch * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->pos, start, batch * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->logit_row, rows.data(), batch * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemsetAsync(m->step, 0, 4, st));
+    NC_TRY(decode_graph(m, batch, graph));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_decode(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
+                                   const int32_t *start, int32_t steps, int32_t per_step, int64_t *tokens,
+                                   float *logits) {
+    cudaGraphExec_t graph;
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
+    cudaStream_t st = m->stream;
+    for (int s = 0; s < steps; ++s) {
+        CUDA_TRY(cudaGraphLaunch(graph, st));
+        if (per_step && tokens) {
+            CUDA_TRY(cudaMemcpyAsync(tokens + (int64_t)s * batch, m->tokens, batch * 8, cudaMemcpyDeviceToHost, st));
+            CUDA_TRY(cudaStreamSynchronize(st));
+        }
+    }
+    if (!per_step && tokens && steps)
+        CUDA_TRY(cudaMemcpyAsync(tokens, m->history, (size_t)steps * batch * 8, cudaMemcpyDeviceToHost, st));
+    if (logits && steps)
+        CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
+                                         const int32_t *start, int32_t steps, float *ms) {
+    cudaGraphExec_t graph;
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
+    cudaStream_t st = m->stream;
+    cudaEvent_t a, b;
+    CUDA_TRY(cudaEventCreate(&a));
+    CUDA_TRY(cudaEventCreate(&b));
+    CUDA_TRY(cudaEventRecord(a, st));
+    for (int s = 0; s < steps; ++s) CUDA_TRY(cudaGraphLaunch(graph, st));
+    CUDA_TRY(cudaEventRecord(b, st));
+    CUDA_TRY(cudaEventSynchronize(b));
+    CUDA_TRY(cudaEventElapsedTime(ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return NC_OK;
+}

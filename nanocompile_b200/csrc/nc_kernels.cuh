@@ -1,0 +1,688 @@
+// nc_kernels.cuh -- the fused-group kernels of a Qwen2 step on sm_100a.
+//
+// Each kernel computes one kind of fused group of nanocompile's int8-vnni (or float32) Qwen2
+// step, bit for bit: the same float32 operations in the same order as the C that
+// nanocompile/fusion.py + codegen_c.py generate.  Parallelism only ever runs across
+// independent results (rows, tokens, heads, accumulator lanes); every sum the reference
+// forms sequentially is formed sequentially here, by one thread.
+#pragma once
+
+#include "nc_common.cuh"
+
+namespace nc {
+
+// ---- gather (nanocompile/fusion.py:713-731) --------------------------------------------
+// One CTA per row.  An id outside 0..vocab-1 records its row in *err (atomicMin; all-ones =
+// none) and leaves the row zero, where the reference returns status 1 before writing.
+__global__ void gather_kernel(float *__restrict__ out, const int64_t *__restrict__ ids,
+                              const float *__restrict__ table, unsigned long long *err,
+                              int64_t vocab, int hidden) {
+    const int r = blockIdx.x;
+    const int64_t id = ids[r];
+    float *dst = out + (int64_t)r * hidden;
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) atomicMin(err, (unsigned long long)r);
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = 0.0f;
+        return;
+    }
+    const float *src = table + id * (int64_t)hidden;
+    if ((hidden & 3) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) d4[i] = s4[i];
+    } else {
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = src[i];
+    }
+}
+
+// ---- rms_norm row kernel + block quantization --------------------------------------------
+// nanocompile/nn.py:34-38 as one row kernel (fusion.py:631-650): acc = acc + x*x over the row
+// in order, then x * (1 / sqrtf(acc / n + eps)) * w; fused with nanocompile/quantize.py:102-124
+// (block absmax, scale, xq, int32 block sums, offset = 128 * in-order sum of sum_b * scale_b).
+// One CTA per output row; row_map (nullable) picks the input row.
+constexpr int NORM_THREADS = 256;
+
+__global__ void __launch_bounds__(NORM_THREADS)
+norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const float *__restrict__ w,
+                  int8_t *__restrict__ xq, float *__restrict__ xs, float *__restrict__ offset,
+                  int32_t *__restrict__ bsums, const int32_t *__restrict__ row_map, int n, float eps) {
+    extern __shared__ float smem[];
+    float *row = smem;            // [n]
+    float *sq = smem + n;         // [n]: squares, then the normalized row
+    __shared__ float s_inv;
+    __shared__ float s_scale[256];
+    __shared__ int s_bsum[256];
+    const int b = blockIdx.x;
+    const int64_t in_row = row_map ? row_map[b] : b;
+    const float *xr = x + in_row * n;
+    for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
+        const float v = xr[i];
+        row[i] = v;
+        sq[i] = fmul(v, v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float acc = 0.0f;
+        int i = 0;
+        if ((n & 3) == 0) {
+            const float4 *s4 = reinterpret_cast<const float4 *>(sq);
+            for (; i < n / 4; ++i) {
+                const float4 v = s4[i];
+                acc = fadd(acc, v.x);
+                acc = fadd(acc, v.y);
+                acc = fadd(acc, v.z);
+                acc = fadd(acc, v.w);
+            }
+            i *= 4;
+        }
+        for (; i < n; ++i) acc = fadd(acc, sq[i]);
+        s_inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(acc, (float)n), eps)));
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
+        const float v = fmul(fmul(row[i], inv), w[i]);
+        if (normed) normed[(int64_t)b * n + i] = v;
+        sq[i] = v;
+    }
+    if (!xq) return;
+    __syncthreads();
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = n / QBLOCK;
+    for (int blk = warp; blk < blocks; blk += NORM_THREADS / 32) {
+        int8_t qv;
+        int bs;
+        const float scale = quantize_block_warp(sq[blk * QBLOCK + lane], &qv, &bs);
+        xq[(int64_t)b * n + blk * QBLOCK + lane] = qv;
+        if (lane == 0) {
+            xs[(int64_t)b * blocks + blk] = scale;
+            if (bsums) bsums[(int64_t)b * blocks + blk] = bs;
+            s_scale[blk] = scale;
+            s_bsum[blk] = bs;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float acc = 0.0f;
+        for (int blk = 0; blk < blocks; ++blk) acc = fadd(acc, fmul((float)s_bsum[blk], s_scale[blk]));
+        offset[b] = fmul(acc, 128.0f);
+    }
+}
+
+// Block quantization alone, one CTA (8 warps) per row; up to 256 blocks (k <= 8192).
+__global__ void __launch_bounds__(NORM_THREADS)
+quantize_kernel(int8_t *__restrict__ xq, const float *__restrict__ x, float *__restrict__ xs,
+                float *__restrict__ offset, int32_t *__restrict__ bsums, int k) {
+    __shared__ float s_scale[256];
+    __shared__ int s_bsum[256];
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = k / QBLOCK;
+    for (int blk = warp; blk < blocks; blk += NORM_THREADS / 32) {
+        int8_t qv;
+        int bs;
+        const float scale = quantize_block_warp(x[(int64_t)b * k + blk * QBLOCK + lane], &qv, &bs);
+        xq[(int64_t)b * k + blk * QBLOCK + lane] = qv;
+        if (lane == 0) {
+            xs[(int64_t)b * blocks + blk] = scale;
+            if (bsums) bsums[(int64_t)b * blocks + blk] = bs;
+            s_scale[blk] = scale;
+            s_bsum[blk] = bs;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float acc = 0.0f;
+        for (int blk = 0; blk < blocks; ++blk) acc = fadd(acc, fmul((float)s_bsum[blk], s_scale[blk]));
+        offset[b] = fmul(acc, 128.0f);
+    }
+}
+
+// ---- int8-vnni GEMV / skinny GEMM -----------------------------------------------------------
+// nanocompile/lower.py:363-397: per output (token m, row n) 32 float32 accumulators; the
+// 128-byte chunk k0 of the row feeds accumulator a = byte/4 with
+//   acc[a] = fmaf(float(Dp4(w[4a..4a+3] + 128, x[..])), xs[block], acc[a])
+// chunks in order; 32-byte groups past the last whole chunk feed accumulators 0..7; then
+// _combine and (sum - offset) * scale, then the epilogue (fusion.py:699-711).
+//
+// LPR lanes cooperate on one row; lane j owns accumulators j*APL .. j*APL+APL-1 and reads
+// the matching BPL bytes of every chunk, so each accumulator's chain stays in one lane, in
+// order.  The combine is a butterfly that pairs exactly the accumulators _combine pairs.
+struct GemvI8Args {
+    float *out;               // [m, n]
+    const int8_t *xq;         // [m, k]
+    const float *xs;          // [m, k/32]
+    const float *offset;      // [m]
+    const uint8_t *w;         // [n, k], int8 + 128
+    const float *scales;      // [n]
+    const float *bias;        // EPI_BIAS: [n]
+    const float *residual;    // EPI_RESIDUAL: [m, n] (may alias out)
+    const uint8_t *w2;        // EPI_SWIGLU: second weight
+    const float *scales2;
+    int m, n, k;
+};
+
+template <int BPL>
+struct Seg;
+template <>
+struct Seg<16> {
+    using T = uint4;
+    __device__ static void split(const T &v, uint32_t *o) { o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w; }
+};
+template <>
+struct Seg<8> {
+    using T = uint2;
+    __device__ static void split(const T &v, uint32_t *o) { o[0] = v.x; o[1] = v.y; }
+};
+template <>
+struct Seg<4> {
+    using T = uint32_t;
+    __device__ static void split(const T &v, uint32_t *o) { o[0] = v; }
+};
+
+// Butterfly over the accumulator index bits in _combine's pairing order: a^8, a^16, a^4,
+// a^1, a^2.  Bits below log2(APL) are inside a lane, the rest across lanes (xor shuffle).
+template <int APL>
+__device__ __forceinline__ float combine_lanes(float *v) {
+    constexpr int LG = APL == 4 ? 2 : (APL == 2 ? 1 : 0);
+    const int order[5] = {3, 4, 2, 0, 1};
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const int bit = order[s];
+        if (bit < LG) {
+#pragma unroll
+            for (int i = 0; i < APL; ++i)
+                if (!(i & (1 << bit))) v[i] = fadd(v[i], v[i | (1 << bit)]);
+        } else {
+            const int lane_bit = 1 << (bit - LG);
+#pragma unroll
+            for (int i = 0; i < APL; ++i) v[i] = fadd(v[i], __shfl_xor_sync(0xffffffffu, v[i], lane_bit));
+        }
+    }
+    return v[0];
+}
+
+template <int LPR, int TOK, int UNROLL, int EPI>
+__global__ void __launch_bounds__(128)
+gemv_i8_kernel(GemvI8Args a) {
+    constexpr int RPW = 32 / LPR;     // rows per warp
+    constexpr int BPL = 128 / LPR;    // bytes of a chunk per lane
+    constexpr int APL = BPL / 4;      // accumulators per lane
+    constexpr bool TWO = EPI == EPI_SWIGLU;
+    using SegT = typename Seg<BPL>::T;
+    __shared__ uint64_t tab[32];
+    if (EPI == EPI_SWIGLU) {
+        if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
+        __syncthreads();
+    }
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int grp = lane / LPR, j = lane % LPR;
+    const int row = (blockIdx.x * (blockDim.x / 32) + warp) * RPW + grp;
+    const bool row_ok = row < a.n;
+    const int rowc = row_ok ? row : a.n - 1;
+    const int K = a.k, blocks = K / QBLOCK;
+    const int chunks = K / CHUNK, stride = chunks * CHUNK, groups = (K % CHUNK) / 32;
+    const uint8_t *wrow = a.w + (int64_t)rowc * K;
+    const uint8_t *wrow2 = TWO ? a.w2 + (int64_t)rowc * K : nullptr;
+
+    for (int m0 = 0; m0 < a.m; m0 += TOK) {
+        float acc[TOK][APL], acc2[TWO ? TOK : 1][APL];
+#pragma unroll
+        for (int t = 0; t < TOK; ++t)
+#pragma unroll
+            for (int i = 0; i < APL; ++i) {
+                acc[t][i] = 0.0f;
+                if (TWO) acc2[t][i] = 0.0f;
+            }
+        // whole 128-byte chunks, UNROLL at a time so the weight loads are in flight together
+        for (int c0 = 0; c0 < chunks; c0 += UNROLL) {
+            uint32_t wv[UNROLL][APL], wv2[TWO ? UNROLL : 1][APL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                if (c0 + u < chunks) {
+                    const int off = (c0 + u) * CHUNK + j * BPL;
+                    Seg<BPL>::split(__ldcs(reinterpret_cast<const SegT *>(wrow + off)), wv[u]);
+                    if (TWO) Seg<BPL>::split(__ldcs(reinterpret_cast<const SegT *>(wrow2 + off)), wv2[u]);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < TOK; ++t) {
+                const int m = m0 + t;
+                if (m >= a.m) break;
+                const int8_t *xrow = a.xq + (int64_t)m * K;
+                const float *xsr = a.xs + (int64_t)m * blocks;
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u) {
+                    if (c0 + u < chunks) {
+                        const int off = (c0 + u) * CHUNK + j * BPL;
+                        uint32_t xv[APL];
+                        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow + off), xv);
+                        const float s = xsr[off / QBLOCK];
+#pragma unroll
+                        for (int i = 0; i < APL; ++i) {
+                            acc[t][i] = __fmaf_rn(dp4_lane(wv[u][i], xv[i]), s, acc[t][i]);
+                            if (TWO) acc2[t][i] = __fmaf_rn(dp4_lane(wv2[u][i], xv[i]), s, acc2[t][i]);
+                        }
+                    }
+                }
+            }
+        }
+        // leftover 32-byte groups: into accumulators 0..7, group after group
+        if (groups && j * BPL < 32) {
+            for (int k1 = 0; k1 < groups; ++k1) {
+                const int off = stride + k1 * 32 + j * BPL;
+                uint32_t wv[APL], wv2[APL];
+                Seg<BPL>::split(*reinterpret_cast<const SegT *>(wrow + off), wv);
+                if (TWO) Seg<BPL>::split(*reinterpret_cast<const SegT *>(wrow2 + off), wv2);
+#pragma unroll
+                for (int t = 0; t < TOK; ++t) {
+                    const int m = m0 + t;
+                    if (m >= a.m) break;
+                    uint32_t xv[APL];
+                    Seg<BPL>::split(*reinterpret_cast<const SegT *>(a.xq + (int64_t)m * K + off), xv);
+                    const float s = a.xs[(int64_t)m * blocks + off / QBLOCK];
+#pragma unroll
+                    for (int i = 0; i < APL; ++i) {
+                        acc[t][i] = __fmaf_rn(dp4_lane(wv[i], xv[i]), s, acc[t][i]);
+                        if (TWO) acc2[t][i] = __fmaf_rn(dp4_lane(wv2[i], xv[i]), s, acc2[t][i]);
+                    }
+                }
+            }
+        }
+        // combine, scale, epilogue
+#pragma unroll
+        for (int t = 0; t < TOK; ++t) {
+            const int m = m0 + t;
+            if (m >= a.m) break;
+            const float sum = combine_lanes<APL>(acc[t]);
+            float sum2 = 0.0f;
+            if (TWO) sum2 = combine_lanes<APL>(acc2[t]);
+            if (j == 0 && row_ok) {
+                const float off = a.offset[m];
+                const float y = fmul(fsub(sum, off), a.scales[row]);
+                float out;
+                if (EPI == EPI_BIAS) {
+                    out = fadd(y, a.bias[row]);
+                } else if (EPI == EPI_RESIDUAL) {
+                    out = fadd(a.residual[(int64_t)m * a.n + row], y);
+                } else if (EPI == EPI_SWIGLU) {
+                    const float y1 = fmul(fsub(sum2, off), a.scales2[row]);
+                    out = swiglu(y, y1, tab);
+                } else {
+                    out = y;
+                }
+                a.out[(int64_t)m * a.n + row] = out;
+            }
+        }
+    }
+}
+
+// ---- float32 GEMV with in-order sums (projections of float32 models, and the LM head) -------
+// nanocompile/lower.py:255-274: acc = acc + x[k] * w[n, k], k = 0, 1, 2, ... -- one thread owns
+// one row n and walks k in order.  Rows are staged through shared memory in 32-column tiles
+// by cp.async (16-byte pieces, XOR-swizzled so a thread reading its own row is conflict-free),
+// STAGES tiles in flight.  With ARGMAX the kernel also reduces each token's logits to the
+// index of the first maximum (np.argmax, nanocompile/models/qwen2.py:364).
+constexpr int F32_ROWS = 128;
+constexpr int F32_TILE = 32;
+constexpr int F32_STAGES = 4;
+
+struct GemvF32Args {
+    float *out;               // [m, n] (nullable with ARGMAX)
+    const float *x;           // [m, k] (row_map picks rows)
+    const float *w;           // [n, k]
+    const float *bias, *residual, *w2;
+    const int32_t *row_map;   // nullable
+    float *part_val;          // ARGMAX scratch [m, gridDim.x]
+    int32_t *part_idx;
+    unsigned int *counter;    // ARGMAX: CTAs finished (reset by the last one)
+    int64_t *tokens;          // ARGMAX: [m]
+    int m, n, k;
+};
+
+__device__ __forceinline__ bool argmax_better(float va, int ia, float vb, int ib) {
+    const bool na = va != va, nb = vb != vb;
+    if (na || nb) return na && (!nb || ia < ib);
+    if (va != vb) return va > vb;
+    return ia < ib;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+template <int TOK, int EPI, bool ARGMAX>
+__global__ void __launch_bounds__(F32_ROWS)
+gemv_f32_kernel(GemvF32Args a) {
+    constexpr bool TWO = EPI == EPI_SWIGLU;
+    constexpr int NW = TWO ? 2 : 1;
+    extern __shared__ float4 smem4[];
+    // per stage: NW weight tiles [128 rows][8 pieces of 4 floats], then the x tile [TOK][32]
+    constexpr int W_PIECES = F32_ROWS * (F32_TILE / 4);
+    constexpr int STAGE_F4 = NW * W_PIECES + TOK * (F32_TILE / 4);
+    __shared__ uint64_t tab[32];
+    if (TWO) {
+        if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
+    }
+    const int t = threadIdx.x;
+    const int row0 = blockIdx.x * F32_ROWS;
+    const int row = row0 + t;
+    const int K = a.k, tiles = K / F32_TILE;
+
+    auto load_tile = [&](int stage, int kt, int m0) {
+        float4 *st = smem4 + stage * STAGE_F4;
+#pragma unroll
+        for (int p = 0; p < NW * W_PIECES / F32_ROWS; ++p) {
+            const int id = t + p * F32_ROWS;             // piece id within the NW tiles
+            const int which = id / W_PIECES, rem = id % W_PIECES;
+            const int r = rem / 8, s = rem % 8;
+            const int gr = min(row0 + r, a.n - 1);
+            const float *src = (which ? a.w2 : a.w) + (int64_t)gr * K + kt * F32_TILE + s * 4;
+            cp_async16(st + which * W_PIECES + r * 8 + (s ^ (r & 7)), src);
+        }
+        if (t < TOK * 8) {
+            const int mm = t / 8, s = t % 8;
+            const int m = min(m0 + mm, a.m - 1);
+            const int64_t xr = a.row_map ? a.row_map[m] : m;
+            cp_async16(st + NW * W_PIECES + mm * 8 + s, a.x + xr * K + kt * F32_TILE + s * 4);
+        }
+    };
+
+    for (int m0 = 0; m0 < a.m; m0 += TOK) {
+        float acc[TOK], acc2[TWO ? TOK : 1];
+#pragma unroll
+        for (int i = 0; i < TOK; ++i) {
+            acc[i] = 0.0f;
+            if (TWO) acc2[i] = 0.0f;
+        }
+#pragma unroll
+        for (int s = 0; s < F32_STAGES - 1; ++s) {
+            if (s < tiles) load_tile(s, s, m0);
+            cp_async_commit();
+        }
+        for (int kt = 0; kt < tiles; ++kt) {
+            cp_async_wait<F32_STAGES - 2>();
+            __syncthreads();
+            const int nxt = kt + F32_STAGES - 1;
+            if (nxt < tiles) load_tile(nxt % F32_STAGES, nxt, m0);
+            cp_async_commit();
+            const float4 *st = smem4 + (kt % F32_STAGES) * STAGE_F4;
+            const float4 *xt = st + NW * W_PIECES;
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+                const float4 wv = st[t * 8 + (s ^ (t & 7))];
+                float4 wv2 = wv;
+                if (TWO) wv2 = st[W_PIECES + t * 8 + (s ^ (t & 7))];
+#pragma unroll
+                for (int i = 0; i < TOK; ++i) {
+                    const float4 xv = xt[i * 8 + s];
+                    acc[i] = fadd(acc[i], fmul(xv.x, wv.x));
+                    acc[i] = fadd(acc[i], fmul(xv.y, wv.y));
+                    acc[i] = fadd(acc[i], fmul(xv.z, wv.z));
+                    acc[i] = fadd(acc[i], fmul(xv.w, wv.w));
+                    if (TWO) {
+                        acc2[i] = fadd(acc2[i], fmul(xv.x, wv2.x));
+                        acc2[i] = fadd(acc2[i], fmul(xv.y, wv2.y));
+                        acc2[i] = fadd(acc2[i], fmul(xv.z, wv2.z));
+                        acc2[i] = fadd(acc2[i], fmul(xv.w, wv2.w));
+                    }
+                }
+            }
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        // epilogue
+#pragma unroll
+        for (int i = 0; i < TOK; ++i) {
+            const int m = m0 + i;
+            if (m >= a.m) break;
+            if (row < a.n) {
+                float y = acc[i];
+                if (EPI == EPI_BIAS) y = fadd(y, a.bias[row]);
+                if (EPI == EPI_RESIDUAL) y = fadd(a.residual[(int64_t)m * a.n + row], y);
+                if (EPI == EPI_SWIGLU) y = swiglu(y, acc2[i], tab);
+                if (a.out) a.out[(int64_t)m * a.n + row] = y;
+            }
+            if (ARGMAX) {
+                float v = row < a.n ? acc[i] : __uint_as_float(0xff800000u);
+                int idx = row < a.n ? row : 0x7fffffff;
+                if (row >= a.n) v = -__uint_as_float(0x7f800000u);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+                    if (argmax_better(ov, oi, v, idx)) { v = ov; idx = oi; }
+                }
+                __shared__ float wv[F32_ROWS / 32];
+                __shared__ int wi[F32_ROWS / 32];
+                if ((t & 31) == 0) { wv[t / 32] = v; wi[t / 32] = idx; }
+                __syncthreads();
+                if (t == 0) {
+                    for (int q = 1; q < F32_ROWS / 32; ++q)
+                        if (argmax_better(wv[q], wi[q], v, idx)) { v = wv[q]; idx = wi[q]; }
+                    a.part_val[(int64_t)m * gridDim.x + blockIdx.x] = v;
+                    a.part_idx[(int64_t)m * gridDim.x + blockIdx.x] = idx;
+                }
+                __syncthreads();
+            }
+        }
+    }
+    if (ARGMAX) {
+        // the last CTA to finish reduces the per-CTA winners, in CTA order
+        __shared__ bool last;
+        __threadfence();
+        __syncthreads();
+        if (t == 0) last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            for (int m = t / 32; m < a.m; m += F32_ROWS / 32) {
+                float v = -__uint_as_float(0x7f800000u);
+                int idx = 0x7fffffff;
+                for (int c = t % 32; c < (int)gridDim.x; c += 32) {
+                    const float cv = __ldcg(a.part_val + (int64_t)m * gridDim.x + c);
+                    const int ci = __ldcg(a.part_idx + (int64_t)m * gridDim.x + c);
+                    if (argmax_better(cv, ci, v, idx)) { v = cv; idx = ci; }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+                    if (argmax_better(ov, oi, v, idx)) { v = ov; idx = oi; }
+                }
+                if ((t & 31) == 0) a.tokens[m] = idx;
+            }
+            if (t == 0) *a.counter = 0u;
+        }
+    }
+}
+
+// ---- RoPE + KV append + decode attention ----------------------------------------------------
+// Per (row, KV head) one CTA over the `group` query heads that share that KV head
+// (repeat_kv, nanocompile/nn.py:109-120).  q and k get RoPE exactly as the fused elementwise
+// kernel does it (nanocompile/nn.py:97-106: t1 = y + b, t1*cos + rot(t1)*sin, bias already in
+// qkv); the new k/v go to the cache; then per head (nanocompile/models/qwen2.py:143-150,
+// nn.py:57-66): scores acc = acc + q*k over d in order, t = score * scale + 0, NaN-propagating
+// max, in-order sum of expf(t - max), p = expf(t - max) / sum, and ctx = in-order sum of p*v.
+// Positions after the row's own are masked in the reference (-inf, so exp = 0 and they add
+// exact zeros); they are skipped here, which is the same result for finite inputs.
+struct AttnArgs {
+    float *ctx;                // [rows, heads*d]
+    const float *qkv;          // [rows, (heads + 2*kv)*d]
+    float *cache;              // this layer, slot 0: [{K,V}][kv][cap][d]; slot stride below
+    const float *cos_tab, *sin_tab;   // [cap, d/2]
+    const int32_t *slot, *pos;
+    int64_t slot_stride;
+    int heads, kv, d, cap;
+    float scale;
+    int mode;                  // 0: rope + append + attend (decode); 1: rope + append only; 2: attend only
+};
+
+constexpr int ATTN_THREADS = 512;
+
+__global__ void __launch_bounds__(ATTN_THREADS)
+attention_kernel(AttnArgs a) {
+    extern __shared__ float sm[];
+    const int group = a.heads / a.kv, d = a.d, half = d / 2;
+    const int r = blockIdx.x / a.kv, g = blockIdx.x % a.kv;
+    const int pos = a.pos[r], len = pos + 1;
+    float *q = sm;                       // [group][d]
+    float *kn = q + group * d;           // [d]
+    float *vn = kn + d;                  // [d]
+    float *sums = vn + d;                // [group]
+    float *maxes = sums + group;         // [group]
+    float *sc = maxes + group;           // [group][len]
+    __shared__ uint64_t tab[32];
+    __shared__ float wmax[ATTN_THREADS / 32][8];
+    if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
+
+    float *base = a.cache + (int64_t)a.slot[r] * a.slot_stride;
+    float *K = base + (int64_t)g * a.cap * d;
+    float *V = base + ((int64_t)a.kv + g) * a.cap * d;
+    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * d;
+    const float *cs = a.cos_tab + (int64_t)pos * half, *sn = a.sin_tab + (int64_t)pos * half;
+
+    if (a.mode != 2) {
+        for (int i = threadIdx.x; i < (group + 2) * d; i += ATTN_THREADS) {
+            const int h = i / d, e = i % d;
+            const float *src;
+            if (h < group) src = qkv + (g * group + h) * d;
+            else if (h == group) src = qkv + (a.heads + g) * d;
+            else src = qkv + (a.heads + a.kv + g) * d;
+            if (h == group + 1) {                 // v: no rotation
+                vn[e] = src[e];
+                continue;
+            }
+            const float t1 = src[e];
+            const float rot = e < half ? -src[e + half] : src[e - half];
+            const float v = fadd(fmul(t1, cs[e % half]), fmul(rot, sn[e % half]));
+            if (h < group) q[h * d + e] = v;
+            else kn[e] = v;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < d; e += ATTN_THREADS) {
+            K[(int64_t)pos * d + e] = kn[e];
+            V[(int64_t)pos * d + e] = vn[e];
+        }
+        if (a.mode == 1) return;
+    } else {
+        for (int i = threadIdx.x; i < group * d; i += ATTN_THREADS) {
+            const int h = i / d, e = i % d;
+            const float *src = qkv + (g * group + h) * d;
+            const float t1 = src[e];
+            const float rot = e < half ? -src[e + half] : src[e - half];
+            q[h * d + e] = fadd(fmul(t1, cs[e % half]), fmul(rot, sn[e % half]));
+        }
+        __syncthreads();
+    }
+
+    // scores, with each thread's running max per head
+    float mx[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) mx[h] = __uint_as_float(0xff800000u);
+    for (int jpos = threadIdx.x; jpos < len; jpos += ATTN_THREADS) {
+        const float *krow = (a.mode == 0 && jpos == pos) ? kn : K + (int64_t)jpos * d;
+        float acc[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
+        for (int e = 0; e < d; e += 4) {
+            const float4 kv4 = *reinterpret_cast<const float4 *>(krow + e);
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                if (h < group) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(q + h * d + e);
+                    acc[h] = fadd(acc[h], fmul(q4.x, kv4.x));
+                    acc[h] = fadd(acc[h], fmul(q4.y, kv4.y));
+                    acc[h] = fadd(acc[h], fmul(q4.z, kv4.z));
+                    acc[h] = fadd(acc[h], fmul(q4.w, kv4.w));
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            if (h < group) {
+                const float t = fadd(fmul(acc[h], a.scale), 0.0f);
+                sc[h * len + jpos] = t;
+                mx[h] = nan_max(mx[h], t);
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 8; ++h) mx[h] = warp_nan_max(mx[h]);
+    if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) wmax[threadIdx.x / 32][h] = mx[h];
+    }
+    __syncthreads();
+    if (threadIdx.x < group) {
+        float m = __uint_as_float(0xff800000u);
+        for (int w = 0; w < ATTN_THREADS / 32; ++w) m = nan_max(m, wmax[w][threadIdx.x]);
+        maxes[threadIdx.x] = m;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < group * len; i += ATTN_THREADS) {
+        const int h = i / len;
+        sc[i] = expf_exact(fsub(sc[i], maxes[h]), tab);
+    }
+    __syncthreads();
+    if (threadIdx.x < group) {               // the in-order sums, one thread per head
+        const float *row = sc + threadIdx.x * len;
+        float acc = 0.0f;
+        for (int jpos = 0; jpos < len; ++jpos) acc = fadd(acc, row[jpos]);
+        sums[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < group * len; i += ATTN_THREADS) sc[i] = fdiv(sc[i], sums[i / len]);
+    __syncthreads();
+    // probabilities @ V: one thread per (head, dim), in position order
+    for (int i = threadIdx.x; i < group * d; i += ATTN_THREADS) {
+        const int h = i / d, e = i % d;
+        const float *p = sc + h * len;
+        float acc = 0.0f;
+        int jpos = 0;
+        const int last = a.mode == 0 ? pos : len;     // mode 0: the new row comes from smem
+        for (; jpos + 8 <= last; jpos += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = V[(int64_t)(jpos + u) * d + e];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = fadd(acc, fmul(p[jpos + u], v[u]));
+        }
+        for (; jpos < last; ++jpos) acc = fadd(acc, fmul(p[jpos], V[(int64_t)jpos * d + e]));
+        if (a.mode == 0) acc = fadd(acc, fmul(p[pos], vn[e]));
+        a.ctx[(int64_t)r * a.heads * d + (g * group + h) * d + e] = acc;
+    }
+}
+
+// ---- small helpers ---------------------------------------------------------------------------
+__global__ void xor80_kernel(uint8_t *p, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        p[i] ^= 0x80;
+}
+
+__global__ void expf_kernel(float *out, const float *x, int64_t n) {
+    __shared__ uint64_t tab[32];
+    if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
+    __syncthreads();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = expf_exact(x[i], tab);
+}
+
+// After a decode step: the argmax becomes the next input, positions advance, and the token
+// is appended to the device-side history.
+__global__ void advance_kernel(int64_t *ids, int32_t *pos, const int64_t *tokens, int64_t *history,
+                               int32_t *step, int rows) {
+    const int r = threadIdx.x;
+    const int s = *step;
+    if (r < rows) {
+        ids[r] = tokens[r];
+        pos[r] += 1;
+        history[(int64_t)s * rows + r] = tokens[r];
+    }
+    __syncthreads();
+    if (r == 0) *step = s + 1;
+}
+
+}  // namespace nc
