@@ -127,6 +127,37 @@ __device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bs
     return scale;
 }
 
+// ---- in-order sums -------------------------------------------------------------------------
+// acc = acc + p[0] + p[1] + ... strictly left to right, by one thread, with the next 32 values
+// loaded while the current 32 are added, so the chain runs at the add latency rather than
+// the shared-memory latency.  p must be 16-byte aligned.
+__device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.0f) {
+    const int n32 = n & ~31;
+    if (n32) {
+        const float4 *p4 = reinterpret_cast<const float4 *>(p);
+        float4 cur[8], nxt[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cur[u] = p4[u];
+        for (int i = 0; i < n32; i += 32) {
+            if (i + 32 < n32) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) nxt[u] = p4[(i + 32) / 4 + u];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                acc = fadd(acc, cur[u].x);
+                acc = fadd(acc, cur[u].y);
+                acc = fadd(acc, cur[u].z);
+                acc = fadd(acc, cur[u].w);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+        }
+    }
+    for (int i = n32; i < n; ++i) acc = fadd(acc, p[i]);
+    return acc;
+}
+
 // ---- epilogues ----------------------------------------------------------------------------
 enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3 };
 

@@ -105,7 +105,7 @@ int32_t launch_norm(cudaStream_t st, float *normed, const float *x, const float 
                     float *off, int32_t *bsums, const int32_t *row_map, int rows, int n, float eps) {
     if (rows <= 0) return NC_OK;
     if (n > 8192 || (xq && n % QBLOCK)) return fail(NC_ERR_ARGUMENT, "rms_norm width %d unsupported", n);
-    const size_t smem = sizeof(float) * 2 * (size_t)n;
+    const size_t smem = sizeof(float) * (((size_t)n + 3) / 4 * 4 + (size_t)n);
     CUDA_TRY(allow_smem(norm_quant_kernel, smem));
     norm_quant_kernel<<<rows, NORM_THREADS, smem, st>>>(normed, x, w, xq, xs, off, bsums, row_map, n, eps);
     return check_launch("norm_quant_kernel");
@@ -133,14 +133,29 @@ int32_t launch_i8_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
     return check_launch("gemv_i8_kernel");
 }
 
+template <int LPR, int NCH>
+int32_t launch_ws_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
+    constexpr int WARPS = 4, RPW = 32 / LPR;
+    const int grid = (a.n + WARPS * RPW - 1) / (WARPS * RPW);
+    switch (epi) {
+        case EPI_NONE: gemv_i8_ws_kernel<LPR, NCH, EPI_NONE><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_BIAS: gemv_i8_ws_kernel<LPR, NCH, EPI_BIAS><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_RESIDUAL: gemv_i8_ws_kernel<LPR, NCH, EPI_RESIDUAL><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_SWIGLU: gemv_i8_ws_kernel<LPR, NCH, EPI_SWIGLU><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+    return check_launch("gemv_i8_ws_kernel");
+}
+
+// Lanes per row by shape: the weights-stationary kernel keeps a row's slices in registers
+// (up to 8 chunks of 16/8 bytes per lane, or 40 chunks of 4 bytes); wider rows stream.
 int32_t launch_i8(cudaStream_t st, const GemvI8Args &a, int epi) {
     if (a.m <= 0 || a.n <= 0) return NC_OK;
     if (a.k % QBLOCK) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a whole number of 32-blocks", a.k);
-    const bool long_k = a.k > 1024;
-    if (a.m == 1) {
-        return long_k ? launch_i8_epi<32, 1, 16>(st, a, epi) : launch_i8_epi<8, 1, 8>(st, a, epi);
-    }
-    return long_k ? launch_i8_epi<32, 4, 16>(st, a, epi) : launch_i8_epi<8, 4, 8>(st, a, epi);
+    const int chunks = a.k / CHUNK;
+    if (chunks <= 8) return a.n <= 2048 ? launch_ws_epi<16, 8>(st, a, epi) : launch_ws_epi<8, 8>(st, a, epi);
+    if (chunks <= 40) return launch_ws_epi<32, 40>(st, a, epi);
+    return a.m == 1 ? launch_i8_epi<32, 1, 16>(st, a, epi) : launch_i8_epi<32, 4, 16>(st, a, epi);
 }
 
 template <int TOK, int EPI, bool ARGMAX>
@@ -170,21 +185,20 @@ int32_t launch_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) 
     if (a.m <= 0 || a.n <= 0) return NC_OK;
     if (a.k % F32_TILE) return fail(NC_ERR_ARGUMENT, "float32 width %d is not a multiple of %d", a.k, F32_TILE);
     if (argmax && epi != EPI_NONE) return fail(NC_ERR_ARGUMENT, "argmax takes no epilogue");
-    return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<8>(st, a, epi, argmax);
+    return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<16>(st, a, epi, argmax);
 }
 
-size_t attention_smem(int group, int d, int cap) {
-    return sizeof(float) * ((size_t)(group + 2) * d + 2 * (size_t)group + (size_t)group * cap);
+size_t attention_smem(int d, int cap) {
+    return sizeof(float) * ((size_t)ATTN_VSTAGES * ATTN_VCHUNK * d + ((size_t)cap + 3) / 4 * 4 + 3 * (size_t)d);
 }
 
 int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
     if (rows <= 0) return NC_OK;
-    const int group = a.heads / a.kv;
-    if (group > 8 || a.heads % a.kv || a.d % 4) return fail(NC_ERR_ARGUMENT, "attention shape unsupported");
-    const size_t smem = attention_smem(group, a.d, a.cap);
+    if (a.heads % a.kv || a.d % 4 || a.d > ATTN_THREADS) return fail(NC_ERR_ARGUMENT, "attention shape unsupported");
+    const size_t smem = attention_smem(a.d, a.cap);
     if (smem > 220 * 1024) return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
     CUDA_TRY(allow_smem(attention_kernel, smem));
-    attention_kernel<<<rows * a.kv, ATTN_THREADS, smem, st>>>(a);
+    attention_kernel<<<rows * a.heads, ATTN_THREADS, smem, st>>>(a);
     return check_launch("attention_kernel");
 }
 
@@ -459,11 +473,11 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     if (!cfg || !out || !inv_freq) return fail(NC_ERR_ARGUMENT, "null argument");
     const nc_qwen2_config c = *cfg;
     if (c.hidden <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads || c.head_dim % 4 ||
-        c.heads / c.kv_heads > 8 || c.max_rows <= 0 || c.max_rows > 1024 || c.slots <= 0 || c.capacity <= 0)
+        c.head_dim > 256 || c.max_rows <= 0 || c.max_rows > 1024 || c.slots <= 0 || c.capacity <= 0)
         return fail(NC_ERR_ARGUMENT, "unsupported model shape");
     if (c.hidden % 32 || c.inter % 32 || (c.heads * c.head_dim) % 32)
         return fail(NC_ERR_ARGUMENT, "widths must be whole 32-blocks");
-    if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024)
+    if (attention_smem((int)c.head_dim, c.capacity) > 220 * 1024)
         return fail(NC_ERR_ARGUMENT, "capacity %d exceeds the attention kernel's shared memory", c.capacity);
 
     auto m = std::make_unique<nc_model>();

@@ -47,11 +47,10 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
                   int8_t *__restrict__ xq, float *__restrict__ xs, float *__restrict__ offset,
                   int32_t *__restrict__ bsums, const int32_t *__restrict__ row_map, int n, float eps) {
     extern __shared__ float smem[];
-    float *row = smem;            // [n]
-    float *sq = smem + n;         // [n]: squares, then the normalized row
+    float *sq = smem;                          // [n]: squares, then the normalized row
+    float *row = smem + ((n + 3) & ~3);        // [n]
     __shared__ float s_inv;
-    __shared__ float s_scale[256];
-    __shared__ int s_bsum[256];
+    __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
     const int64_t in_row = row_map ? row_map[b] : b;
     const float *xr = x + in_row * n;
@@ -61,23 +60,7 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
         sq[i] = fmul(v, v);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float acc = 0.0f;
-        int i = 0;
-        if ((n & 3) == 0) {
-            const float4 *s4 = reinterpret_cast<const float4 *>(sq);
-            for (; i < n / 4; ++i) {
-                const float4 v = s4[i];
-                acc = fadd(acc, v.x);
-                acc = fadd(acc, v.y);
-                acc = fadd(acc, v.z);
-                acc = fadd(acc, v.w);
-            }
-            i *= 4;
-        }
-        for (; i < n; ++i) acc = fadd(acc, sq[i]);
-        s_inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(acc, (float)n), eps)));
-    }
+    if (threadIdx.x == 0) s_inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(chain_sum(sq, n), (float)n), eps)));
     __syncthreads();
     const float inv = s_inv;
     for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
@@ -96,24 +79,18 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
         if (lane == 0) {
             xs[(int64_t)b * blocks + blk] = scale;
             if (bsums) bsums[(int64_t)b * blocks + blk] = bs;
-            s_scale[blk] = scale;
-            s_bsum[blk] = bs;
+            s_term[blk] = fmul((float)bs, scale);
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float acc = 0.0f;
-        for (int blk = 0; blk < blocks; ++blk) acc = fadd(acc, fmul((float)s_bsum[blk], s_scale[blk]));
-        offset[b] = fmul(acc, 128.0f);
-    }
+    if (threadIdx.x == 0) offset[b] = fmul(chain_sum(s_term, blocks), 128.0f);
 }
 
 // Block quantization alone, one CTA (8 warps) per row; up to 256 blocks (k <= 8192).
 __global__ void __launch_bounds__(NORM_THREADS)
 quantize_kernel(int8_t *__restrict__ xq, const float *__restrict__ x, float *__restrict__ xs,
                 float *__restrict__ offset, int32_t *__restrict__ bsums, int k) {
-    __shared__ float s_scale[256];
-    __shared__ int s_bsum[256];
+    __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = k / QBLOCK;
     for (int blk = warp; blk < blocks; blk += NORM_THREADS / 32) {
@@ -124,16 +101,11 @@ quantize_kernel(int8_t *__restrict__ xq, const float *__restrict__ x, float *__r
         if (lane == 0) {
             xs[(int64_t)b * blocks + blk] = scale;
             if (bsums) bsums[(int64_t)b * blocks + blk] = bs;
-            s_scale[blk] = scale;
-            s_bsum[blk] = bs;
+            s_term[blk] = fmul((float)bs, scale);
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float acc = 0.0f;
-        for (int blk = 0; blk < blocks; ++blk) acc = fadd(acc, fmul((float)s_bsum[blk], s_scale[blk]));
-        offset[b] = fmul(acc, 128.0f);
-    }
+    if (threadIdx.x == 0) offset[b] = fmul(chain_sum(s_term, blocks), 128.0f);
 }
 
 // ---- int8-vnni GEMV / skinny GEMM -----------------------------------------------------------
@@ -311,6 +283,99 @@ gemv_i8_kernel(GemvI8Args a) {
                 }
                 a.out[(int64_t)m * a.n + row] = out;
             }
+        }
+    }
+}
+
+// Weights-stationary form: each lane loads its BPL-byte slice of every chunk of its row once,
+// into registers (NCH chunks at most), then walks the tokens.  The weights cross HBM once per
+// step whatever the number of tokens; the activations are re-read from L1.
+template <int LPR, int NCH, int EPI>
+__global__ void __launch_bounds__(128)
+gemv_i8_ws_kernel(GemvI8Args a) {
+    constexpr int BPL = 128 / LPR;
+    constexpr int APL = BPL / 4;
+    constexpr bool TWO = EPI == EPI_SWIGLU;
+    constexpr int MAXG = 3;                 // 32-byte groups past the last whole chunk
+    using SegT = typename Seg<BPL>::T;
+    __shared__ uint64_t tab[32];
+    if (EPI == EPI_SWIGLU) {
+        if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
+        __syncthreads();
+    }
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int grp = lane / LPR, j = lane % LPR;
+    const int row = (blockIdx.x * (blockDim.x / 32) + warp) * (32 / LPR) + grp;
+    const bool row_ok = row < a.n;
+    const int rowc = row_ok ? row : a.n - 1;
+    const int K = a.k, blocks = K / QBLOCK;
+    const int chunks = K / CHUNK, stride = chunks * CHUNK, groups = (K % CHUNK) / 32;
+    const bool tail_lane = j * BPL < 32;
+    const uint8_t *wrow = a.w + (int64_t)rowc * K;
+    const uint8_t *wrow2 = TWO ? a.w2 + (int64_t)rowc * K : nullptr;
+
+    uint32_t wv[NCH][APL], wv2[TWO ? NCH : 1][APL], tw[MAXG][APL], tw2[TWO ? MAXG : 1][APL];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        if (c < chunks) {
+            Seg<BPL>::split(__ldcs(reinterpret_cast<const SegT *>(wrow + c * CHUNK + j * BPL)), wv[c]);
+            if (TWO) Seg<BPL>::split(__ldcs(reinterpret_cast<const SegT *>(wrow2 + c * CHUNK + j * BPL)), wv2[c]);
+        }
+    }
+#pragma unroll
+    for (int k1 = 0; k1 < MAXG; ++k1) {
+        if (k1 < groups && tail_lane) {
+            Seg<BPL>::split(__ldcs(reinterpret_cast<const SegT *>(wrow + stride + k1 * 32 + j * BPL)), tw[k1]);
+            if (TWO) Seg<BPL>::split(__ldcs(reinterpret_cast<const SegT *>(wrow2 + stride + k1 * 32 + j * BPL)), tw2[k1]);
+        }
+    }
+    const float scale = a.scales[rowc];
+    const float scale2 = TWO ? a.scales2[rowc] : 0.0f;
+    for (int m = 0; m < a.m; ++m) {
+        const int8_t *xrow = a.xq + (int64_t)m * K;
+        const float *xsr = a.xs + (int64_t)m * blocks;
+        float acc[APL], acc2[APL];
+#pragma unroll
+        for (int i = 0; i < APL; ++i) { acc[i] = 0.0f; acc2[i] = 0.0f; }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            if (c < chunks) {
+                const int off = c * CHUNK + j * BPL;
+                uint32_t xv[APL];
+                Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow + off), xv);
+                const float s = xsr[off / QBLOCK];
+#pragma unroll
+                for (int i = 0; i < APL; ++i) {
+                    acc[i] = __fmaf_rn(dp4_lane(wv[c][i], xv[i]), s, acc[i]);
+                    if (TWO) acc2[i] = __fmaf_rn(dp4_lane(wv2[c][i], xv[i]), s, acc2[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k1 = 0; k1 < MAXG; ++k1) {
+            if (k1 < groups && tail_lane) {
+                const int off = stride + k1 * 32 + j * BPL;
+                uint32_t xv[APL];
+                Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow + off), xv);
+                const float s = xsr[off / QBLOCK];
+#pragma unroll
+                for (int i = 0; i < APL; ++i) {
+                    acc[i] = __fmaf_rn(dp4_lane(tw[k1][i], xv[i]), s, acc[i]);
+                    if (TWO) acc2[i] = __fmaf_rn(dp4_lane(tw2[k1][i], xv[i]), s, acc2[i]);
+                }
+            }
+        }
+        const float sum = combine_lanes<APL>(acc);
+        const float sum2 = TWO ? combine_lanes<APL>(acc2) : 0.0f;
+        if (j == 0 && row_ok) {
+            const float off = a.offset[m];
+            const float y = fmul(fsub(sum, off), scale);
+            float out;
+            if (EPI == EPI_BIAS) out = fadd(y, a.bias[row]);
+            else if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)m * a.n + row], y);
+            else if (EPI == EPI_SWIGLU) out = swiglu(y, fmul(fsub(sum2, off), scale2), tab);
+            else out = y;
+            a.out[(int64_t)m * a.n + row] = out;
         }
     }
 }
@@ -500,12 +565,14 @@ gemv_f32_kernel(GemvF32Args a) {
 }
 
 // ---- RoPE + KV append + decode attention ----------------------------------------------------
-// Per (row, KV head) one CTA over the `group` query heads that share that KV head
-// (repeat_kv, nanocompile/nn.py:109-120).  q and k get RoPE exactly as the fused elementwise
-// kernel does it (nanocompile/nn.py:97-106: t1 = y + b, t1*cos + rot(t1)*sin, bias already in
-// qkv); the new k/v go to the cache; then per head (nanocompile/models/qwen2.py:143-150,
-// nn.py:57-66): scores acc = acc + q*k over d in order, t = score * scale + 0, NaN-propagating
-// max, in-order sum of expf(t - max), p = expf(t - max) / sum, and ctx = in-order sum of p*v.
+// One CTA per (row, query head).  q and k get RoPE exactly as the fused elementwise kernel does
+// it (nanocompile/nn.py:97-106: t1 = y + b, t1*cos + rot(t1)*sin; the bias is already in qkv);
+// the first head of each KV group writes the new k and v to the cache; then
+// (nanocompile/models/qwen2.py:143-150, nn.py:57-66): scores acc = acc + q*k over d in order,
+// t = score * scale + 0, NaN-propagating max, in-order sum of expf(t - max),
+// p = expf(t - max) / sum, ctx = in-order sum over positions of p * v.  The two position-long
+// sums are single-thread chains (chain_sum); V is staged through shared memory in chunks by
+// cp.async, several chunks ahead of the chain that consumes them.
 // Positions after the row's own are masked in the reference (-inf, so exp = 0 and they add
 // exact zeros); they are skipped here, which is the same result for finite inputs.
 struct AttnArgs {
@@ -520,23 +587,25 @@ struct AttnArgs {
     int mode;                  // 0: rope + append + attend (decode); 1: rope + append only; 2: attend only
 };
 
-constexpr int ATTN_THREADS = 512;
+constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_VCHUNK = 64;      // positions per staged V chunk
+constexpr int ATTN_VSTAGES = 4;
 
 __global__ void __launch_bounds__(ATTN_THREADS)
 attention_kernel(AttnArgs a) {
-    extern __shared__ float sm[];
-    const int group = a.heads / a.kv, d = a.d, half = d / 2;
-    const int r = blockIdx.x / a.kv, g = blockIdx.x % a.kv;
+    extern __shared__ __align__(16) float sm[];
+    const int d = a.d, half = d / 2, group = a.heads / a.kv;
+    const int r = blockIdx.x / a.heads, h = blockIdx.x % a.heads, g = h / group;
     const int pos = a.pos[r], len = pos + 1;
-    float *q = sm;                       // [group][d]
-    float *kn = q + group * d;           // [d]
-    float *vn = kn + d;                  // [d]
-    float *sums = vn + d;                // [group]
-    float *maxes = sums + group;         // [group]
-    float *sc = maxes + group;           // [group][len]
+    float *vbuf = sm;                                        // [VSTAGES][VCHUNK][d]
+    float *e = vbuf + ATTN_VSTAGES * ATTN_VCHUNK * d;        // [cap]: scores, exps, probabilities
+    float *q = e + ((a.cap + 3) & ~3);                       // [d]
+    float *kn = q + d, *vn = kn + d;                         // [d] each
     __shared__ uint64_t tab[32];
-    __shared__ float wmax[ATTN_THREADS / 32][8];
-    if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
+    __shared__ float wred[ATTN_THREADS / 32];
+    __shared__ float s_max, s_sum;
+    const int t = threadIdx.x;
+    if (t < 32) tab[t] = kExpTab[t];
 
     float *base = a.cache + (int64_t)a.slot[r] * a.slot_stride;
     float *K = base + (int64_t)g * a.cap * d;
@@ -544,116 +613,113 @@ attention_kernel(AttnArgs a) {
     const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * d;
     const float *cs = a.cos_tab + (int64_t)pos * half, *sn = a.sin_tab + (int64_t)pos * half;
 
-    if (a.mode != 2) {
-        for (int i = threadIdx.x; i < (group + 2) * d; i += ATTN_THREADS) {
-            const int h = i / d, e = i % d;
-            const float *src;
-            if (h < group) src = qkv + (g * group + h) * d;
-            else if (h == group) src = qkv + (a.heads + g) * d;
-            else src = qkv + (a.heads + a.kv + g) * d;
-            if (h == group + 1) {                 // v: no rotation
-                vn[e] = src[e];
-                continue;
-            }
-            const float t1 = src[e];
-            const float rot = e < half ? -src[e + half] : src[e - half];
-            const float v = fadd(fmul(t1, cs[e % half]), fmul(rot, sn[e % half]));
-            if (h < group) q[h * d + e] = v;
-            else kn[e] = v;
+    // RoPE of q (and of this group's new k), and v
+    for (int i = t; i < 3 * d; i += ATTN_THREADS) {
+        const int which = i / d, c = i % d;
+        const float *src = which == 0 ? qkv + h * d : (which == 1 ? qkv + (a.heads + g) * d : qkv + (a.heads + a.kv + g) * d);
+        if (which == 2) {
+            vn[c] = src[c];
+            continue;
         }
-        __syncthreads();
-        for (int e = threadIdx.x; e < d; e += ATTN_THREADS) {
-            K[(int64_t)pos * d + e] = kn[e];
-            V[(int64_t)pos * d + e] = vn[e];
-        }
-        if (a.mode == 1) return;
-    } else {
-        for (int i = threadIdx.x; i < group * d; i += ATTN_THREADS) {
-            const int h = i / d, e = i % d;
-            const float *src = qkv + (g * group + h) * d;
-            const float t1 = src[e];
-            const float rot = e < half ? -src[e + half] : src[e - half];
-            q[h * d + e] = fadd(fmul(t1, cs[e % half]), fmul(rot, sn[e % half]));
-        }
-        __syncthreads();
+        const float t1 = src[c];
+        const float rot = c < half ? -src[c + half] : src[c - half];
+        const float v = fadd(fmul(t1, cs[c % half]), fmul(rot, sn[c % half]));
+        (which == 0 ? q : kn)[c] = v;
     }
+    __syncthreads();
+    if (a.mode != 2 && h % group == 0) {
+        for (int c = t; c < d; c += ATTN_THREADS) {
+            K[(int64_t)pos * d + c] = kn[c];
+            V[(int64_t)pos * d + c] = vn[c];
+        }
+    }
+    if (a.mode == 1) return;
+    const bool own_new = a.mode == 0;      // position pos comes from kn / vn, not the cache
 
-    // scores, with each thread's running max per head
-    float mx[8];
-#pragma unroll
-    for (int h = 0; h < 8; ++h) mx[h] = __uint_as_float(0xff800000u);
-    for (int jpos = threadIdx.x; jpos < len; jpos += ATTN_THREADS) {
-        const float *krow = (a.mode == 0 && jpos == pos) ? kn : K + (int64_t)jpos * d;
-        float acc[8];
-#pragma unroll
-        for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
-        for (int e = 0; e < d; e += 4) {
-            const float4 kv4 = *reinterpret_cast<const float4 *>(krow + e);
-#pragma unroll
-            for (int h = 0; h < 8; ++h) {
-                if (h < group) {
-                    const float4 q4 = *reinterpret_cast<const float4 *>(q + h * d + e);
-                    acc[h] = fadd(acc[h], fmul(q4.x, kv4.x));
-                    acc[h] = fadd(acc[h], fmul(q4.y, kv4.y));
-                    acc[h] = fadd(acc[h], fmul(q4.z, kv4.z));
-                    acc[h] = fadd(acc[h], fmul(q4.w, kv4.w));
-                }
+    // stage the first V chunks while the scores and the sum are computed
+    const int chunks = (len + ATTN_VCHUNK - 1) / ATTN_VCHUNK;
+    const int pieces = ATTN_VCHUNK * d / 4;
+    auto stage_chunk = [&](int c) {
+        if (c < chunks) {
+            float *dst = vbuf + (c % ATTN_VSTAGES) * ATTN_VCHUNK * d;
+            for (int pc = t; pc < pieces; pc += ATTN_THREADS) {
+                const int row = pc / (d / 4), col = pc % (d / 4);
+                const int jpos = c * ATTN_VCHUNK + row;
+                if (jpos < len) cp_async16(dst + row * d + col * 4, V + (int64_t)jpos * d + col * 4);
             }
         }
+        cp_async_commit();
+    };
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-            if (h < group) {
-                const float t = fadd(fmul(acc[h], a.scale), 0.0f);
-                sc[h * len + jpos] = t;
-                mx[h] = nan_max(mx[h], t);
+    for (int c = 0; c < ATTN_VSTAGES - 1; ++c) stage_chunk(c);
+
+    // scores, two positions at a time per thread
+    float mx = __uint_as_float(0xff800000u);
+    for (int j0 = t; j0 < len; j0 += 2 * ATTN_THREADS) {
+        const int j1 = j0 + ATTN_THREADS;
+        const float *k0 = (own_new && j0 == pos) ? kn : K + (int64_t)j0 * d;
+        const float *k1 = j1 < len ? ((own_new && j1 == pos) ? kn : K + (int64_t)j1 * d) : k0;
+        float acc0 = 0.0f, acc1 = 0.0f;
+        for (int c = 0; c < d; c += 4) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(k0 + c);
+            const float4 a1 = *reinterpret_cast<const float4 *>(k1 + c);
+            const float4 qv = *reinterpret_cast<const float4 *>(q + c);
+            acc0 = fadd(acc0, fmul(qv.x, a0.x)); acc1 = fadd(acc1, fmul(qv.x, a1.x));
+            acc0 = fadd(acc0, fmul(qv.y, a0.y)); acc1 = fadd(acc1, fmul(qv.y, a1.y));
+            acc0 = fadd(acc0, fmul(qv.z, a0.z)); acc1 = fadd(acc1, fmul(qv.z, a1.z));
+            acc0 = fadd(acc0, fmul(qv.w, a0.w)); acc1 = fadd(acc1, fmul(qv.w, a1.w));
+        }
+        const float t0 = fadd(fmul(acc0, a.scale), 0.0f);
+        e[j0] = t0;
+        mx = nan_max(mx, t0);
+        if (j1 < len) {
+            const float t1 = fadd(fmul(acc1, a.scale), 0.0f);
+            e[j1] = t1;
+            mx = nan_max(mx, t1);
+        }
+    }
+    mx = warp_nan_max(mx);
+    if ((t & 31) == 0) wred[t / 32] = mx;
+    __syncthreads();
+    if (t == 0) {
+        float m = wred[0];
+        for (int w = 1; w < ATTN_THREADS / 32; ++w) m = nan_max(m, wred[w]);
+        s_max = m;
+    }
+    __syncthreads();
+    const float m = s_max;
+    for (int j = t; j < len; j += ATTN_THREADS) e[j] = expf_exact(fsub(e[j], m), tab);
+    __syncthreads();
+    if (t == 0) s_sum = chain_sum(e, len);
+    __syncthreads();
+    const float sum = s_sum;
+    for (int j = t; j < len; j += ATTN_THREADS) e[j] = fdiv(e[j], sum);
+
+    // probabilities @ V, chunk by chunk; thread c < d owns output c
+    float acc = 0.0f;
+    for (int c = 0; c < chunks; ++c) {
+        cp_async_wait<ATTN_VSTAGES - 2>();
+        __syncthreads();
+        stage_chunk(c + ATTN_VSTAGES - 1);
+        if (t < d) {
+            const float *vb = vbuf + (c % ATTN_VSTAGES) * ATTN_VCHUNK * d + t;
+            const int j0 = c * ATTN_VCHUNK;
+            const int n = min(ATTN_VCHUNK, len - j0);
+            const int stop = (own_new && j0 + n == len) ? n - 1 : n;   // the new row comes from vn
+            int jj = 0;
+            for (; jj + 8 <= stop; jj += 8) {
+                float pv[8], vv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) { pv[u] = e[j0 + jj + u]; vv[u] = vb[(jj + u) * d]; }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc = fadd(acc, fmul(pv[u], vv[u]));
             }
+            for (; jj < stop; ++jj) acc = fadd(acc, fmul(e[j0 + jj], vb[jj * d]));
+            if (stop != n) acc = fadd(acc, fmul(e[pos], vn[t]));
         }
     }
-#pragma unroll
-    for (int h = 0; h < 8; ++h) mx[h] = warp_nan_max(mx[h]);
-    if ((threadIdx.x & 31) == 0) {
-#pragma unroll
-        for (int h = 0; h < 8; ++h) wmax[threadIdx.x / 32][h] = mx[h];
-    }
-    __syncthreads();
-    if (threadIdx.x < group) {
-        float m = __uint_as_float(0xff800000u);
-        for (int w = 0; w < ATTN_THREADS / 32; ++w) m = nan_max(m, wmax[w][threadIdx.x]);
-        maxes[threadIdx.x] = m;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < group * len; i += ATTN_THREADS) {
-        const int h = i / len;
-        sc[i] = expf_exact(fsub(sc[i], maxes[h]), tab);
-    }
-    __syncthreads();
-    if (threadIdx.x < group) {               // the in-order sums, one thread per head
-        const float *row = sc + threadIdx.x * len;
-        float acc = 0.0f;
-        for (int jpos = 0; jpos < len; ++jpos) acc = fadd(acc, row[jpos]);
-        sums[threadIdx.x] = acc;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < group * len; i += ATTN_THREADS) sc[i] = fdiv(sc[i], sums[i / len]);
-    __syncthreads();
-    // probabilities @ V: one thread per (head, dim), in position order
-    for (int i = threadIdx.x; i < group * d; i += ATTN_THREADS) {
-        const int h = i / d, e = i % d;
-        const float *p = sc + h * len;
-        float acc = 0.0f;
-        int jpos = 0;
-        const int last = a.mode == 0 ? pos : len;     // mode 0: the new row comes from smem
-        for (; jpos + 8 <= last; jpos += 8) {
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = V[(int64_t)(jpos + u) * d + e];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc = fadd(acc, fmul(p[jpos + u], v[u]));
-        }
-        for (; jpos < last; ++jpos) acc = fadd(acc, fmul(p[jpos], V[(int64_t)jpos * d + e]));
-        if (a.mode == 0) acc = fadd(acc, fmul(p[pos], vn[e]));
-        a.ctx[(int64_t)r * a.heads * d + (g * group + h) * d + e] = acc;
-    }
+    cp_async_wait<0>();
+    if (t < d) a.ctx[(int64_t)r * a.heads * d + h * d + t] = acc;
 }
 
 // ---- small helpers ---------------------------------------------------------------------------
