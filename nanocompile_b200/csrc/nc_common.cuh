@@ -113,48 +113,66 @@ __device__ __forceinline__ float swiglu(float g, float u, const uint64_t *tab) {
 
 // One 32-value block of block-32 quantization by one warp, lane = position in the block
 // (nanocompile/quantize.py:102-124): returns the scale; *q the lane's int8 and *bsum the
-// block's int32 sum.
-__device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bsum) {
-    const float a = (0.0f <= v) ? v : -v;
-    const float mag = warp_nan_max(a);
-    const float scale = (mag <= 0.0f) ? 1.0f : fdiv(mag, 127.0f);
+// block's int32 sum.  |v| >= 0 orders like its bit pattern, so the block maximum is one
+// integer max-reduction; a NaN anywhere makes the maximum a NaN, as the reference's
+// NaN-propagating max does (only the NaN payload may differ).  A -0 magnitude becomes +0,
+// which gives the same scale (mag <= 0 -> 1).
+__device__ __forceinline__ float block_magnitude(float v) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu));
+}
+__device__ __forceinline__ float block_scale(float mag) { return (mag <= 0.0f) ? 1.0f : fdiv(mag, 127.0f); }
+__device__ __forceinline__ int8_t quantize_value(float v, float scale) {
     float t = roundf(fdiv(v, scale));
     t = (t <= 127.0f) ? t : 127.0f;
     t = (-127.0f <= t) ? t : -127.0f;
-    const int8_t qi = (int8_t)t;
+    return (int8_t)t;
+}
+__device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bsum) {
+    const float scale = block_scale(block_magnitude(v));
+    const int8_t qi = quantize_value(v, scale);
     *q = qi;
-    *bsum = warp_sum_int((int)qi);
+    *bsum = __reduce_add_sync(0xffffffffu, (int)qi);
     return scale;
 }
 
 // ---- in-order sums -------------------------------------------------------------------------
-// acc = acc + p[0] + p[1] + ... strictly left to right, by one thread, with the next 32 values
-// loaded while the current 32 are added, so the chain runs at the add latency rather than
-// the shared-memory latency.  p must be 16-byte aligned.
+// acc = acc + p[0] + p[1] + ... strictly left to right, by one thread.  Two 32-value register
+// buffers alternate: the next block's shared-memory loads are issued before the current
+// block's 32 dependent adds, so the chain runs at the add latency.  p must be 16-byte aligned.
+__device__ __forceinline__ void add32(float &acc, const float4 *v) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        acc = fadd(acc, v[u].x);
+        acc = fadd(acc, v[u].y);
+        acc = fadd(acc, v[u].z);
+        acc = fadd(acc, v[u].w);
+    }
+}
+
 __device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.0f) {
     const int n32 = n & ~31;
+    const float4 *p4 = reinterpret_cast<const float4 *>(p);
+    float4 a[8], b[8];
+    int i = 0;
     if (n32) {
-        const float4 *p4 = reinterpret_cast<const float4 *>(p);
-        float4 cur[8], nxt[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) cur[u] = p4[u];
-        for (int i = 0; i < n32; i += 32) {
-            if (i + 32 < n32) {
+        for (int u = 0; u < 8; ++u) a[u] = p4[u];
+        for (; i + 64 <= n32; i += 64) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) nxt[u] = p4[(i + 32) / 4 + u];
+            for (int u = 0; u < 8; ++u) b[u] = p4[(i + 32) / 4 + u];
+            add32(acc, a);
+            if (i + 64 < n32) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) a[u] = p4[(i + 64) / 4 + u];
             }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                acc = fadd(acc, cur[u].x);
-                acc = fadd(acc, cur[u].y);
-                acc = fadd(acc, cur[u].z);
-                acc = fadd(acc, cur[u].w);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+            add32(acc, b);
+        }
+        if (i < n32) {
+            add32(acc, a);
+            i += 32;
         }
     }
-    for (int i = n32; i < n; ++i) acc = fadd(acc, p[i]);
+    for (; i < n; ++i) acc = fadd(acc, p[i]);
     return acc;
 }
 

@@ -105,7 +105,7 @@ int32_t launch_norm(cudaStream_t st, float *normed, const float *x, const float 
                     float *off, int32_t *bsums, const int32_t *row_map, int rows, int n, float eps) {
     if (rows <= 0) return NC_OK;
     if (n > 8192 || (xq && n % QBLOCK)) return fail(NC_ERR_ARGUMENT, "rms_norm width %d unsupported", n);
-    const size_t smem = sizeof(float) * (((size_t)n + 3) / 4 * 4 + (size_t)n);
+    const size_t smem = sizeof(float) * 3 * (((size_t)n + 3) / 4 * 4);
     CUDA_TRY(allow_smem(norm_quant_kernel, smem));
     norm_quant_kernel<<<rows, NORM_THREADS, smem, st>>>(normed, x, w, xq, xs, off, bsums, row_map, n, eps);
     return check_launch("norm_quant_kernel");
@@ -115,7 +115,7 @@ int32_t launch_quant(cudaStream_t st, int8_t *xq, const float *x, float *xs, flo
                      int rows, int k) {
     if (rows <= 0) return NC_OK;
     if (k % QBLOCK || k > 8192) return fail(NC_ERR_ARGUMENT, "quantize width %d unsupported", k);
-    quantize_kernel<<<rows, NORM_THREADS, 0, st>>>(xq, x, xs, off, bsums, k);
+    quantize_kernel<<<rows, NORM_THREADS, sizeof(float) * k, st>>>(xq, x, xs, off, bsums, k);
     return check_launch("quantize_kernel");
 }
 
@@ -133,29 +133,67 @@ int32_t launch_i8_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
     return check_launch("gemv_i8_kernel");
 }
 
-template <int LPR, int NCH>
-int32_t launch_ws_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
-    constexpr int WARPS = 4, RPW = 32 / LPR;
-    const int grid = (a.n + WARPS * RPW - 1) / (WARPS * RPW);
-    switch (epi) {
-        case EPI_NONE: gemv_i8_ws_kernel<LPR, NCH, EPI_NONE><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        case EPI_BIAS: gemv_i8_ws_kernel<LPR, NCH, EPI_BIAS><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        case EPI_RESIDUAL: gemv_i8_ws_kernel<LPR, NCH, EPI_RESIDUAL><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        case EPI_SWIGLU: gemv_i8_ws_kernel<LPR, NCH, EPI_SWIGLU><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
-    }
-    return check_launch("gemv_i8_ws_kernel");
+template <int LPR, int NCH, int PRO, int EPI>
+int32_t launch_fused_t(cudaStream_t st, const FusedI8Args &f, size_t smem) {
+    constexpr int THREADS = 256, ROWS = (THREADS / 32) * (32 / LPR);
+    auto kernel = gemv_i8_fused_kernel<LPR, NCH, PRO, EPI>;
+    CUDA_TRY(allow_smem(kernel, smem));
+    kernel<<<(f.g.n + ROWS - 1) / ROWS, THREADS, smem, st>>>(f);
+    return check_launch("gemv_i8_fused_kernel");
 }
 
-// Lanes per row by shape: the weights-stationary kernel keeps a row's slices in registers
-// (up to 8 chunks of 16/8 bytes per lane, or 40 chunks of 4 bytes); wider rows stream.
-int32_t launch_i8(cudaStream_t st, const GemvI8Args &a, int epi) {
+template <int LPR, int NCH, int PRO>
+int32_t launch_fused_epi(cudaStream_t st, const FusedI8Args &f, int epi, size_t smem) {
+    switch (epi) {
+        case EPI_NONE: return launch_fused_t<LPR, NCH, PRO, EPI_NONE>(st, f, smem);
+        case EPI_BIAS: return launch_fused_t<LPR, NCH, PRO, EPI_BIAS>(st, f, smem);
+        case EPI_RESIDUAL: return launch_fused_t<LPR, NCH, PRO, EPI_RESIDUAL>(st, f, smem);
+        case EPI_SWIGLU: return launch_fused_t<LPR, NCH, PRO, EPI_SWIGLU>(st, f, smem);
+        case EPI_SWIGLU_QUANT: return launch_fused_t<LPR, NCH, PRO, EPI_SWIGLU_QUANT>(st, f, smem);
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+}
+
+template <int LPR, int NCH>
+int32_t launch_fused_pro(cudaStream_t st, const FusedI8Args &f, int pro, int epi, size_t smem) {
+    switch (pro) {
+        case PRO_NONE: return launch_fused_epi<LPR, NCH, PRO_NONE>(st, f, epi, smem);
+        case PRO_OFFSET: return launch_fused_epi<LPR, NCH, PRO_OFFSET>(st, f, epi, smem);
+        case PRO_NORM:
+            if constexpr (NCH <= 8) return launch_fused_epi<LPR, NCH, PRO_NORM>(st, f, epi, smem);
+            return fail(NC_ERR_ARGUMENT, "the norm prologue takes widths up to 1024");
+        default: return fail(NC_ERR_ARGUMENT, "unknown prologue %d", pro);
+    }
+}
+
+// The int8-vnni projection: weights-stationary, lanes per row chosen by shape (a row's slices
+// must fit in registers: up to 8 chunks of 16 or 8 bytes per lane, or 40 chunks of 4 bytes).
+int32_t launch_i8_fused(cudaStream_t st, const FusedI8Args &f, int pro, int epi) {
+    const GemvI8Args &a = f.g;
     if (a.m <= 0 || a.n <= 0) return NC_OK;
     if (a.k % QBLOCK) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a whole number of 32-blocks", a.k);
-    const int chunks = a.k / CHUNK;
-    if (chunks <= 8) return a.n <= 2048 ? launch_ws_epi<16, 8>(st, a, epi) : launch_ws_epi<8, 8>(st, a, epi);
-    if (chunks <= 40) return launch_ws_epi<32, 40>(st, a, epi);
+    if (pro == PRO_NORM && a.m > PRO_NORM_ROWS) return fail(NC_ERR_ARGUMENT, "the norm prologue takes up to 4 rows");
+    if (epi == EPI_SWIGLU_QUANT && a.n % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized output width %d", a.n);
+    const int blocks = a.k / QBLOCK, bl4 = (blocks + 3) & ~3, chunks = a.k / CHUNK;
+    size_t smem = 32 * sizeof(float);
+    if (pro == PRO_NORM)
+        smem = std::max(smem, sizeof(float) * (4 * (size_t)a.k + bl4 + 4 + 4 * (size_t)blocks) + 4 * (size_t)a.k);
+    if (pro == PRO_OFFSET) smem = std::max(smem, sizeof(float) * ((size_t)a.m * bl4 + a.m));
+    if (smem > 200 * 1024) return fail(NC_ERR_ARGUMENT, "projection prologue needs too much shared memory");
+    if (chunks <= 8) {
+        if (a.n <= 2048 && epi != EPI_SWIGLU_QUANT) return launch_fused_pro<16, 8>(st, f, pro, epi, smem);
+        return launch_fused_pro<8, 8>(st, f, pro, epi, smem);
+    }
+    if (chunks <= 40 && epi != EPI_SWIGLU_QUANT) return launch_fused_pro<32, 40>(st, f, pro, epi, smem);
+    if (pro != PRO_NONE || epi == EPI_SWIGLU_QUANT)
+        return fail(NC_ERR_ARGUMENT, "int8 width %d too wide for the fused projection", a.k);
     return a.m == 1 ? launch_i8_epi<32, 1, 16>(st, a, epi) : launch_i8_epi<32, 4, 16>(st, a, epi);
+}
+
+int32_t launch_i8(cudaStream_t st, const GemvI8Args &a, int epi) {
+    FusedI8Args f{};
+    f.g = a;
+    return launch_i8_fused(st, f, PRO_NONE, epi);
 }
 
 template <int TOK, int EPI, bool ARGMAX>
@@ -357,7 +395,9 @@ struct nc_model {
     // activations and step state
     float *x = nullptr, *normed = nullptr, *xs = nullptr, *off = nullptr, *qkv = nullptr, *ctx = nullptr,
           *hbuf = nullptr, *logits = nullptr, *part_val = nullptr;
-    int8_t *xq = nullptr;
+    int8_t *xq = nullptr, *hq = nullptr;      // quantized activations: hidden-wide, and of the SwiGLU output
+    float *hxs = nullptr;
+    int32_t *bsums = nullptr;
     int32_t *part_idx = nullptr, *slot = nullptr, *pos = nullptr, *logit_row = nullptr, *step = nullptr;
     int64_t *ids = nullptr, *tokens = nullptr, *history = nullptr;
     unsigned long long *err = nullptr;
@@ -382,12 +422,22 @@ struct Layout {
     }
 };
 
+// One step: the fused groups of every layer, then the final norm and the LM head.  For int8
+// with few rows (decode, short prompts) five kernels per layer:
+//   q/k/v projection (rms_norm + quantize prologue, bias epilogue)
+//   RoPE + cache append + attention (quantizing epilogue)
+//   o projection (offset prologue, residual epilogue)
+//   gate/up projection (rms_norm + quantize prologue, silu*up + quantize epilogue)
+//   down projection (offset prologue, residual epilogue)
+// With more rows the norms run as their own row kernels (one CTA per row, in parallel).
 int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
     const nc_qwen2_config &c = m->c;
     cudaStream_t st = m->stream;
     const int H = (int)c.hidden, I = (int)c.inter, d = (int)c.head_dim;
     const int Hq = (int)(c.heads * d), Nqkv = (int)((c.heads + 2 * c.kv_heads) * d);
     const bool q8 = c.quant != 0;
+    const bool norm_fused = rows <= PRO_NORM_ROWS && H <= 8 * CHUNK;
+    const bool attn_quant = q8 && d % QBLOCK == 0;
 
     CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
     gather_kernel<<<rows, 256, 0, st>>>(m->x, m->ids, m->embed, m->err, c.vocab, H);
@@ -395,25 +445,31 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
 
     for (int l = 0; l < (int)c.layers; ++l) {
         const nc_model::Layer &L = m->layers[l];
-        // input norm (+ quantize) -> q/k/v projections with their biases
-        NC_TRY(launch_norm(st, q8 ? nullptr : m->normed, m->x, L.in_norm, q8 ? m->xq : nullptr, m->xs, m->off,
-                           nullptr, nullptr, rows, H, c.eps));
+        // input norm -> q/k/v projections with their biases
         if (q8) {
-            GemvI8Args a{};
-            a.out = m->qkv; a.xq = m->xq; a.xs = m->xs; a.offset = m->off; a.w = L.wqkv; a.scales = L.sqkv;
-            a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
-            NC_TRY(launch_i8(st, a, EPI_BIAS));
+            FusedI8Args f{};
+            f.g.out = m->qkv; f.g.xq = m->xq; f.g.xs = m->xs; f.g.offset = m->off; f.g.w = L.wqkv;
+            f.g.scales = L.sqkv; f.g.bias = L.bqkv; f.g.m = rows; f.g.n = Nqkv; f.g.k = H;
+            if (norm_fused) {
+                f.x = m->x; f.norm_w = L.in_norm; f.eps = c.eps;
+                NC_TRY(launch_i8_fused(st, f, PRO_NORM, EPI_BIAS));
+            } else {
+                NC_TRY(launch_norm(st, nullptr, m->x, L.in_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
+                NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_BIAS));
+            }
         } else {
+            NC_TRY(launch_norm(st, m->normed, m->x, L.in_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
             GemvF32Args a{};
             a.out = m->qkv; a.x = m->normed; a.w = L.fqkv; a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
             NC_TRY(launch_f32(st, a, EPI_BIAS, false));
         }
-        // RoPE, cache append, attention
+        // RoPE, cache append, attention (and the quantization of its output)
         AttnArgs at{};
-        at.ctx = m->ctx; at.qkv = m->qkv; at.cache = m->kv + (int64_t)l * m->layer_stride;
+        at.ctx = attn_quant ? nullptr : m->ctx; at.qkv = m->qkv; at.cache = m->kv + (int64_t)l * m->layer_stride;
         at.cos_tab = m->cos_tab; at.sin_tab = m->sin_tab; at.slot = m->slot; at.pos = m->pos;
         at.slot_stride = m->slot_stride; at.heads = (int)c.heads; at.kv = (int)c.kv_heads; at.d = d;
         at.cap = c.capacity; at.scale = c.attn_scale;
+        if (attn_quant) { at.q_out = m->xq; at.xs_out = m->xs; at.bsums_out = m->bsums; }
         if (fused) {
             at.mode = 0;
             NC_TRY(launch_attention(st, at, rows));
@@ -425,30 +481,40 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
         }
         // o_proj with the residual add
         if (q8) {
-            NC_TRY(launch_quant(st, m->xq, m->ctx, m->xs, m->off, nullptr, rows, Hq));
-            GemvI8Args a{};
-            a.out = m->x; a.xq = m->xq; a.xs = m->xs; a.offset = m->off; a.w = L.wo; a.scales = L.so;
-            a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
-            NC_TRY(launch_i8(st, a, EPI_RESIDUAL));
+            FusedI8Args f{};
+            f.g.out = m->x; f.g.xq = m->xq; f.g.xs = m->xs; f.g.offset = m->off; f.g.w = L.wo; f.g.scales = L.so;
+            f.g.residual = m->x; f.g.m = rows; f.g.n = H; f.g.k = Hq;
+            if (attn_quant) {
+                f.bsums_in = m->bsums;
+                NC_TRY(launch_i8_fused(st, f, PRO_OFFSET, EPI_RESIDUAL));
+            } else {
+                NC_TRY(launch_quant(st, m->xq, m->ctx, m->xs, m->off, nullptr, rows, Hq));
+                NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_RESIDUAL));
+            }
         } else {
             GemvF32Args a{};
             a.out = m->x; a.x = m->ctx; a.w = L.fo; a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
             NC_TRY(launch_f32(st, a, EPI_RESIDUAL, false));
         }
-        // post-attention norm -> gate/up with SiLU * up -> down with the residual add
-        NC_TRY(launch_norm(st, q8 ? nullptr : m->normed, m->x, L.post_norm, q8 ? m->xq : nullptr, m->xs, m->off,
-                           nullptr, nullptr, rows, H, c.eps));
+        // post-attention norm -> gate/up with silu * up (quantized) -> down with the residual add
         if (q8) {
-            GemvI8Args a{};
-            a.out = m->hbuf; a.xq = m->xq; a.xs = m->xs; a.offset = m->off; a.w = L.wg; a.scales = L.sg;
-            a.w2 = L.wu; a.scales2 = L.su; a.m = rows; a.n = I; a.k = H;
-            NC_TRY(launch_i8(st, a, EPI_SWIGLU));
-            NC_TRY(launch_quant(st, m->xq, m->hbuf, m->xs, m->off, nullptr, rows, I));
-            GemvI8Args b{};
-            b.out = m->x; b.xq = m->xq; b.xs = m->xs; b.offset = m->off; b.w = L.wd; b.scales = L.sd;
-            b.residual = m->x; b.m = rows; b.n = H; b.k = I;
-            NC_TRY(launch_i8(st, b, EPI_RESIDUAL));
+            FusedI8Args f{};
+            f.g.xq = m->xq; f.g.xs = m->xs; f.g.offset = m->off; f.g.w = L.wg; f.g.scales = L.sg;
+            f.g.w2 = L.wu; f.g.scales2 = L.su; f.g.m = rows; f.g.n = I; f.g.k = H;
+            f.q_out = m->hq; f.xs_out = m->hxs; f.bsums_out = m->bsums;
+            if (norm_fused) {
+                f.x = m->x; f.norm_w = L.post_norm; f.eps = c.eps;
+                NC_TRY(launch_i8_fused(st, f, PRO_NORM, EPI_SWIGLU_QUANT));
+            } else {
+                NC_TRY(launch_norm(st, nullptr, m->x, L.post_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
+                NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_SWIGLU_QUANT));
+            }
+            FusedI8Args b{};
+            b.g.out = m->x; b.g.xq = m->hq; b.g.xs = m->hxs; b.g.w = L.wd; b.g.scales = L.sd;
+            b.g.residual = m->x; b.g.m = rows; b.g.n = H; b.g.k = I; b.bsums_in = m->bsums;
+            NC_TRY(launch_i8_fused(st, b, PRO_OFFSET, EPI_RESIDUAL));
         } else {
+            NC_TRY(launch_norm(st, m->normed, m->x, L.post_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
             GemvF32Args a{};
             a.out = m->hbuf; a.x = m->normed; a.w = L.fg; a.w2 = L.fu; a.m = rows; a.n = I; a.k = H;
             NC_TRY(launch_f32(st, a, EPI_SWIGLU, false));
@@ -527,6 +593,9 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     lay.add(&m->xq, R * kmax);
     lay.add(&m->xs, R * (kmax / 32) * 4);
     lay.add(&m->off, R * 4);
+    lay.add(&m->hq, R * I);
+    lay.add(&m->hxs, R * (I / 32) * 4);
+    lay.add(&m->bsums, R * (kmax / 32) * 4);
     lay.add(&m->qkv, R * Nqkv * 4);
     lay.add(&m->ctx, R * Hq * 4);
     lay.add(&m->hbuf, R * I * 4);

@@ -35,6 +35,39 @@ __global__ void gather_kernel(float *__restrict__ out, const int64_t *__restrict
     }
 }
 
+// ---- block quantization of a row held in shared memory --------------------------------------
+// Warp w quantizes blocks w, w + nwarps, ... (nanocompile/quantize.py:102-124), up to 8 of
+// them at once so their divisions overlap; writes xq / xs / block sums and leaves each block's
+// offset term float(sum_b) * scale_b in term[b].
+__device__ __forceinline__ void quantize_row_smem(const float *row, int n, int8_t *xq, float *xs, int32_t *bsums,
+                                                  float *term, int warp, int nwarps, int lane) {
+    const int blocks = n / QBLOCK;
+    for (int b0 = warp; b0 < blocks; b0 += 8 * nwarps) {
+        float v[8], scale[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int b = b0 + u * nwarps;
+            v[u] = b < blocks ? row[b * QBLOCK + lane] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) scale[u] = block_scale(block_magnitude(v[u]));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int b = b0 + u * nwarps;
+            const int8_t qv = quantize_value(v[u], scale[u]);
+            const int bs = __reduce_add_sync(0xffffffffu, (int)qv);
+            if (b < blocks) {
+                xq[b * QBLOCK + lane] = qv;
+                if (lane == 0) {
+                    xs[b] = scale[u];
+                    if (bsums) bsums[b] = bs;
+                    term[b] = fmul((float)bs, scale[u]);
+                }
+            }
+        }
+    }
+}
+
 // ---- rms_norm row kernel + block quantization --------------------------------------------
 // nanocompile/nn.py:34-38 as one row kernel (fusion.py:631-650): acc = acc + x*x over the row
 // in order, then x * (1 / sqrtf(acc / n + eps)) * w; fused with nanocompile/quantize.py:102-124
@@ -42,46 +75,43 @@ __global__ void gather_kernel(float *__restrict__ out, const int64_t *__restrict
 // One CTA per output row; row_map (nullable) picks the input row.
 constexpr int NORM_THREADS = 256;
 
+// The norm of one row held in shared memory: x -> normalized, in place (squares in sq).
+__device__ __forceinline__ void rms_norm_smem(float *x, float *sq, const float *w, int n, float eps, float *s_inv) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sq[i] = fmul(x[i], x[i]);
+    __syncthreads();
+    if (threadIdx.x == 0) *s_inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(chain_sum(sq, n), (float)n), eps)));
+    __syncthreads();
+    const float inv = *s_inv;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = fmul(fmul(x[i], inv), w[i]);
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(NORM_THREADS)
 norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const float *__restrict__ w,
                   int8_t *__restrict__ xq, float *__restrict__ xs, float *__restrict__ offset,
                   int32_t *__restrict__ bsums, const int32_t *__restrict__ row_map, int n, float eps) {
-    extern __shared__ float smem[];
-    float *sq = smem;                          // [n]: squares, then the normalized row
-    float *row = smem + ((n + 3) & ~3);        // [n]
+    extern __shared__ __align__(16) float smem[];
+    const int n4 = (n + 3) & ~3;
+    float *sq = smem;                          // [n]: squares
+    float *row = smem + n4;                    // [n]: the row, then its normalized values
+    float *ws = row + n4;                      // [n]: the gains
     __shared__ float s_inv;
     __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
     const int64_t in_row = row_map ? row_map[b] : b;
     const float *xr = x + in_row * n;
     for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
-        const float v = xr[i];
-        row[i] = v;
-        sq[i] = fmul(v, v);
+        row[i] = xr[i];
+        ws[i] = w[i];
     }
     __syncthreads();
-    if (threadIdx.x == 0) s_inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(chain_sum(sq, n), (float)n), eps)));
-    __syncthreads();
-    const float inv = s_inv;
-    for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
-        const float v = fmul(fmul(row[i], inv), w[i]);
-        if (normed) normed[(int64_t)b * n + i] = v;
-        sq[i] = v;
-    }
+    rms_norm_smem(row, sq, ws, n, eps, &s_inv);
+    if (normed)
+        for (int i = threadIdx.x; i < n; i += NORM_THREADS) normed[(int64_t)b * n + i] = row[i];
     if (!xq) return;
-    __syncthreads();
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = n / QBLOCK;
-    for (int blk = warp; blk < blocks; blk += NORM_THREADS / 32) {
-        int8_t qv;
-        int bs;
-        const float scale = quantize_block_warp(sq[blk * QBLOCK + lane], &qv, &bs);
-        xq[(int64_t)b * n + blk * QBLOCK + lane] = qv;
-        if (lane == 0) {
-            xs[(int64_t)b * blocks + blk] = scale;
-            if (bsums) bsums[(int64_t)b * blocks + blk] = bs;
-            s_term[blk] = fmul((float)bs, scale);
-        }
-    }
+    quantize_row_smem(row, n, xq + (int64_t)b * n, xs + (int64_t)b * blocks, bsums ? bsums + (int64_t)b * blocks : nullptr,
+                      s_term, warp, NORM_THREADS / 32, lane);
     __syncthreads();
     if (threadIdx.x == 0) offset[b] = fmul(chain_sum(s_term, blocks), 128.0f);
 }
@@ -90,20 +120,14 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
 __global__ void __launch_bounds__(NORM_THREADS)
 quantize_kernel(int8_t *__restrict__ xq, const float *__restrict__ x, float *__restrict__ xs,
                 float *__restrict__ offset, int32_t *__restrict__ bsums, int k) {
+    extern __shared__ __align__(16) float qrow[];
     __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = k / QBLOCK;
-    for (int blk = warp; blk < blocks; blk += NORM_THREADS / 32) {
-        int8_t qv;
-        int bs;
-        const float scale = quantize_block_warp(x[(int64_t)b * k + blk * QBLOCK + lane], &qv, &bs);
-        xq[(int64_t)b * k + blk * QBLOCK + lane] = qv;
-        if (lane == 0) {
-            xs[(int64_t)b * blocks + blk] = scale;
-            if (bsums) bsums[(int64_t)b * blocks + blk] = bs;
-            s_term[blk] = fmul((float)bs, scale);
-        }
-    }
+    for (int i = threadIdx.x; i < k; i += NORM_THREADS) qrow[i] = x[(int64_t)b * k + i];
+    __syncthreads();
+    quantize_row_smem(qrow, k, xq + (int64_t)b * k, xs + (int64_t)b * blocks, bsums ? bsums + (int64_t)b * blocks : nullptr,
+                      s_term, warp, NORM_THREADS / 32, lane);
     __syncthreads();
     if (threadIdx.x == 0) offset[b] = fmul(chain_sum(s_term, blocks), 128.0f);
 }
@@ -287,25 +311,49 @@ gemv_i8_kernel(GemvI8Args a) {
     }
 }
 
-// Weights-stationary form: each lane loads its BPL-byte slice of every chunk of its row once,
-// into registers (NCH chunks at most), then walks the tokens.  The weights cross HBM once per
-// step whatever the number of tokens; the activations are re-read from L1.
-template <int LPR, int NCH, int EPI>
-__global__ void __launch_bounds__(128)
-gemv_i8_ws_kernel(GemvI8Args a) {
+// Weights-stationary fused projection.  Each lane loads its BPL-byte slice of every chunk of
+// its row into registers first (NCH chunks at most) -- the weights cross HBM once per step,
+// and their latency overlaps the prologue.  Then per token: the Dp4 chains, the combine, the
+// epilogue.  The activations come from one of three prologues:
+//   PRO_NONE   xq / xs / offset in global memory (written by an earlier kernel);
+//   PRO_NORM   the CTA computes rms_norm + block quantization of x itself (rows <= 4): the
+//              input-norm / post-attention-norm row kernel and calls 2-7, fused in front;
+//   PRO_OFFSET xq / xs / block sums in global memory, the offset (128 * in-order sum over
+//              blocks of sum_b * scale_b) formed here.
+// EPI_SWIGLU_QUANT is silu(gate) * up followed by the block quantization of that output
+// (calls 33-38): the CTA owns whole 32-row blocks and writes xq / xs / block sums.
+enum Prologue : int { PRO_NONE = 0, PRO_NORM = 1, PRO_OFFSET = 2 };
+constexpr int EPI_SWIGLU_QUANT = 4;
+constexpr int PRO_NORM_ROWS = 4;
+
+struct FusedI8Args {
+    GemvI8Args g;
+    const float *x;            // PRO_NORM: the residual stream [m, k]
+    const float *norm_w;       // PRO_NORM: gains [k]
+    float eps;
+    const int32_t *bsums_in;   // PRO_OFFSET: block sums [m, k/32]
+    int8_t *q_out;             // EPI_SWIGLU_QUANT: xq / xs / block sums of the output [m, n]
+    float *xs_out;
+    int32_t *bsums_out;
+};
+
+template <int LPR, int NCH, int PRO, int EPI>
+__global__ void __launch_bounds__(256)
+gemv_i8_fused_kernel(FusedI8Args f) {
     constexpr int BPL = 128 / LPR;
     constexpr int APL = BPL / 4;
-    constexpr bool TWO = EPI == EPI_SWIGLU;
+    constexpr bool TWO = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT;
     constexpr int MAXG = 3;                 // 32-byte groups past the last whole chunk
     using SegT = typename Seg<BPL>::T;
+    const GemvI8Args &a = f.g;
+    extern __shared__ __align__(16) float dsm[];
     __shared__ uint64_t tab[32];
-    if (EPI == EPI_SWIGLU) {
-        if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
-        __syncthreads();
-    }
+    __shared__ float s_inv;
+    const int nwarps = blockDim.x / 32;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int grp = lane / LPR, j = lane % LPR;
-    const int row = (blockIdx.x * (blockDim.x / 32) + warp) * (32 / LPR) + grp;
+    const int row0 = blockIdx.x * nwarps * (32 / LPR);
+    const int row = row0 + warp * (32 / LPR) + grp;
     const bool row_ok = row < a.n;
     const int rowc = row_ok ? row : a.n - 1;
     const int K = a.k, blocks = K / QBLOCK;
@@ -313,6 +361,7 @@ gemv_i8_ws_kernel(GemvI8Args a) {
     const bool tail_lane = j * BPL < 32;
     const uint8_t *wrow = a.w + (int64_t)rowc * K;
     const uint8_t *wrow2 = TWO ? a.w2 + (int64_t)rowc * K : nullptr;
+    if (TWO && threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
 
     uint32_t wv[NCH][APL], wv2[TWO ? NCH : 1][APL], tw[MAXG][APL], tw2[TWO ? MAXG : 1][APL];
 #pragma unroll
@@ -331,9 +380,47 @@ gemv_i8_ws_kernel(GemvI8Args a) {
     }
     const float scale = a.scales[rowc];
     const float scale2 = TWO ? a.scales2[rowc] : 0.0f;
+
+    // ---- prologue: where this kernel's activations come from ----
+    const int8_t *xq_base = a.xq;
+    const float *xs_base = a.xs;
+    const float *off_base = a.offset;
+    if (PRO == PRO_NORM) {
+        // dsm: xrow[k] | sq[k] | gains[k] | term[blocks] | off[rows] | xs[rows][blocks] | xq[rows][k] (bytes)
+        float *xrow = dsm, *sq = xrow + K, *gains = sq + K, *term = gains + K, *offs = term + ((blocks + 3) & ~3);
+        float *xss = offs + PRO_NORM_ROWS;
+        int8_t *xqs = reinterpret_cast<int8_t *>(xss + PRO_NORM_ROWS * blocks);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) gains[i] = f.norm_w[i];
+        for (int m = 0; m < a.m; ++m) {
+            for (int i = threadIdx.x; i < K; i += blockDim.x) xrow[i] = f.x[(int64_t)m * K + i];
+            __syncthreads();
+            rms_norm_smem(xrow, sq, gains, K, f.eps, &s_inv);
+            quantize_row_smem(xrow, K, xqs + m * K, xss + m * blocks, nullptr, term, warp, nwarps, lane);
+            __syncthreads();
+            if (threadIdx.x == 0) offs[m] = fmul(chain_sum(term, blocks), 128.0f);
+            __syncthreads();
+        }
+        xq_base = xqs;
+        xs_base = xss;
+        off_base = offs;
+    } else if (PRO == PRO_OFFSET) {
+        // dsm: term[rows][blocks] | off[rows]
+        const int bl4 = (blocks + 3) & ~3;
+        float *term = dsm, *offs = dsm + a.m * bl4;
+        for (int i = threadIdx.x; i < a.m * blocks; i += blockDim.x) {
+            const int m = i / blocks, b = i % blocks;
+            term[m * bl4 + b] = fmul((float)f.bsums_in[i], a.xs[i]);
+        }
+        __syncthreads();
+        for (int m = threadIdx.x; m < a.m; m += blockDim.x) offs[m] = fmul(chain_sum(term + m * bl4, blocks), 128.0f);
+        __syncthreads();
+        off_base = offs;
+    }
+
+    float *hq = dsm;           // EPI_SWIGLU_QUANT: this CTA's outputs of one token (prologue space reused)
     for (int m = 0; m < a.m; ++m) {
-        const int8_t *xrow = a.xq + (int64_t)m * K;
-        const float *xsr = a.xs + (int64_t)m * blocks;
+        const int8_t *xrow = xq_base + (int64_t)m * K;
+        const float *xsr = xs_base + (int64_t)m * blocks;
         float acc[APL], acc2[APL];
 #pragma unroll
         for (int i = 0; i < APL; ++i) { acc[i] = 0.0f; acc2[i] = 0.0f; }
@@ -367,15 +454,35 @@ gemv_i8_ws_kernel(GemvI8Args a) {
         }
         const float sum = combine_lanes<APL>(acc);
         const float sum2 = TWO ? combine_lanes<APL>(acc2) : 0.0f;
-        if (j == 0 && row_ok) {
-            const float off = a.offset[m];
+        float out = 0.0f;
+        if (j == 0) {
+            const float off = off_base[m];
             const float y = fmul(fsub(sum, off), scale);
-            float out;
-            if (EPI == EPI_BIAS) out = fadd(y, a.bias[row]);
-            else if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)m * a.n + row], y);
-            else if (EPI == EPI_SWIGLU) out = swiglu(y, fmul(fsub(sum2, off), scale2), tab);
+            if (EPI == EPI_BIAS) out = fadd(y, a.bias[rowc]);
+            else if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)m * a.n + rowc], y);
+            else if (TWO) out = swiglu(y, fmul(fsub(sum2, off), scale2), tab);
             else out = y;
-            a.out[(int64_t)m * a.n + row] = out;
+            if (EPI != EPI_SWIGLU_QUANT && row_ok) a.out[(int64_t)m * a.n + row] = out;
+        }
+        if (EPI == EPI_SWIGLU_QUANT) {
+            // the CTA's rows are whole blocks: gather them, then one warp per block
+            const int rows_cta = nwarps * (32 / LPR);
+            __syncthreads();
+            if (j == 0) hq[row - row0] = out;
+            __syncthreads();
+            for (int blk = warp; blk < rows_cta / QBLOCK; blk += nwarps) {
+                const int gb = row0 / QBLOCK + blk;
+                if (gb < a.n / QBLOCK) {
+                    int8_t qv;
+                    int bs;
+                    const float sc = quantize_block_warp(hq[blk * QBLOCK + lane], &qv, &bs);
+                    f.q_out[(int64_t)m * a.n + gb * QBLOCK + lane] = qv;
+                    if (lane == 0) {
+                        f.xs_out[(int64_t)m * (a.n / QBLOCK) + gb] = sc;
+                        f.bsums_out[(int64_t)m * (a.n / QBLOCK) + gb] = bs;
+                    }
+                }
+            }
         }
     }
 }
@@ -585,6 +692,9 @@ struct AttnArgs {
     int heads, kv, d, cap;
     float scale;
     int mode;                  // 0: rope + append + attend (decode); 1: rope + append only; 2: attend only
+    int8_t *q_out;             // nullable: block-quantize ctx (d % 32 == 0) into xq / xs / block sums
+    float *xs_out;
+    int32_t *bsums_out;
 };
 
 constexpr int ATTN_THREADS = 256;
@@ -719,7 +829,25 @@ attention_kernel(AttnArgs a) {
         }
     }
     cp_async_wait<0>();
-    if (t < d) a.ctx[(int64_t)r * a.heads * d + h * d + t] = acc;
+    if (t < d && a.ctx) a.ctx[(int64_t)r * a.heads * d + h * d + t] = acc;
+    if (a.q_out) {
+        // this head's outputs are whole quantization blocks of o_proj's input (calls 18-23)
+        __syncthreads();
+        if (t < d) q[t] = acc;
+        __syncthreads();
+        const int w = t / 32, lane = t % 32, width = a.heads * d;
+        if (w < d / QBLOCK) {
+            int8_t qv;
+            int bs;
+            const float sc = quantize_block_warp(q[w * QBLOCK + lane], &qv, &bs);
+            const int blk = (h * d) / QBLOCK + w;
+            a.q_out[(int64_t)r * width + h * d + w * QBLOCK + lane] = qv;
+            if (lane == 0) {
+                a.xs_out[(int64_t)r * (width / QBLOCK) + blk] = sc;
+                a.bsums_out[(int64_t)r * (width / QBLOCK) + blk] = bs;
+            }
+        }
+    }
 }
 
 // ---- small helpers ---------------------------------------------------------------------------
