@@ -176,6 +176,14 @@ __device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.
     return acc;
 }
 
+// ---- programmatic dependent launch -----------------------------------------------------------
+// Every kernel of a step is launched with programmatic stream serialization: it may start while
+// the previous kernel still runs, loads what does not depend on it (weights, scales, the KV
+// history), and waits here before touching the previous kernel's outputs -- or writing anything.
+// Launched without the attribute, both instructions are no-ops.
+__device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void release_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---- epilogues ----------------------------------------------------------------------------
 enum Epilogue : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3 };
 

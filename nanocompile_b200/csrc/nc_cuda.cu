@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -89,6 +90,32 @@ extern "C" int32_t nc_device_synchronize(void) {
 // ---- kernel launchers (shared by the fused-group ABI and the model) -------------------------
 namespace {
 
+// Every kernel of the step is launched with programmatic stream serialization (PDL): it may
+// begin while its predecessor runs, prefetch immutable data (weights), and wait in-kernel for
+// the predecessor's results.  NC_PDL=0 in the environment turns it off (for A/B timing).
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NC_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 template <typename K>
 cudaError_t allow_smem(K kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return cudaSuccess;
@@ -107,7 +134,7 @@ int32_t launch_norm(cudaStream_t st, float *normed, const float *x, const float 
     if (n > 8192 || (xq && n % QBLOCK)) return fail(NC_ERR_ARGUMENT, "rms_norm width %d unsupported", n);
     const size_t smem = sizeof(float) * 3 * (((size_t)n + 3) / 4 * 4);
     CUDA_TRY(allow_smem(norm_quant_kernel, smem));
-    norm_quant_kernel<<<rows, NORM_THREADS, smem, st>>>(normed, x, w, xq, xs, off, bsums, row_map, n, eps);
+    CUDA_TRY(launch_k(norm_quant_kernel, rows, NORM_THREADS, smem, st, normed, x, w, xq, xs, off, bsums, row_map, n, eps));
     return check_launch("norm_quant_kernel");
 }
 
@@ -115,7 +142,8 @@ int32_t launch_quant(cudaStream_t st, int8_t *xq, const float *x, float *xs, flo
                      int rows, int k) {
     if (rows <= 0) return NC_OK;
     if (k % QBLOCK || k > 8192) return fail(NC_ERR_ARGUMENT, "quantize width %d unsupported", k);
-    quantize_kernel<<<rows, NORM_THREADS, sizeof(float) * k, st>>>(xq, x, xs, off, bsums, k);
+    CUDA_TRY(allow_smem(quantize_kernel, sizeof(float) * k));
+    CUDA_TRY(launch_k(quantize_kernel, rows, NORM_THREADS, sizeof(float) * k, st, xq, x, xs, off, bsums, k));
     return check_launch("quantize_kernel");
 }
 
@@ -124,46 +152,53 @@ int32_t launch_i8_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
     constexpr int WARPS = 4, RPW = 32 / LPR;
     const int grid = (a.n + WARPS * RPW - 1) / (WARPS * RPW);
     switch (epi) {
-        case EPI_NONE: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_NONE><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        case EPI_BIAS: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_BIAS><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        case EPI_RESIDUAL: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_RESIDUAL><<<grid, 32 * WARPS, 0, st>>>(a); break;
-        case EPI_SWIGLU: gemv_i8_kernel<LPR, TOK, UNROLL, EPI_SWIGLU><<<grid, 32 * WARPS, 0, st>>>(a); break;
+        case EPI_NONE: CUDA_TRY(launch_k(gemv_i8_kernel<LPR, TOK, UNROLL, EPI_NONE>, grid, 32 * WARPS, 0, st, a)); break;
+        case EPI_BIAS: CUDA_TRY(launch_k(gemv_i8_kernel<LPR, TOK, UNROLL, EPI_BIAS>, grid, 32 * WARPS, 0, st, a)); break;
+        case EPI_RESIDUAL: CUDA_TRY(launch_k(gemv_i8_kernel<LPR, TOK, UNROLL, EPI_RESIDUAL>, grid, 32 * WARPS, 0, st, a)); break;
+        case EPI_SWIGLU: CUDA_TRY(launch_k(gemv_i8_kernel<LPR, TOK, UNROLL, EPI_SWIGLU>, grid, 32 * WARPS, 0, st, a)); break;
         default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
     }
     return check_launch("gemv_i8_kernel");
 }
 
-template <int LPR, int NCH, int PRO, int EPI>
+template <int LPR, int NCH, int MAXG, int PRO, int EPI>
 int32_t launch_fused_t(cudaStream_t st, const FusedI8Args &f, size_t smem) {
     constexpr int THREADS = 256, ROWS = (THREADS / 32) * (32 / LPR);
-    auto kernel = gemv_i8_fused_kernel<LPR, NCH, PRO, EPI>;
+    auto kernel = gemv_i8_fused_kernel<LPR, NCH, MAXG, PRO, EPI>;
     CUDA_TRY(allow_smem(kernel, smem));
-    kernel<<<(f.g.n + ROWS - 1) / ROWS, THREADS, smem, st>>>(f);
+    CUDA_TRY(launch_k(kernel, (f.g.n + ROWS - 1) / ROWS, THREADS, smem, st, f));
     return check_launch("gemv_i8_fused_kernel");
 }
 
-template <int LPR, int NCH, int PRO>
+template <int LPR, int NCH, int MAXG, int PRO>
 int32_t launch_fused_epi(cudaStream_t st, const FusedI8Args &f, int epi, size_t smem) {
     switch (epi) {
-        case EPI_NONE: return launch_fused_t<LPR, NCH, PRO, EPI_NONE>(st, f, smem);
-        case EPI_BIAS: return launch_fused_t<LPR, NCH, PRO, EPI_BIAS>(st, f, smem);
-        case EPI_RESIDUAL: return launch_fused_t<LPR, NCH, PRO, EPI_RESIDUAL>(st, f, smem);
-        case EPI_SWIGLU: return launch_fused_t<LPR, NCH, PRO, EPI_SWIGLU>(st, f, smem);
-        case EPI_SWIGLU_QUANT: return launch_fused_t<LPR, NCH, PRO, EPI_SWIGLU_QUANT>(st, f, smem);
+        case EPI_NONE: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_NONE>(st, f, smem);
+        case EPI_BIAS: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_BIAS>(st, f, smem);
+        case EPI_RESIDUAL: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_RESIDUAL>(st, f, smem);
+        case EPI_SWIGLU: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_SWIGLU>(st, f, smem);
+        case EPI_SWIGLU_QUANT: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_SWIGLU_QUANT>(st, f, smem);
         default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
     }
 }
 
-template <int LPR, int NCH>
-int32_t launch_fused_pro(cudaStream_t st, const FusedI8Args &f, int pro, int epi, size_t smem) {
+template <int LPR, int NCH, int MAXG>
+int32_t launch_fused_pro_g(cudaStream_t st, const FusedI8Args &f, int pro, int epi, size_t smem) {
     switch (pro) {
-        case PRO_NONE: return launch_fused_epi<LPR, NCH, PRO_NONE>(st, f, epi, smem);
-        case PRO_OFFSET: return launch_fused_epi<LPR, NCH, PRO_OFFSET>(st, f, epi, smem);
+        case PRO_NONE: return launch_fused_epi<LPR, NCH, MAXG, PRO_NONE>(st, f, epi, smem);
+        case PRO_OFFSET: return launch_fused_epi<LPR, NCH, MAXG, PRO_OFFSET>(st, f, epi, smem);
         case PRO_NORM:
-            if constexpr (NCH <= 8) return launch_fused_epi<LPR, NCH, PRO_NORM>(st, f, epi, smem);
+            if constexpr (NCH <= 8) return launch_fused_epi<LPR, NCH, MAXG, PRO_NORM>(st, f, epi, smem);
             return fail(NC_ERR_ARGUMENT, "the norm prologue takes widths up to 1024");
         default: return fail(NC_ERR_ARGUMENT, "unknown prologue %d", pro);
     }
+}
+
+// Widths that are whole 128-byte chunks (the model's) use the variant without tail registers.
+template <int LPR, int NCH>
+int32_t launch_fused_pro(cudaStream_t st, const FusedI8Args &f, int pro, int epi, size_t smem) {
+    if (f.g.k % CHUNK == 0) return launch_fused_pro_g<LPR, NCH, 0>(st, f, pro, epi, smem);
+    return launch_fused_pro_g<LPR, NCH, 3>(st, f, pro, epi, smem);
 }
 
 // The int8-vnni projection: weights-stationary, lanes per row chosen by shape (a row's slices
@@ -175,11 +210,13 @@ int32_t launch_i8_fused(cudaStream_t st, const FusedI8Args &f, int pro, int epi)
     if (pro == PRO_NORM && a.m > PRO_NORM_ROWS) return fail(NC_ERR_ARGUMENT, "the norm prologue takes up to 4 rows");
     if (epi == EPI_SWIGLU_QUANT && a.n % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized output width %d", a.n);
     const int blocks = a.k / QBLOCK, bl4 = (blocks + 3) & ~3, chunks = a.k / CHUNK;
-    size_t smem = 32 * sizeof(float);
-    if (pro == PRO_NORM)
-        smem = std::max(smem, sizeof(float) * (4 * (size_t)a.k + bl4 + 4 + 4 * (size_t)blocks) + 4 * (size_t)a.k);
-    if (pro == PRO_OFFSET) smem = std::max(smem, sizeof(float) * ((size_t)a.m * bl4 + a.m));
-    if (smem > 200 * 1024) return fail(NC_ERR_ARGUMENT, "projection prologue needs too much shared memory");
+    if (a.k % 16) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a multiple of 16", a.k);
+    const int tile = pro == PRO_NORM ? PRO_NORM_ROWS : std::min(a.m, act_tile_tokens(a.k));
+    if (tile < 1) return fail(NC_ERR_ARGUMENT, "int8 width %d too wide for the activation tile", a.k);
+    size_t smem = (size_t)tile * a.k + sizeof(float) * ((size_t)tile * bl4 + ((a.m + 3) & ~3));
+    if (pro == PRO_NORM) smem += sizeof(float) * ((size_t)bl4 + 3 * (size_t)a.k);
+    if (pro == PRO_OFFSET) smem += sizeof(float) * (size_t)a.m * bl4;
+    if (smem > 200 * 1024) return fail(NC_ERR_ARGUMENT, "projection needs too much shared memory");
     if (chunks <= 8) {
         if (a.n <= 2048 && epi != EPI_SWIGLU_QUANT) return launch_fused_pro<16, 8>(st, f, pro, epi, smem);
         return launch_fused_pro<8, 8>(st, f, pro, epi, smem);
@@ -203,7 +240,7 @@ int32_t launch_f32_t(cudaStream_t st, const GemvF32Args &a) {
     auto kernel = gemv_f32_kernel<TOK, EPI, ARGMAX>;
     CUDA_TRY(allow_smem(kernel, smem));
     const int grid = (a.n + F32_ROWS - 1) / F32_ROWS;
-    kernel<<<grid, F32_ROWS, smem, st>>>(a);
+    CUDA_TRY(launch_k(kernel, grid, F32_ROWS, smem, st, a));
     return check_launch("gemv_f32_kernel");
 }
 
@@ -236,7 +273,7 @@ int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
     const size_t smem = attention_smem(a.d, a.cap);
     if (smem > 220 * 1024) return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
     CUDA_TRY(allow_smem(attention_kernel, smem));
-    attention_kernel<<<rows * a.heads, ATTN_THREADS, smem, st>>>(a);
+    CUDA_TRY(launch_k(attention_kernel, rows * a.heads, ATTN_THREADS, smem, st, a));
     return check_launch("attention_kernel");
 }
 
@@ -254,8 +291,8 @@ float f32_from_bits(int64_t bits) {
 extern "C" int32_t nc_gather_rows(void **p, const int64_t *s, void *stream) {
     const int rows = (int)s[0];
     if (rows <= 0) return NC_OK;
-    gather_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>((float *)p[0], (const int64_t *)p[1], (const float *)p[2],
-                                                          (unsigned long long *)p[3], s[1], (int)s[2]);
+    CUDA_TRY(launch_k(gather_kernel, rows, 256, 0, (cudaStream_t)stream, (float *)p[0], (const int64_t *)p[1],
+                      (const float *)p[2], (unsigned long long *)p[3], s[1], (int)s[2]));
     return check_launch("gather_kernel");
 }
 
@@ -439,8 +476,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
     const bool norm_fused = rows <= PRO_NORM_ROWS && H <= 8 * CHUNK;
     const bool attn_quant = q8 && d % QBLOCK == 0;
 
-    CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
-    gather_kernel<<<rows, 256, 0, st>>>(m->x, m->ids, m->embed, m->err, c.vocab, H);
+    CUDA_TRY(launch_k(gather_kernel, rows, 256, 0, st, m->x, m->ids, m->embed, m->err, c.vocab, H));
     NC_TRY(check_launch("gather_kernel"));
 
     for (int l = 0; l < (int)c.layers; ++l) {
@@ -798,6 +834,7 @@ extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, 
     CUDA_TRY(cudaMemcpyAsync(m->slot, slot, rows * 4, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemcpyAsync(m->pos, pos, rows * 4, cudaMemcpyHostToDevice, st));
     if (logit_rows) CUDA_TRY(cudaMemcpyAsync(m->logit_row, logit_row, logit_rows * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
     NC_TRY(enqueue_step(m, rows, logit_rows, fused));
     unsigned long long err = 0;
     CUDA_TRY(cudaMemcpyAsync(&err, m->err, 8, cudaMemcpyDeviceToHost, st));
@@ -823,7 +860,9 @@ static int32_t decode_graph(nc_model *m, int batch, cudaGraphExec_t *out) {
     CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int32_t s = enqueue_step(m, batch, batch, true);
     if (s == NC_OK) {
-        advance_kernel<<<1, 1024, 0, m->stream>>>(m->ids, m->pos, m->tokens, m->history, m->step, batch);
+        if (launch_k(advance_kernel, 1, 1024, 0, m->stream, m->ids, m->pos, m->tokens, m->history, m->step, batch) !=
+            cudaSuccess)
+            s = fail(NC_ERR_CUDA, "launching advance_kernel");
         s = check_launch("advance_kernel");
     }
     cudaError_t e = cudaStreamEndCapture(m->stream, &graph);

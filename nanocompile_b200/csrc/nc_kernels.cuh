@@ -17,6 +17,8 @@ namespace nc {
 __global__ void gather_kernel(float *__restrict__ out, const int64_t *__restrict__ ids,
                               const float *__restrict__ table, unsigned long long *err,
                               int64_t vocab, int hidden) {
+    release_dependents();
+    wait_for_producer();
     const int r = blockIdx.x;
     const int64_t id = ids[r];
     float *dst = out + (int64_t)r * hidden;
@@ -98,12 +100,12 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
     __shared__ float s_inv;
     __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
+    release_dependents();
+    for (int i = threadIdx.x; i < n; i += NORM_THREADS) ws[i] = w[i];
+    wait_for_producer();
     const int64_t in_row = row_map ? row_map[b] : b;
     const float *xr = x + in_row * n;
-    for (int i = threadIdx.x; i < n; i += NORM_THREADS) {
-        row[i] = xr[i];
-        ws[i] = w[i];
-    }
+    for (int i = threadIdx.x; i < n; i += NORM_THREADS) row[i] = xr[i];
     __syncthreads();
     rms_norm_smem(row, sq, ws, n, eps, &s_inv);
     if (normed)
@@ -124,6 +126,8 @@ quantize_kernel(int8_t *__restrict__ xq, const float *__restrict__ x, float *__r
     __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = k / QBLOCK;
+    release_dependents();
+    wait_for_producer();
     for (int i = threadIdx.x; i < k; i += NORM_THREADS) qrow[i] = x[(int64_t)b * k + i];
     __syncthreads();
     quantize_row_smem(qrow, k, xq + (int64_t)b * k, xs + (int64_t)b * blocks, bsums ? bsums + (int64_t)b * blocks : nullptr,
@@ -205,6 +209,8 @@ gemv_i8_kernel(GemvI8Args a) {
     constexpr bool TWO = EPI == EPI_SWIGLU;
     using SegT = typename Seg<BPL>::T;
     __shared__ uint64_t tab[32];
+    release_dependents();
+    wait_for_producer();
     if (EPI == EPI_SWIGLU) {
         if (threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
         __syncthreads();
@@ -337,18 +343,25 @@ struct FusedI8Args {
     int32_t *bsums_out;
 };
 
-template <int LPR, int NCH, int PRO, int EPI>
-__global__ void __launch_bounds__(256)
+// Shared-memory budget for the activations of one token tile (xq rows + their block scales).
+constexpr int ACT_TILE_BYTES = 64 * 1024;
+
+__host__ __device__ inline int act_tile_tokens(int k) { return ACT_TILE_BYTES / (k + 4 * (k / QBLOCK)); }
+
+template <int LPR, int NCH, int MAXG, int PRO, int EPI>
+__global__ void __launch_bounds__(256, (EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT) ? 2 : 1)
 gemv_i8_fused_kernel(FusedI8Args f) {
+    // MAXG: 32-byte groups past the last whole chunk (0 when the width is whole chunks)
     constexpr int BPL = 128 / LPR;
     constexpr int APL = BPL / 4;
     constexpr bool TWO = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT;
-    constexpr int MAXG = 3;                 // 32-byte groups past the last whole chunk
+    constexpr bool XPRE = !TWO;             // activations of all chunks into registers first
     using SegT = typename Seg<BPL>::T;
     const GemvI8Args &a = f.g;
     extern __shared__ __align__(16) float dsm[];
     __shared__ uint64_t tab[32];
     __shared__ float s_inv;
+    __shared__ float hq[32 * 8];
     const int nwarps = blockDim.x / 32;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int grp = lane / LPR, j = lane % LPR;
@@ -356,14 +369,16 @@ gemv_i8_fused_kernel(FusedI8Args f) {
     const int row = row0 + warp * (32 / LPR) + grp;
     const bool row_ok = row < a.n;
     const int rowc = row_ok ? row : a.n - 1;
-    const int K = a.k, blocks = K / QBLOCK;
+    const int K = a.k, blocks = K / QBLOCK, bl4 = (blocks + 3) & ~3;
     const int chunks = K / CHUNK, stride = chunks * CHUNK, groups = (K % CHUNK) / 32;
     const bool tail_lane = j * BPL < 32;
     const uint8_t *wrow = a.w + (int64_t)rowc * K;
     const uint8_t *wrow2 = TWO ? a.w2 + (int64_t)rowc * K : nullptr;
     if (TWO && threadIdx.x < 32) tab[threadIdx.x] = kExpTab[threadIdx.x];
 
-    uint32_t wv[NCH][APL], wv2[TWO ? NCH : 1][APL], tw[MAXG][APL], tw2[TWO ? MAXG : 1][APL];
+    // ---- what does not depend on the previous kernel: this row's weights and constants ----
+    release_dependents();
+    uint32_t wv[NCH][APL], wv2[TWO ? NCH : 1][APL], tw[MAXG ? MAXG : 1][APL], tw2[TWO && MAXG ? MAXG : 1][APL];
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
         if (c < chunks) {
@@ -380,108 +395,140 @@ gemv_i8_fused_kernel(FusedI8Args f) {
     }
     const float scale = a.scales[rowc];
     const float scale2 = TWO ? a.scales2[rowc] : 0.0f;
+    const float bias = EPI == EPI_BIAS ? a.bias[rowc] : 0.0f;
 
-    // ---- prologue: where this kernel's activations come from ----
-    const int8_t *xq_base = a.xq;
-    const float *xs_base = a.xs;
-    const float *off_base = a.offset;
-    if (PRO == PRO_NORM) {
-        // dsm: xrow[k] | sq[k] | gains[k] | term[blocks] | off[rows] | xs[rows][blocks] | xq[rows][k] (bytes)
-        float *xrow = dsm, *sq = xrow + K, *gains = sq + K, *term = gains + K, *offs = term + ((blocks + 3) & ~3);
-        float *xss = offs + PRO_NORM_ROWS;
-        int8_t *xqs = reinterpret_cast<int8_t *>(xss + PRO_NORM_ROWS * blocks);
+    // dsm layout: [activation tile: xq rows | xs rows] [prologue scratch]
+    const int tile_tokens = PRO == PRO_NORM ? PRO_NORM_ROWS : min(a.m, act_tile_tokens(K));
+    int8_t *xq_t = reinterpret_cast<int8_t *>(dsm);
+    float *xs_t = dsm + tile_tokens * K / 4;
+    float *scratch = xs_t + tile_tokens * bl4;
+    float *offs = scratch;                       // [m]
+    float *term = offs + ((a.m + 3) & ~3);       // PRO_OFFSET: [m][bl4]; PRO_NORM: [bl4]
+    float *xrow = term + bl4, *sq = xrow + K, *gains = sq + K;   // PRO_NORM only
+    if (PRO == PRO_NORM)
         for (int i = threadIdx.x; i < K; i += blockDim.x) gains[i] = f.norm_w[i];
+
+    wait_for_producer();
+
+    // ---- prologue: the offsets (and for PRO_NORM the whole quantized activations) ----
+    if (PRO == PRO_NORM) {
         for (int m = 0; m < a.m; ++m) {
             for (int i = threadIdx.x; i < K; i += blockDim.x) xrow[i] = f.x[(int64_t)m * K + i];
             __syncthreads();
             rms_norm_smem(xrow, sq, gains, K, f.eps, &s_inv);
-            quantize_row_smem(xrow, K, xqs + m * K, xss + m * blocks, nullptr, term, warp, nwarps, lane);
+            quantize_row_smem(xrow, K, xq_t + m * K, xs_t + m * bl4, nullptr, term, warp, nwarps, lane);
             __syncthreads();
             if (threadIdx.x == 0) offs[m] = fmul(chain_sum(term, blocks), 128.0f);
             __syncthreads();
         }
-        xq_base = xqs;
-        xs_base = xss;
-        off_base = offs;
     } else if (PRO == PRO_OFFSET) {
-        // dsm: term[rows][blocks] | off[rows]
-        const int bl4 = (blocks + 3) & ~3;
-        float *term = dsm, *offs = dsm + a.m * bl4;
         for (int i = threadIdx.x; i < a.m * blocks; i += blockDim.x) {
             const int m = i / blocks, b = i % blocks;
             term[m * bl4 + b] = fmul((float)f.bsums_in[i], a.xs[i]);
         }
         __syncthreads();
         for (int m = threadIdx.x; m < a.m; m += blockDim.x) offs[m] = fmul(chain_sum(term + m * bl4, blocks), 128.0f);
-        __syncthreads();
-        off_base = offs;
+    } else {
+        for (int m = threadIdx.x; m < a.m; m += blockDim.x) offs[m] = a.offset[m];
     }
 
-    float *hq = dsm;           // EPI_SWIGLU_QUANT: this CTA's outputs of one token (prologue space reused)
-    for (int m = 0; m < a.m; ++m) {
-        const int8_t *xrow = xq_base + (int64_t)m * K;
-        const float *xsr = xs_base + (int64_t)m * blocks;
-        float acc[APL], acc2[APL];
-#pragma unroll
-        for (int i = 0; i < APL; ++i) { acc[i] = 0.0f; acc2[i] = 0.0f; }
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-            if (c < chunks) {
-                const int off = c * CHUNK + j * BPL;
-                uint32_t xv[APL];
-                Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow + off), xv);
-                const float s = xsr[off / QBLOCK];
-#pragma unroll
-                for (int i = 0; i < APL; ++i) {
-                    acc[i] = __fmaf_rn(dp4_lane(wv[c][i], xv[i]), s, acc[i]);
-                    if (TWO) acc2[i] = __fmaf_rn(dp4_lane(wv2[c][i], xv[i]), s, acc2[i]);
-                }
-            }
-        }
-#pragma unroll
-        for (int k1 = 0; k1 < MAXG; ++k1) {
-            if (k1 < groups && tail_lane) {
-                const int off = stride + k1 * 32 + j * BPL;
-                uint32_t xv[APL];
-                Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow + off), xv);
-                const float s = xsr[off / QBLOCK];
-#pragma unroll
-                for (int i = 0; i < APL; ++i) {
-                    acc[i] = __fmaf_rn(dp4_lane(tw[k1][i], xv[i]), s, acc[i]);
-                    if (TWO) acc2[i] = __fmaf_rn(dp4_lane(tw2[k1][i], xv[i]), s, acc2[i]);
-                }
-            }
-        }
-        const float sum = combine_lanes<APL>(acc);
-        const float sum2 = TWO ? combine_lanes<APL>(acc2) : 0.0f;
-        float out = 0.0f;
-        if (j == 0) {
-            const float off = off_base[m];
-            const float y = fmul(fsub(sum, off), scale);
-            if (EPI == EPI_BIAS) out = fadd(y, a.bias[rowc]);
-            else if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)m * a.n + rowc], y);
-            else if (TWO) out = swiglu(y, fmul(fsub(sum2, off), scale2), tab);
-            else out = y;
-            if (EPI != EPI_SWIGLU_QUANT && row_ok) a.out[(int64_t)m * a.n + row] = out;
-        }
-        if (EPI == EPI_SWIGLU_QUANT) {
-            // the CTA's rows are whole blocks: gather them, then one warp per block
-            const int rows_cta = nwarps * (32 / LPR);
+    for (int t0 = 0; t0 < a.m; t0 += tile_tokens) {
+        const int tn = min(tile_tokens, a.m - t0);
+        if (PRO != PRO_NORM) {
+            // stage this tile's activations: xq rows (16-byte pieces) and block scales
             __syncthreads();
-            if (j == 0) hq[row - row0] = out;
-            __syncthreads();
-            for (int blk = warp; blk < rows_cta / QBLOCK; blk += nwarps) {
-                const int gb = row0 / QBLOCK + blk;
-                if (gb < a.n / QBLOCK) {
-                    int8_t qv;
-                    int bs;
-                    const float sc = quantize_block_warp(hq[blk * QBLOCK + lane], &qv, &bs);
-                    f.q_out[(int64_t)m * a.n + gb * QBLOCK + lane] = qv;
-                    if (lane == 0) {
-                        f.xs_out[(int64_t)m * (a.n / QBLOCK) + gb] = sc;
-                        f.bsums_out[(int64_t)m * (a.n / QBLOCK) + gb] = bs;
+            const int pieces = tn * K / 16;
+            for (int i = threadIdx.x; i < pieces; i += blockDim.x)
+                reinterpret_cast<uint4 *>(xq_t)[i] = reinterpret_cast<const uint4 *>(a.xq + (int64_t)t0 * K)[i];
+            for (int i = threadIdx.x; i < tn * blocks; i += blockDim.x)
+                xs_t[(i / blocks) * bl4 + i % blocks] = a.xs[(int64_t)t0 * blocks + i];
+        }
+        __syncthreads();
+        for (int tm = 0; tm < tn; ++tm) {
+            const int m = t0 + tm;
+            const int8_t *xrow_q = xq_t + tm * K;
+            const float *xsr = xs_t + tm * bl4;
+            uint32_t xv[XPRE ? NCH : 1][APL];
+            float sv[XPRE ? NCH : 1];
+            if (XPRE) {
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    if (c < chunks) {
+                        const int off = c * CHUNK + j * BPL;
+                        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow_q + off), xv[c]);
+                        sv[c] = xsr[off / QBLOCK];
                     }
                 }
+            }
+            float acc[APL], acc2[APL];
+#pragma unroll
+            for (int i = 0; i < APL; ++i) { acc[i] = 0.0f; acc2[i] = 0.0f; }
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                if (c < chunks) {
+                    uint32_t xc[APL];
+                    float sc;
+                    if (XPRE) {
+#pragma unroll
+                        for (int i = 0; i < APL; ++i) xc[i] = xv[XPRE ? c : 0][i];
+                        sc = sv[XPRE ? c : 0];
+                    } else {
+                        const int off = c * CHUNK + j * BPL;
+                        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow_q + off), xc);
+                        sc = xsr[off / QBLOCK];
+                    }
+#pragma unroll
+                    for (int i = 0; i < APL; ++i) {
+                        acc[i] = __fmaf_rn(dp4_lane(wv[c][i], xc[i]), sc, acc[i]);
+                        if (TWO) acc2[i] = __fmaf_rn(dp4_lane(wv2[c][i], xc[i]), sc, acc2[i]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k1 = 0; k1 < MAXG; ++k1) {
+                if (k1 < groups && tail_lane) {
+                    const int off = stride + k1 * 32 + j * BPL;
+                    uint32_t tx[APL];
+                    Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow_q + off), tx);
+                    const float s = xsr[off / QBLOCK];
+#pragma unroll
+                    for (int i = 0; i < APL; ++i) {
+                        acc[i] = __fmaf_rn(dp4_lane(tw[MAXG ? k1 : 0][i], tx[i]), s, acc[i]);
+                        if (TWO) acc2[i] = __fmaf_rn(dp4_lane(tw2[TWO && MAXG ? k1 : 0][i], tx[i]), s, acc2[i]);
+                    }
+                }
+            }
+            const float sum = combine_lanes<APL>(acc);
+            const float sum2 = TWO ? combine_lanes<APL>(acc2) : 0.0f;
+            float out = 0.0f;
+            if (j == 0) {
+                const float off = offs[m];
+                const float y = fmul(fsub(sum, off), scale);
+                if (EPI == EPI_BIAS) out = fadd(y, bias);
+                else if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)m * a.n + rowc], y);
+                else if (TWO) out = swiglu(y, fmul(fsub(sum2, off), scale2), tab);
+                else out = y;
+                if (EPI != EPI_SWIGLU_QUANT && row_ok) a.out[(int64_t)m * a.n + row] = out;
+            }
+            if (EPI == EPI_SWIGLU_QUANT) {
+                // the CTA's rows are whole blocks: gather them, then one warp per block
+                const int rows_cta = nwarps * (32 / LPR);
+                if (j == 0) hq[row - row0] = out;
+                __syncthreads();
+                for (int blk = warp; blk < rows_cta / QBLOCK; blk += nwarps) {
+                    const int gb = row0 / QBLOCK + blk;
+                    if (gb < a.n / QBLOCK) {
+                        int8_t qv;
+                        int bs;
+                        const float sc = quantize_block_warp(hq[blk * QBLOCK + lane], &qv, &bs);
+                        f.q_out[(int64_t)m * a.n + gb * QBLOCK + lane] = qv;
+                        if (lane == 0) {
+                            f.xs_out[(int64_t)m * (a.n / QBLOCK) + gb] = sc;
+                            f.bsums_out[(int64_t)m * (a.n / QBLOCK) + gb] = bs;
+                        }
+                    }
+                }
+                __syncthreads();
             }
         }
     }
@@ -543,7 +590,7 @@ gemv_f32_kernel(GemvF32Args a) {
     const int row = row0 + t;
     const int K = a.k, tiles = K / F32_TILE;
 
-    auto load_tile = [&](int stage, int kt, int m0) {
+    auto load_w = [&](int stage, int kt) {
         float4 *st = smem4 + stage * STAGE_F4;
 #pragma unroll
         for (int p = 0; p < NW * W_PIECES / F32_ROWS; ++p) {
@@ -554,6 +601,9 @@ gemv_f32_kernel(GemvF32Args a) {
             const float *src = (which ? a.w2 : a.w) + (int64_t)gr * K + kt * F32_TILE + s * 4;
             cp_async16(st + which * W_PIECES + r * 8 + (s ^ (r & 7)), src);
         }
+    };
+    auto load_x = [&](int stage, int kt, int m0) {
+        float4 *st = smem4 + stage * STAGE_F4;
         if (t < TOK * 8) {
             const int mm = t / 8, s = t % 8;
             const int m = min(m0 + mm, a.m - 1);
@@ -561,6 +611,18 @@ gemv_f32_kernel(GemvF32Args a) {
             cp_async16(st + NW * W_PIECES + mm * 8 + s, a.x + xr * K + kt * F32_TILE + s * 4);
         }
     };
+    auto load_tile = [&](int stage, int kt, int m0) {
+        load_w(stage, kt);
+        load_x(stage, kt, m0);
+    };
+
+    // the weights of the first tiles do not depend on the previous kernel: issue them first
+    release_dependents();
+#pragma unroll
+    for (int s = 0; s < F32_STAGES - 1; ++s)
+        if (s < tiles) load_w(s, s);
+    wait_for_producer();
+    bool prefetched = true;
 
     for (int m0 = 0; m0 < a.m; m0 += TOK) {
         float acc[TOK], acc2[TWO ? TOK : 1];
@@ -571,9 +633,13 @@ gemv_f32_kernel(GemvF32Args a) {
         }
 #pragma unroll
         for (int s = 0; s < F32_STAGES - 1; ++s) {
-            if (s < tiles) load_tile(s, s, m0);
+            if (s < tiles) {
+                if (!prefetched) load_w(s, s);
+                load_x(s, s, m0);
+            }
             cp_async_commit();
         }
+        prefetched = false;
         for (int kt = 0; kt < tiles; ++kt) {
             cp_async_wait<F32_STAGES - 2>();
             __syncthreads();
@@ -704,6 +770,8 @@ constexpr int ATTN_VSTAGES = 4;
 __global__ void __launch_bounds__(ATTN_THREADS)
 attention_kernel(AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
+    release_dependents();
+    wait_for_producer();
     const int d = a.d, half = d / 2, group = a.heads / a.kv;
     const int r = blockIdx.x / a.heads, h = blockIdx.x % a.heads, g = h / group;
     const int pos = a.pos[r], len = pos + 1;
@@ -868,6 +936,8 @@ __global__ void expf_kernel(float *out, const float *x, int64_t n) {
 // is appended to the device-side history.
 __global__ void advance_kernel(int64_t *ids, int32_t *pos, const int64_t *tokens, int64_t *history,
                                int32_t *step, int rows) {
+    release_dependents();
+    wait_for_producer();
     const int r = threadIdx.x;
     const int s = *step;
     if (r < rows) {
