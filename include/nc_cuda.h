@@ -54,7 +54,8 @@ int32_t nc_device_synchronize(void);
 
 /* gather (nanocompile/fusion.py:713-731, call 0): rows of the embedding table by token id.
  * p: [0] out f32[rows, hidden]  [1] ids i64[rows]  [2] table f32[vocab, hidden]
- *    [3] error word i64[2] (device; [0] = 1 + first bad row, [1] = its id; zero it first)
+ *    [3] error word u64 (device; set every byte to 0xff before the call; after it, the
+ *        smallest row whose id was out of range, or still all ones)
  * s: rows, vocab, hidden */
 int32_t nc_gather_rows(void **p, const int64_t *s, void *stream);
 
@@ -117,6 +118,10 @@ int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t b
 /* glibc's expf, bit for bit, evaluated on the device (test hook for the softmax / SiLU math).
  * p: [0] out f32[n]  [1] x f32[n];  s: n */
 int32_t nc_expf_exact(void **p, const int64_t *s, void *stream);
+
+/* The block scale mag / 127 is computed by a branch-free correctly rounded division; this runs
+ * it against the IEEE divide on every non-negative float and reports the differences (0). */
+int32_t nc_selfcheck_div127(int64_t *mismatches);
 
 /* ---- 2. the model runtime ---------------------------------------------------------------- */
 

@@ -120,9 +120,27 @@ __device__ __forceinline__ float swiglu(float g, float u, const uint64_t *tab) {
 __device__ __forceinline__ float block_magnitude(float v) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu));
 }
-__device__ __forceinline__ float block_scale(float mag) { return (mag <= 0.0f) ? 1.0f : fdiv(mag, 127.0f); }
+// mag / 127 correctly rounded, without the IEEE divide's branchy slow path: q0 = mag * y with
+// y = RN(1/127), then one remainder correction r = mag - q0 * 127 (exact, by FMA), q = q0 + r * y
+// (the correction step of Markstein's FMA division).  Checked equal to IEEE division for every
+// non-negative float by nc_selfcheck_div127; non-finite and tiny magnitudes take the IEEE divide.
+__device__ __forceinline__ float div127(float mag) {
+    const float y = 0x1.020408p-7f;                      // RN(1/127)
+    if (!(mag < 0x1p+120f) || mag < 0x1p-100f) return fdiv(mag, 127.0f);
+    const float q0 = fmul(mag, y);
+    const float r = __fmaf_rn(-q0, 127.0f, mag);
+    return __fmaf_rn(r, y, q0);
+}
+__device__ __forceinline__ float block_scale(float mag) { return (mag <= 0.0f) ? 1.0f : div127(mag); }
+// xq = (int8)clamp(roundf(v / scale), -127, 127).  Only the rounded integer is kept, so the
+// quotient may come from the fast approximate divide (error <= 2 ulp, |v / scale| <= 128): the
+// rounding can only differ from IEEE division's when the quotient is within 2 ulp of a
+// half-integer, and every quotient within 1/512 of one is recomputed with the IEEE divide.
 __device__ __forceinline__ int8_t quantize_value(float v, float scale) {
-    float t = roundf(fdiv(v, scale));
+    float t = __fdividef(v, scale);
+    const float a = fabsf(t);
+    if (!(a < 256.0f) || !(scale >= 0x1p-100f) || fabsf(a - floorf(a) - 0.5f) < (1.0f / 512)) t = fdiv(v, scale);
+    t = roundf(t);
     t = (t <= 127.0f) ? t : 127.0f;
     t = (-127.0f <= t) ? t : -127.0f;
     return (int8_t)t;

@@ -263,18 +263,39 @@ int32_t launch_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) 
     return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<16>(st, a, epi, argmax);
 }
 
-size_t attention_smem(int d, int cap) {
-    return sizeof(float) * ((size_t)ATTN_VSTAGES * ATTN_VCHUNK * d + ((size_t)cap + 3) / 4 * 4 + 3 * (size_t)d);
+size_t attention_smem(int group, int d, int cap) {
+    switch (d) {
+        case 16: return sizeof(float) * attention_smem_floats<16>(group, cap);
+        case 64: return sizeof(float) * attention_smem_floats<64>(group, cap);
+        case 128: return sizeof(float) * attention_smem_floats<128>(group, cap);
+        default: return (size_t)1 << 40;
+    }
+}
+
+template <int D>
+int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows) {
+    const int group = a.heads / a.kv;
+    const size_t smem = sizeof(float) * attention_smem_floats<D>(group, a.cap);
+    CUDA_TRY(allow_smem(attention_kernel<D>, smem));
+    CUDA_TRY(launch_k(attention_kernel<D>, rows * a.kv, ATTN_THREADS, smem, st, a));
+    return check_launch("attention_kernel");
 }
 
 int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
     if (rows <= 0) return NC_OK;
-    if (a.heads % a.kv || a.d % 4 || a.d > ATTN_THREADS) return fail(NC_ERR_ARGUMENT, "attention shape unsupported");
-    const size_t smem = attention_smem(a.d, a.cap);
-    if (smem > 220 * 1024) return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
-    CUDA_TRY(allow_smem(attention_kernel, smem));
-    CUDA_TRY(launch_k(attention_kernel, rows * a.heads, ATTN_THREADS, smem, st, a));
-    return check_launch("attention_kernel");
+    const int group = a.heads / a.kv;
+    if (a.heads % a.kv || group > ATTN_MAX_GROUP || group * 64 > ATTN_THREADS || group * a.d > ATTN_THREADS)
+        return fail(NC_ERR_ARGUMENT, "attention with %d heads over %d KV heads of dim %d is unsupported", a.heads,
+                    a.kv, a.d);
+    if (a.q_out && (group * a.d) % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized attention output needs whole blocks");
+    if (attention_smem(group, a.d, a.cap) > 220 * 1024)
+        return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
+    switch (a.d) {
+        case 16: return launch_attention_d<16>(st, a, rows);
+        case 64: return launch_attention_d<64>(st, a, rows);
+        case 128: return launch_attention_d<128>(st, a, rows);
+        default: return fail(NC_ERR_ARGUMENT, "head dim %d unsupported (16, 64, 128)", a.d);
+    }
 }
 
 float f32_from_bits(int64_t bits) {
@@ -394,6 +415,19 @@ extern "C" int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host
     return NC_OK;
 }
 
+extern "C" int32_t nc_selfcheck_div127(int64_t *mismatches) {
+    unsigned long long *d = nullptr;
+    CUDA_TRY(cudaMalloc(&d, sizeof *d));
+    CUDA_TRY(cudaMemset(d, 0, sizeof *d));
+    selfcheck_div127_kernel<<<1184, 256>>>(d);
+    NC_TRY(check_launch("selfcheck_div127_kernel"));
+    unsigned long long h = 0;
+    CUDA_TRY(cudaMemcpy(&h, d, sizeof h, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaFree(d));
+    *mismatches = (int64_t)h;
+    return NC_OK;
+}
+
 extern "C" int32_t nc_expf_exact(void **p, const int64_t *s, void *stream) {
     if (s[0] <= 0) return NC_OK;
     expf_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>((float *)p[0], (const float *)p[1], s[0]);
@@ -474,7 +508,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
     const int Hq = (int)(c.heads * d), Nqkv = (int)((c.heads + 2 * c.kv_heads) * d);
     const bool q8 = c.quant != 0;
     const bool norm_fused = rows <= PRO_NORM_ROWS && H <= 8 * CHUNK;
-    const bool attn_quant = q8 && d % QBLOCK == 0;
+    const bool attn_quant = q8 && ((c.heads / c.kv_heads) * d) % QBLOCK == 0;
 
     CUDA_TRY(launch_k(gather_kernel, rows, 256, 0, st, m->x, m->ids, m->embed, m->err, c.vocab, H));
     NC_TRY(check_launch("gather_kernel"));
@@ -579,7 +613,7 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
         return fail(NC_ERR_ARGUMENT, "unsupported model shape");
     if (c.hidden % 32 || c.inter % 32 || (c.heads * c.head_dim) % 32)
         return fail(NC_ERR_ARGUMENT, "widths must be whole 32-blocks");
-    if (attention_smem((int)c.head_dim, c.capacity) > 220 * 1024)
+    if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024)
         return fail(NC_ERR_ARGUMENT, "capacity %d exceeds the attention kernel's shared memory", c.capacity);
 
     auto m = std::make_unique<nc_model>();

@@ -763,156 +763,191 @@ struct AttnArgs {
     int32_t *bsums_out;
 };
 
-constexpr int ATTN_THREADS = 256;
-constexpr int ATTN_VCHUNK = 64;      // positions per staged V chunk
-constexpr int ATTN_VSTAGES = 4;
+constexpr int ATTN_THREADS = 512;
+constexpr int ATTN_CHUNK = 128;      // positions per staged K or V chunk
+constexpr int ATTN_STAGES = 3;
+constexpr int ATTN_MAX_GROUP = 8;    // query heads per KV head
 
+template <int D>
+__host__ __device__ constexpr size_t attention_smem_floats(int group, int cap) {
+    return (size_t)ATTN_STAGES * ATTN_CHUNK * D + (size_t)group * (((size_t)cap + 3) & ~(size_t)3) +
+           (size_t)(group + 2) * D;
+}
+
+// One CTA per (row, KV head) serves the `group` query heads that share the KV head
+// (repeat_kv, nanocompile/nn.py:109-120): K and V cross to the SM once.  K chunks, then V
+// chunks, stream through a ring of shared-memory stages by cp.async, XOR-swizzled by 16-byte
+// piece so a thread reading one position's row does not bank-conflict with its neighbours.
+template <int D>
 __global__ void __launch_bounds__(ATTN_THREADS)
 attention_kernel(AttnArgs a) {
+    constexpr int PPR = D / 4;                       // 16-byte pieces per row
+    constexpr int HALF = D / 2;
     extern __shared__ __align__(16) float sm[];
     release_dependents();
     wait_for_producer();
-    const int d = a.d, half = d / 2, group = a.heads / a.kv;
-    const int r = blockIdx.x / a.heads, h = blockIdx.x % a.heads, g = h / group;
+    const int group = a.heads / a.kv;
+    const int r = blockIdx.x / a.kv, g = blockIdx.x % a.kv;
     const int pos = a.pos[r], len = pos + 1;
-    float *vbuf = sm;                                        // [VSTAGES][VCHUNK][d]
-    float *e = vbuf + ATTN_VSTAGES * ATTN_VCHUNK * d;        // [cap]: scores, exps, probabilities
-    float *q = e + ((a.cap + 3) & ~3);                       // [d]
-    float *kn = q + d, *vn = kn + d;                         // [d] each
+    const int cap4 = (a.cap + 3) & ~3;
+    float4 *ring = reinterpret_cast<float4 *>(sm);                 // [STAGES][CHUNK][PPR]
+    float *e = sm + ATTN_STAGES * ATTN_CHUNK * D;                  // [group][cap4]
+    float *q = e + group * cap4;                                   // [group][D]
+    float *kn = q + group * D, *vn = kn + D;                       // [D] each
     __shared__ uint64_t tab[32];
-    __shared__ float wred[ATTN_THREADS / 32];
-    __shared__ float s_max, s_sum;
+    __shared__ float s_max[ATTN_MAX_GROUP], s_sum[ATTN_MAX_GROUP];
+    __shared__ float wmax[ATTN_THREADS / 32];
     const int t = threadIdx.x;
     if (t < 32) tab[t] = kExpTab[t];
 
     float *base = a.cache + (int64_t)a.slot[r] * a.slot_stride;
-    float *K = base + (int64_t)g * a.cap * d;
-    float *V = base + ((int64_t)a.kv + g) * a.cap * d;
-    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * d;
-    const float *cs = a.cos_tab + (int64_t)pos * half, *sn = a.sin_tab + (int64_t)pos * half;
+    float *K = base + (int64_t)g * a.cap * D;
+    float *V = base + ((int64_t)a.kv + g) * a.cap * D;
+    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
+    const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
 
-    // RoPE of q (and of this group's new k), and v
-    for (int i = t; i < 3 * d; i += ATTN_THREADS) {
-        const int which = i / d, c = i % d;
-        const float *src = which == 0 ? qkv + h * d : (which == 1 ? qkv + (a.heads + g) * d : qkv + (a.heads + a.kv + g) * d);
-        if (which == 2) {
+    // RoPE of the group's q heads and of the new k; the new v
+    for (int i = t; i < (group + 2) * D; i += ATTN_THREADS) {
+        const int h = i / D, c = i % D;
+        const float *src = h < group ? qkv + (g * group + h) * D : (h == group ? qkv + (a.heads + g) * D
+                                                                              : qkv + (a.heads + a.kv + g) * D);
+        if (h == group + 1) {
             vn[c] = src[c];
             continue;
         }
         const float t1 = src[c];
-        const float rot = c < half ? -src[c + half] : src[c - half];
-        const float v = fadd(fmul(t1, cs[c % half]), fmul(rot, sn[c % half]));
-        (which == 0 ? q : kn)[c] = v;
+        const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
+        const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
+        if (h < group) q[h * D + c] = v;
+        else kn[c] = v;
     }
     __syncthreads();
-    if (a.mode != 2 && h % group == 0) {
-        for (int c = t; c < d; c += ATTN_THREADS) {
-            K[(int64_t)pos * d + c] = kn[c];
-            V[(int64_t)pos * d + c] = vn[c];
+    if (a.mode != 2) {
+        for (int c = t; c < D; c += ATTN_THREADS) {
+            K[(int64_t)pos * D + c] = kn[c];
+            V[(int64_t)pos * D + c] = vn[c];
         }
+        if (a.mode == 1) return;
     }
-    if (a.mode == 1) return;
-    const bool own_new = a.mode == 0;      // position pos comes from kn / vn, not the cache
+    const bool own_new = a.mode == 0;       // position pos comes from kn / vn, not the cache
 
-    // stage the first V chunks while the scores and the sum are computed
-    const int chunks = (len + ATTN_VCHUNK - 1) / ATTN_VCHUNK;
-    const int pieces = ATTN_VCHUNK * d / 4;
-    auto stage_chunk = [&](int c) {
-        if (c < chunks) {
-            float *dst = vbuf + (c % ATTN_VSTAGES) * ATTN_VCHUNK * d;
-            for (int pc = t; pc < pieces; pc += ATTN_THREADS) {
-                const int row = pc / (d / 4), col = pc % (d / 4);
-                const int jpos = c * ATTN_VCHUNK + row;
-                if (jpos < len) cp_async16(dst + row * d + col * 4, V + (int64_t)jpos * d + col * 4);
+    const int nk = (len + ATTN_CHUNK - 1) / ATTN_CHUNK;
+    auto stage = [&](int idx) {             // chunk idx < nk: K chunk idx; else V chunk idx - nk
+        if (idx < 2 * nk) {
+            const float *src = idx < nk ? K : V;
+            const int j0 = (idx < nk ? idx : idx - nk) * ATTN_CHUNK;
+            float4 *dst = ring + (idx % ATTN_STAGES) * ATTN_CHUNK * PPR;
+            for (int pc = t; pc < ATTN_CHUNK * PPR; pc += ATTN_THREADS) {
+                const int row = pc / PPR, col = pc % PPR;
+                if (j0 + row < len) cp_async16(dst + row * PPR + (col ^ (row % PPR)), src + (int64_t)(j0 + row) * D + col * 4);
             }
         }
         cp_async_commit();
     };
 #pragma unroll
-    for (int c = 0; c < ATTN_VSTAGES - 1; ++c) stage_chunk(c);
+    for (int i = 0; i < ATTN_STAGES - 1; ++i) stage(i);
 
-    // scores, two positions at a time per thread
+    // scores: thread t owns head t / 64 and positions t % 64 (+ 64) of each chunk
+    const int hh = t / 64, pl = t % 64;
+    const bool scorer = hh < group;
     float mx = __uint_as_float(0xff800000u);
-    for (int j0 = t; j0 < len; j0 += 2 * ATTN_THREADS) {
-        const int j1 = j0 + ATTN_THREADS;
-        const float *k0 = (own_new && j0 == pos) ? kn : K + (int64_t)j0 * d;
-        const float *k1 = j1 < len ? ((own_new && j1 == pos) ? kn : K + (int64_t)j1 * d) : k0;
-        float acc0 = 0.0f, acc1 = 0.0f;
-        for (int c = 0; c < d; c += 4) {
-            const float4 a0 = *reinterpret_cast<const float4 *>(k0 + c);
-            const float4 a1 = *reinterpret_cast<const float4 *>(k1 + c);
-            const float4 qv = *reinterpret_cast<const float4 *>(q + c);
-            acc0 = fadd(acc0, fmul(qv.x, a0.x)); acc1 = fadd(acc1, fmul(qv.x, a1.x));
-            acc0 = fadd(acc0, fmul(qv.y, a0.y)); acc1 = fadd(acc1, fmul(qv.y, a1.y));
-            acc0 = fadd(acc0, fmul(qv.z, a0.z)); acc1 = fadd(acc1, fmul(qv.z, a1.z));
-            acc0 = fadd(acc0, fmul(qv.w, a0.w)); acc1 = fadd(acc1, fmul(qv.w, a1.w));
-        }
-        const float t0 = fadd(fmul(acc0, a.scale), 0.0f);
-        e[j0] = t0;
-        mx = nan_max(mx, t0);
-        if (j1 < len) {
-            const float t1 = fadd(fmul(acc1, a.scale), 0.0f);
-            e[j1] = t1;
-            mx = nan_max(mx, t1);
-        }
-    }
-    mx = warp_nan_max(mx);
-    if ((t & 31) == 0) wred[t / 32] = mx;
-    __syncthreads();
-    if (t == 0) {
-        float m = wred[0];
-        for (int w = 1; w < ATTN_THREADS / 32; ++w) m = nan_max(m, wred[w]);
-        s_max = m;
-    }
-    __syncthreads();
-    const float m = s_max;
-    for (int j = t; j < len; j += ATTN_THREADS) e[j] = expf_exact(fsub(e[j], m), tab);
-    __syncthreads();
-    if (t == 0) s_sum = chain_sum(e, len);
-    __syncthreads();
-    const float sum = s_sum;
-    for (int j = t; j < len; j += ATTN_THREADS) e[j] = fdiv(e[j], sum);
-
-    // probabilities @ V, chunk by chunk; thread c < d owns output c
-    float acc = 0.0f;
-    for (int c = 0; c < chunks; ++c) {
-        cp_async_wait<ATTN_VSTAGES - 2>();
+    for (int ci = 0; ci < nk; ++ci) {
+        cp_async_wait<ATTN_STAGES - 2>();
         __syncthreads();
-        stage_chunk(c + ATTN_VSTAGES - 1);
-        if (t < d) {
-            const float *vb = vbuf + (c % ATTN_VSTAGES) * ATTN_VCHUNK * d + t;
-            const int j0 = c * ATTN_VCHUNK;
-            const int n = min(ATTN_VCHUNK, len - j0);
-            const int stop = (own_new && j0 + n == len) ? n - 1 : n;   // the new row comes from vn
+        stage(ci + ATTN_STAGES - 1);
+        if (scorer) {
+            const float4 *ck = ring + (ci % ATTN_STAGES) * ATTN_CHUNK * PPR;
+            const float4 *qh = reinterpret_cast<const float4 *>(q + hh * D);
+#pragma unroll
+            for (int half = 0; half < ATTN_CHUNK / 64; ++half) {
+                const int row = pl + half * 64, j = ci * ATTN_CHUNK + row;
+                if (j < len) {
+                    const bool fresh = own_new && j == pos;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < PPR; ++c) {
+                        const float4 kv4 = fresh ? reinterpret_cast<const float4 *>(kn)[c] : ck[row * PPR + (c ^ (row % PPR))];
+                        const float4 q4 = qh[c];
+                        acc = fadd(acc, fmul(q4.x, kv4.x));
+                        acc = fadd(acc, fmul(q4.y, kv4.y));
+                        acc = fadd(acc, fmul(q4.z, kv4.z));
+                        acc = fadd(acc, fmul(q4.w, kv4.w));
+                    }
+                    const float sc = fadd(fmul(acc, a.scale), 0.0f);
+                    e[hh * cap4 + j] = sc;
+                    mx = nan_max(mx, sc);
+                }
+            }
+        }
+    }
+    // per-head maximum: the two warps of each head
+    mx = warp_nan_max(mx);
+    if ((t & 31) == 0) wmax[t / 32] = mx;
+    __syncthreads();
+    if (t < group) s_max[t] = nan_max(wmax[2 * t], wmax[2 * t + 1]);
+    __syncthreads();
+    for (int i = t; i < group * len; i += ATTN_THREADS) {
+        const int h = i / len, j = i % len;
+        e[h * cap4 + j] = expf_exact(fsub(e[h * cap4 + j], s_max[h]), tab);
+    }
+    __syncthreads();
+    if (t < group) s_sum[t] = chain_sum(e + t * cap4, len);           // the in-order sums
+    __syncthreads();
+    for (int i = t; i < group * len; i += ATTN_THREADS) {
+        const int h = i / len, j = i % len;
+        e[h * cap4 + j] = fdiv(e[h * cap4 + j], s_sum[h]);
+    }
+
+    // probabilities @ V: thread t owns (head t / D, dimension t % D), positions in order
+    const int ph = t / D, dim = t % D;
+    const bool pv = ph < group;
+    float acc = 0.0f;
+    for (int ci = 0; ci < nk; ++ci) {
+        const int idx = nk + ci;
+        cp_async_wait<ATTN_STAGES - 2>();
+        __syncthreads();
+        stage(idx + ATTN_STAGES - 1);
+        if (pv) {
+            const float *cv = reinterpret_cast<const float *>(ring + (idx % ATTN_STAGES) * ATTN_CHUNK * PPR);
+            const float *p = e + ph * cap4 + ci * ATTN_CHUNK;
+            const int n = min(ATTN_CHUNK, len - ci * ATTN_CHUNK);
+            const bool last = ci == nk - 1;
+            const int stop = (own_new && last) ? n - 1 : n;           // the new row comes from vn
+            const int piece = dim / 4, within = dim % 4;
             int jj = 0;
             for (; jj + 8 <= stop; jj += 8) {
-                float pv[8], vv[8];
+                float pw[8], vw[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) { pv[u] = e[j0 + jj + u]; vv[u] = vb[(jj + u) * d]; }
+                for (int u = 0; u < 8; ++u) {
+                    const int row = jj + u;
+                    pw[u] = p[row];
+                    vw[u] = cv[(row * PPR + (piece ^ (row % PPR))) * 4 + within];
+                }
 #pragma unroll
-                for (int u = 0; u < 8; ++u) acc = fadd(acc, fmul(pv[u], vv[u]));
+                for (int u = 0; u < 8; ++u) acc = fadd(acc, fmul(pw[u], vw[u]));
             }
-            for (; jj < stop; ++jj) acc = fadd(acc, fmul(e[j0 + jj], vb[jj * d]));
-            if (stop != n) acc = fadd(acc, fmul(e[pos], vn[t]));
+            for (; jj < stop; ++jj) acc = fadd(acc, fmul(p[jj], cv[(jj * PPR + (piece ^ (jj % PPR))) * 4 + within]));
+            if (stop != n) acc = fadd(acc, fmul(p[n - 1], vn[dim]));
         }
     }
     cp_async_wait<0>();
-    if (t < d && a.ctx) a.ctx[(int64_t)r * a.heads * d + h * d + t] = acc;
+    const int width = a.heads * D;
+    if (pv && a.ctx) a.ctx[(int64_t)r * width + (g * group + ph) * D + dim] = acc;
     if (a.q_out) {
-        // this head's outputs are whole quantization blocks of o_proj's input (calls 18-23)
+        // the group's outputs are whole quantization blocks of o_proj's input (calls 18-23)
         __syncthreads();
-        if (t < d) q[t] = acc;
+        if (pv) q[ph * D + dim] = acc;
         __syncthreads();
-        const int w = t / 32, lane = t % 32, width = a.heads * d;
-        if (w < d / QBLOCK) {
+        const int w = t / 32, lane = t % 32;
+        if (w < group * D / QBLOCK) {
             int8_t qv;
             int bs;
             const float sc = quantize_block_warp(q[w * QBLOCK + lane], &qv, &bs);
-            const int blk = (h * d) / QBLOCK + w;
-            a.q_out[(int64_t)r * width + h * d + w * QBLOCK + lane] = qv;
+            const int col = g * group * D + w * QBLOCK;
+            a.q_out[(int64_t)r * width + col + lane] = qv;
             if (lane == 0) {
-                a.xs_out[(int64_t)r * (width / QBLOCK) + blk] = sc;
-                a.bsums_out[(int64_t)r * (width / QBLOCK) + blk] = bs;
+                a.xs_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = sc;
+                a.bsums_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = bs;
             }
         }
     }
@@ -922,6 +957,18 @@ attention_kernel(AttnArgs a) {
 __global__ void xor80_kernel(uint8_t *p, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         p[i] ^= 0x80;
+}
+
+// Every non-negative float through div127 and through the IEEE divide; counts differences.
+__global__ void selfcheck_div127_kernel(unsigned long long *mismatches) {
+    unsigned long long bad = 0;
+    for (uint64_t u = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; u < 0x80000000ull;
+         u += (uint64_t)gridDim.x * blockDim.x) {
+        const float x = __uint_as_float((uint32_t)u);
+        const float a = div127(x), b = fdiv(x, 127.0f);
+        if (__float_as_uint(a) != __float_as_uint(b) && !(a != a && b != b)) ++bad;
+    }
+    if (bad) atomicAdd(mismatches, bad);
 }
 
 __global__ void expf_kernel(float *out, const float *x, int64_t n) {

@@ -74,6 +74,8 @@ def library() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.argtypes = [ctypes.POINTER(_vp), _P64, _vp]
             fn.restype = _i32
+        L.nc_selfcheck_div127.argtypes = [_P64]
+        L.nc_selfcheck_div127.restype = _i32
         L.nc_lm_head_scratch_bytes.argtypes = [_i64, _i64]
         L.nc_lm_head_scratch_bytes.restype = _i64
         L.nc_device_count.argtypes = [_P32]

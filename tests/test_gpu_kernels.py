@@ -39,12 +39,23 @@ def test_expf_is_glibc_bit_for_bit(cuda):
     assert same_bits(dout.numpy(), oracle.expf_libm(x))
 
 
+def test_block_scale_division_is_ieee_for_every_float(cuda):
+    import ctypes
+
+    bad = ctypes.c_int64(-1)
+    cuda.check(cuda.library().nc_selfcheck_div127(ctypes.byref(bad)))
+    assert bad.value == 0
+
+
 @pytest.mark.parametrize("rows,k", [(1, 896), (3, 4864), (7, 96), (2, 64)])
 def test_quantize_blocks(cuda, rows, k):
     rng = np.random.default_rng(rows * k)
     x = activations(rng, rows, k)
     x[0, :32] = 0.0                                  # an all-zero block: scale 1
     x[-1, 32:36] = [0.5, -0.5, 1.5, -2.5]
+    if k >= 96:                                      # quotients landing on half-integers
+        x[0, 64:96] = np.arange(-16, 16, dtype=np.float32) + 0.5
+        x[0, 64] = 127.0
     xq, xs, off, sums = oracle.quantize_blocks(x)
     dx = DeviceArray(cuda, x)
     dq = DeviceArray(cuda, shape=(rows, k), dtype=np.int8)
