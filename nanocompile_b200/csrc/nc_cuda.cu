@@ -263,33 +263,46 @@ int32_t launch_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) 
     return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<16>(st, a, epi, argmax);
 }
 
-size_t attention_smem(int group, int d, int cap) {
+size_t attention_smem(int heads_per_cta, int d, int cap) {
     switch (d) {
-        case 16: return sizeof(float) * attention_smem_floats<16>(group, cap);
-        case 64: return sizeof(float) * attention_smem_floats<64>(group, cap);
-        case 128: return sizeof(float) * attention_smem_floats<128>(group, cap);
+        case 16: return sizeof(float) * attention_smem_floats<16>(heads_per_cta, cap);
+        case 64: return sizeof(float) * attention_smem_floats<64>(heads_per_cta, cap);
+        case 128: return sizeof(float) * attention_smem_floats<128>(heads_per_cta, cap);
         default: return (size_t)1 << 40;
     }
 }
 
+template <int D, int G>
+int32_t launch_attention_g(cudaStream_t st, const AttnArgs &a, int rows) {
+    const size_t smem = sizeof(float) * attention_smem_floats<D>(G, a.cap);
+    if (smem > 220 * 1024) return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
+    CUDA_TRY(allow_smem(attention_kernel<D, G>, smem));
+    CUDA_TRY(launch_k(attention_kernel<D, G>, rows * (a.heads / G), attention_threads(G), smem, st, a));
+    return check_launch("attention_kernel");
+}
+
+// Few rows (decode of a handful of sequences): one CTA per query head, for parallelism.  Many
+// rows: one CTA per KV head, reading each KV row once for its group of query heads.
 template <int D>
 int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows) {
     const int group = a.heads / a.kv;
-    const size_t smem = sizeof(float) * attention_smem_floats<D>(group, a.cap);
-    CUDA_TRY(allow_smem(attention_kernel<D>, smem));
-    CUDA_TRY(launch_k(attention_kernel<D>, rows * a.kv, ATTN_THREADS, smem, st, a));
-    return check_launch("attention_kernel");
+    if (rows <= 8 || group == 1) return launch_attention_g<D, 1>(st, a, rows);
+    switch (group) {
+        case 2: return launch_attention_g<D, 2>(st, a, rows);
+        case 4: return launch_attention_g<D, 4>(st, a, rows);
+        case 7: return launch_attention_g<D, 7>(st, a, rows);
+        case 8: return launch_attention_g<D, 8>(st, a, rows);
+        default: return launch_attention_g<D, 1>(st, a, rows);
+    }
 }
 
 int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
     if (rows <= 0) return NC_OK;
     const int group = a.heads / a.kv;
-    if (a.heads % a.kv || group > ATTN_MAX_GROUP || group * 64 > ATTN_THREADS || group * a.d > ATTN_THREADS)
+    if (a.heads % a.kv || group > ATTN_MAX_GROUP || group * a.d > attention_threads(group))
         return fail(NC_ERR_ARGUMENT, "attention with %d heads over %d KV heads of dim %d is unsupported", a.heads,
                     a.kv, a.d);
-    if (a.q_out && (group * a.d) % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized attention output needs whole blocks");
-    if (attention_smem(group, a.d, a.cap) > 220 * 1024)
-        return fail(NC_ERR_ARGUMENT, "attention over %d positions exceeds shared memory", a.cap);
+    if (a.q_out && a.d % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized attention output needs whole blocks");
     switch (a.d) {
         case 16: return launch_attention_d<16>(st, a, rows);
         case 64: return launch_attention_d<64>(st, a, rows);
@@ -508,7 +521,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
     const int Hq = (int)(c.heads * d), Nqkv = (int)((c.heads + 2 * c.kv_heads) * d);
     const bool q8 = c.quant != 0;
     const bool norm_fused = rows <= PRO_NORM_ROWS && H <= 8 * CHUNK;
-    const bool attn_quant = q8 && ((c.heads / c.kv_heads) * d) % QBLOCK == 0;
+    const bool attn_quant = q8 && d % QBLOCK == 0;
 
     CUDA_TRY(launch_k(gather_kernel, rows, 256, 0, st, m->x, m->ids, m->embed, m->err, c.vocab, H));
     NC_TRY(check_launch("gather_kernel"));
@@ -613,7 +626,8 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
         return fail(NC_ERR_ARGUMENT, "unsupported model shape");
     if (c.hidden % 32 || c.inter % 32 || (c.heads * c.head_dim) % 32)
         return fail(NC_ERR_ARGUMENT, "widths must be whole 32-blocks");
-    if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024)
+    if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024 &&
+        attention_smem(1, (int)c.head_dim, c.capacity) > 220 * 1024)
         return fail(NC_ERR_ARGUMENT, "capacity %d exceeds the attention kernel's shared memory", c.capacity);
 
     auto m = std::make_unique<nc_model>();

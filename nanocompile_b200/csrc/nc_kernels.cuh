@@ -763,40 +763,45 @@ struct AttnArgs {
     int32_t *bsums_out;
 };
 
-constexpr int ATTN_THREADS = 512;
 constexpr int ATTN_CHUNK = 128;      // positions per staged K or V chunk
 constexpr int ATTN_STAGES = 3;
 constexpr int ATTN_MAX_GROUP = 8;    // query heads per KV head
 
+__host__ __device__ constexpr int attention_threads(int heads_per_cta) { return 64 * (heads_per_cta < 2 ? 2 : heads_per_cta); }
+
 template <int D>
-__host__ __device__ constexpr size_t attention_smem_floats(int group, int cap) {
-    return (size_t)ATTN_STAGES * ATTN_CHUNK * D + (size_t)group * (((size_t)cap + 3) & ~(size_t)3) +
-           (size_t)(group + 2) * D;
+__host__ __device__ constexpr size_t attention_smem_floats(int heads_per_cta, int cap) {
+    return (size_t)ATTN_STAGES * ATTN_CHUNK * D + (size_t)heads_per_cta * (((size_t)cap + 3) & ~(size_t)3) +
+           (size_t)(heads_per_cta + 2) * D;
 }
 
-// One CTA per (row, KV head) serves the `group` query heads that share the KV head
-// (repeat_kv, nanocompile/nn.py:109-120): K and V cross to the SM once.  K chunks, then V
+// One CTA per (row, G query heads that share one KV head; repeat_kv, nanocompile/nn.py:109-120).
+// G = 1 spreads a decode step's heads over as many SMs as there are heads; G = the group size
+// reads each KV head's rows once for all its query heads (large batches).  K chunks, then V
 // chunks, stream through a ring of shared-memory stages by cp.async, XOR-swizzled by 16-byte
 // piece so a thread reading one position's row does not bank-conflict with its neighbours.
-template <int D>
-__global__ void __launch_bounds__(ATTN_THREADS)
+template <int D, int G>
+__global__ void __launch_bounds__(attention_threads(G))
 attention_kernel(AttnArgs a) {
+    constexpr int T = attention_threads(G);
     constexpr int PPR = D / 4;                       // 16-byte pieces per row
     constexpr int HALF = D / 2;
     extern __shared__ __align__(16) float sm[];
     release_dependents();
     wait_for_producer();
     const int group = a.heads / a.kv;
-    const int r = blockIdx.x / a.kv, g = blockIdx.x % a.kv;
+    const int ctas_per_row = a.heads / G;
+    const int r = blockIdx.x / ctas_per_row, h0 = (blockIdx.x % ctas_per_row) * G, g = h0 / group;
+    const bool owner = h0 % group == 0;              // the CTA that writes this KV head's new row
     const int pos = a.pos[r], len = pos + 1;
     const int cap4 = (a.cap + 3) & ~3;
     float4 *ring = reinterpret_cast<float4 *>(sm);                 // [STAGES][CHUNK][PPR]
-    float *e = sm + ATTN_STAGES * ATTN_CHUNK * D;                  // [group][cap4]
-    float *q = e + group * cap4;                                   // [group][D]
-    float *kn = q + group * D, *vn = kn + D;                       // [D] each
+    float *e = sm + ATTN_STAGES * ATTN_CHUNK * D;                  // [G][cap4]
+    float *q = e + G * cap4;                                       // [G][D]
+    float *kn = q + G * D, *vn = kn + D;                           // [D] each
     __shared__ uint64_t tab[32];
-    __shared__ float s_max[ATTN_MAX_GROUP], s_sum[ATTN_MAX_GROUP];
-    __shared__ float wmax[ATTN_THREADS / 32];
+    __shared__ float s_max[G], s_sum[G];
+    __shared__ float wmax[T / 32][G];
     const int t = threadIdx.x;
     if (t < 32) tab[t] = kExpTab[t];
 
@@ -806,27 +811,27 @@ attention_kernel(AttnArgs a) {
     const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
     const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
 
-    // RoPE of the group's q heads and of the new k; the new v
-    for (int i = t; i < (group + 2) * D; i += ATTN_THREADS) {
+    // RoPE of the CTA's q heads and of the new k; the new v
+    for (int i = t; i < (G + 2) * D; i += T) {
         const int h = i / D, c = i % D;
-        const float *src = h < group ? qkv + (g * group + h) * D : (h == group ? qkv + (a.heads + g) * D
-                                                                              : qkv + (a.heads + a.kv + g) * D);
-        if (h == group + 1) {
+        const float *src = h < G ? qkv + (h0 + h) * D : (h == G ? qkv + (a.heads + g) * D : qkv + (a.heads + a.kv + g) * D);
+        if (h == G + 1) {
             vn[c] = src[c];
             continue;
         }
         const float t1 = src[c];
         const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
         const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
-        if (h < group) q[h * D + c] = v;
+        if (h < G) q[h * D + c] = v;
         else kn[c] = v;
     }
     __syncthreads();
     if (a.mode != 2) {
-        for (int c = t; c < D; c += ATTN_THREADS) {
-            K[(int64_t)pos * D + c] = kn[c];
-            V[(int64_t)pos * D + c] = vn[c];
-        }
+        if (owner)
+            for (int c = t; c < D; c += T) {
+                K[(int64_t)pos * D + c] = kn[c];
+                V[(int64_t)pos * D + c] = vn[c];
+            }
         if (a.mode == 1) return;
     }
     const bool own_new = a.mode == 0;       // position pos comes from kn / vn, not the cache
@@ -837,7 +842,7 @@ attention_kernel(AttnArgs a) {
             const float *src = idx < nk ? K : V;
             const int j0 = (idx < nk ? idx : idx - nk) * ATTN_CHUNK;
             float4 *dst = ring + (idx % ATTN_STAGES) * ATTN_CHUNK * PPR;
-            for (int pc = t; pc < ATTN_CHUNK * PPR; pc += ATTN_THREADS) {
+            for (int pc = t; pc < ATTN_CHUNK * PPR; pc += T) {
                 const int row = pc / PPR, col = pc % PPR;
                 if (j0 + row < len) cp_async16(dst + row * PPR + (col ^ (row % PPR)), src + (int64_t)(j0 + row) * D + col * 4);
             }
@@ -847,60 +852,68 @@ attention_kernel(AttnArgs a) {
 #pragma unroll
     for (int i = 0; i < ATTN_STAGES - 1; ++i) stage(i);
 
-    // scores: thread t owns head t / 64 and positions t % 64 (+ 64) of each chunk
-    const int hh = t / 64, pl = t % 64;
-    const bool scorer = hh < group;
-    float mx = __uint_as_float(0xff800000u);
+    // scores: (head, position) pairs of each chunk spread over the threads
+    float mx[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) mx[h] = __uint_as_float(0xff800000u);
     for (int ci = 0; ci < nk; ++ci) {
         cp_async_wait<ATTN_STAGES - 2>();
         __syncthreads();
         stage(ci + ATTN_STAGES - 1);
-        if (scorer) {
-            const float4 *ck = ring + (ci % ATTN_STAGES) * ATTN_CHUNK * PPR;
-            const float4 *qh = reinterpret_cast<const float4 *>(q + hh * D);
+        const float4 *ck = ring + (ci % ATTN_STAGES) * ATTN_CHUNK * PPR;
 #pragma unroll
-            for (int half = 0; half < ATTN_CHUNK / 64; ++half) {
-                const int row = pl + half * 64, j = ci * ATTN_CHUNK + row;
-                if (j < len) {
-                    const bool fresh = own_new && j == pos;
-                    float acc = 0.0f;
+        for (int pair0 = 0; pair0 < G * ATTN_CHUNK; pair0 += T) {
+            const int pair = pair0 + t;
+            const int hh = pair / ATTN_CHUNK, row = pair % ATTN_CHUNK, j = ci * ATTN_CHUNK + row;
+            if (pair < G * ATTN_CHUNK && j < len) {
+                const bool fresh = own_new && j == pos;
+                const float4 *qh = reinterpret_cast<const float4 *>(q + hh * D);
+                float acc = 0.0f;
 #pragma unroll
-                    for (int c = 0; c < PPR; ++c) {
-                        const float4 kv4 = fresh ? reinterpret_cast<const float4 *>(kn)[c] : ck[row * PPR + (c ^ (row % PPR))];
-                        const float4 q4 = qh[c];
-                        acc = fadd(acc, fmul(q4.x, kv4.x));
-                        acc = fadd(acc, fmul(q4.y, kv4.y));
-                        acc = fadd(acc, fmul(q4.z, kv4.z));
-                        acc = fadd(acc, fmul(q4.w, kv4.w));
-                    }
-                    const float sc = fadd(fmul(acc, a.scale), 0.0f);
-                    e[hh * cap4 + j] = sc;
-                    mx = nan_max(mx, sc);
+                for (int c = 0; c < PPR; ++c) {
+                    const float4 kv4 = fresh ? reinterpret_cast<const float4 *>(kn)[c] : ck[row * PPR + (c ^ (row % PPR))];
+                    const float4 q4 = qh[c];
+                    acc = fadd(acc, fmul(q4.x, kv4.x));
+                    acc = fadd(acc, fmul(q4.y, kv4.y));
+                    acc = fadd(acc, fmul(q4.z, kv4.z));
+                    acc = fadd(acc, fmul(q4.w, kv4.w));
                 }
+                const float sc = fadd(fmul(acc, a.scale), 0.0f);
+                e[hh * cap4 + j] = sc;
+#pragma unroll
+                for (int h = 0; h < G; ++h)
+                    if (h == hh) mx[h] = nan_max(mx[h], sc);
             }
         }
     }
-    // per-head maximum: the two warps of each head
-    mx = warp_nan_max(mx);
-    if ((t & 31) == 0) wmax[t / 32] = mx;
+    // per-head maxima
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        const float m = warp_nan_max(mx[h]);
+        if ((t & 31) == 0) wmax[t / 32][h] = m;
+    }
     __syncthreads();
-    if (t < group) s_max[t] = nan_max(wmax[2 * t], wmax[2 * t + 1]);
+    if (t < G) {
+        float m = wmax[0][t];
+        for (int w = 1; w < T / 32; ++w) m = nan_max(m, wmax[w][t]);
+        s_max[t] = m;
+    }
     __syncthreads();
-    for (int i = t; i < group * len; i += ATTN_THREADS) {
+    for (int i = t; i < G * len; i += T) {
         const int h = i / len, j = i % len;
         e[h * cap4 + j] = expf_exact(fsub(e[h * cap4 + j], s_max[h]), tab);
     }
     __syncthreads();
-    if (t < group) s_sum[t] = chain_sum(e + t * cap4, len);           // the in-order sums
+    if (t < G) s_sum[t] = chain_sum(e + t * cap4, len);           // the in-order sums
     __syncthreads();
-    for (int i = t; i < group * len; i += ATTN_THREADS) {
+    for (int i = t; i < G * len; i += T) {
         const int h = i / len, j = i % len;
         e[h * cap4 + j] = fdiv(e[h * cap4 + j], s_sum[h]);
     }
 
     // probabilities @ V: thread t owns (head t / D, dimension t % D), positions in order
     const int ph = t / D, dim = t % D;
-    const bool pv = ph < group;
+    const bool pv = ph < G;
     float acc = 0.0f;
     for (int ci = 0; ci < nk; ++ci) {
         const int idx = nk + ci;
@@ -932,18 +945,18 @@ attention_kernel(AttnArgs a) {
     }
     cp_async_wait<0>();
     const int width = a.heads * D;
-    if (pv && a.ctx) a.ctx[(int64_t)r * width + (g * group + ph) * D + dim] = acc;
+    if (pv && a.ctx) a.ctx[(int64_t)r * width + (h0 + ph) * D + dim] = acc;
     if (a.q_out) {
-        // the group's outputs are whole quantization blocks of o_proj's input (calls 18-23)
+        // the CTA's outputs are whole quantization blocks of o_proj's input (calls 18-23)
         __syncthreads();
         if (pv) q[ph * D + dim] = acc;
         __syncthreads();
         const int w = t / 32, lane = t % 32;
-        if (w < group * D / QBLOCK) {
+        if (w < G * D / QBLOCK) {
             int8_t qv;
             int bs;
             const float sc = quantize_block_warp(q[w * QBLOCK + lane], &qv, &bs);
-            const int col = g * group * D + w * QBLOCK;
+            const int col = h0 * D + w * QBLOCK;
             a.q_out[(int64_t)r * width + col + lane] = qv;
             if (lane == 0) {
                 a.xs_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = sc;
