@@ -161,23 +161,38 @@ int32_t launch_i8_epi(cudaStream_t st, const GemvI8Args &a, int epi) {
     return check_launch("gemv_i8_kernel");
 }
 
-template <int LPR, int NCH, int MAXG, int PRO, int EPI>
+template <int LPR, int NCH, int MAXG, int PRO, int EPI, int TB>
 int32_t launch_fused_t(cudaStream_t st, const FusedI8Args &f, size_t smem) {
     constexpr int THREADS = 256, ROWS = (THREADS / 32) * (32 / LPR);
-    auto kernel = gemv_i8_fused_kernel<LPR, NCH, MAXG, PRO, EPI>;
+    auto kernel = gemv_i8_fused_kernel<LPR, NCH, MAXG, PRO, EPI, TB>;
     CUDA_TRY(allow_smem(kernel, smem));
     CUDA_TRY(launch_k(kernel, (f.g.n + ROWS - 1) / ROWS, THREADS, smem, st, f));
     return check_launch("gemv_i8_fused_kernel");
 }
 
+// Several tokens are advanced together only in the batched model path's combinations.
+template <int PRO, int EPI>
+constexpr bool batched_combo() {
+    return (PRO == PRO_NONE && (EPI == EPI_BIAS || EPI == EPI_RESIDUAL || EPI == EPI_SWIGLU_QUANT)) ||
+           (PRO == PRO_OFFSET && EPI == EPI_RESIDUAL);
+}
+
+template <int LPR, int NCH, int MAXG, int PRO, int EPI>
+int32_t launch_fused_tb(cudaStream_t st, const FusedI8Args &f, size_t smem) {
+    if constexpr (batched_combo<PRO, EPI>()) {
+        if (f.g.m >= 4) return launch_fused_t<LPR, NCH, MAXG, PRO, EPI, 4>(st, f, smem);
+    }
+    return launch_fused_t<LPR, NCH, MAXG, PRO, EPI, 1>(st, f, smem);
+}
+
 template <int LPR, int NCH, int MAXG, int PRO>
 int32_t launch_fused_epi(cudaStream_t st, const FusedI8Args &f, int epi, size_t smem) {
     switch (epi) {
-        case EPI_NONE: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_NONE>(st, f, smem);
-        case EPI_BIAS: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_BIAS>(st, f, smem);
-        case EPI_RESIDUAL: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_RESIDUAL>(st, f, smem);
-        case EPI_SWIGLU: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_SWIGLU>(st, f, smem);
-        case EPI_SWIGLU_QUANT: return launch_fused_t<LPR, NCH, MAXG, PRO, EPI_SWIGLU_QUANT>(st, f, smem);
+        case EPI_NONE: return launch_fused_tb<LPR, NCH, MAXG, PRO, EPI_NONE>(st, f, smem);
+        case EPI_BIAS: return launch_fused_tb<LPR, NCH, MAXG, PRO, EPI_BIAS>(st, f, smem);
+        case EPI_RESIDUAL: return launch_fused_tb<LPR, NCH, MAXG, PRO, EPI_RESIDUAL>(st, f, smem);
+        case EPI_SWIGLU: return launch_fused_tb<LPR, NCH, MAXG, PRO, EPI_SWIGLU>(st, f, smem);
+        case EPI_SWIGLU_QUANT: return launch_fused_tb<LPR, NCH, MAXG, PRO, EPI_SWIGLU_QUANT>(st, f, smem);
         default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
     }
 }

@@ -348,20 +348,21 @@ constexpr int ACT_TILE_BYTES = 64 * 1024;
 
 __host__ __device__ inline int act_tile_tokens(int k) { return ACT_TILE_BYTES / (k + 4 * (k / QBLOCK)); }
 
-template <int LPR, int NCH, int MAXG, int PRO, int EPI>
+template <int LPR, int NCH, int MAXG, int PRO, int EPI, int TB>
 __global__ void __launch_bounds__(256, (EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT) ? 2 : 1)
 gemv_i8_fused_kernel(FusedI8Args f) {
-    // MAXG: 32-byte groups past the last whole chunk (0 when the width is whole chunks)
+    // MAXG: 32-byte groups past the last whole chunk (0 when the width is whole chunks).
+    // TB: tokens advanced together (independent chains in flight; 1 for a single token).
     constexpr int BPL = 128 / LPR;
     constexpr int APL = BPL / 4;
     constexpr bool TWO = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT;
-    constexpr bool XPRE = !TWO;             // activations of all chunks into registers first
+    constexpr bool XPRE = !TWO && TB == 1;  // activations of all chunks into registers first
     using SegT = typename Seg<BPL>::T;
     const GemvI8Args &a = f.g;
     extern __shared__ __align__(16) float dsm[];
     __shared__ uint64_t tab[32];
     __shared__ float s_inv;
-    __shared__ float hq[32 * 8];
+    __shared__ float hq[TB][32 * 8];
     const int nwarps = blockDim.x / 32;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int grp = lane / LPR, j = lane % LPR;
@@ -444,10 +445,12 @@ gemv_i8_fused_kernel(FusedI8Args f) {
                 xs_t[(i / blocks) * bl4 + i % blocks] = a.xs[(int64_t)t0 * blocks + i];
         }
         __syncthreads();
-        for (int tm = 0; tm < tn; ++tm) {
-            const int m = t0 + tm;
-            const int8_t *xrow_q = xq_t + tm * K;
-            const float *xsr = xs_t + tm * bl4;
+        for (int tm = 0; tm < tn; tm += TB) {
+            float acc[TB][APL], acc2[TB][APL];
+#pragma unroll
+            for (int b = 0; b < TB; ++b)
+#pragma unroll
+                for (int i = 0; i < APL; ++i) { acc[b][i] = 0.0f; acc2[b][i] = 0.0f; }
             uint32_t xv[XPRE ? NCH : 1][APL];
             float sv[XPRE ? NCH : 1];
             if (XPRE) {
@@ -455,32 +458,34 @@ gemv_i8_fused_kernel(FusedI8Args f) {
                 for (int c = 0; c < NCH; ++c) {
                     if (c < chunks) {
                         const int off = c * CHUNK + j * BPL;
-                        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow_q + off), xv[c]);
-                        sv[c] = xsr[off / QBLOCK];
+                        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xq_t + tm * K + off), xv[c]);
+                        sv[c] = xs_t[tm * bl4 + off / QBLOCK];
                     }
                 }
             }
-            float acc[APL], acc2[APL];
-#pragma unroll
-            for (int i = 0; i < APL; ++i) { acc[i] = 0.0f; acc2[i] = 0.0f; }
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
                 if (c < chunks) {
-                    uint32_t xc[APL];
-                    float sc;
-                    if (XPRE) {
+                    const int off = c * CHUNK + j * BPL;
 #pragma unroll
-                        for (int i = 0; i < APL; ++i) xc[i] = xv[XPRE ? c : 0][i];
-                        sc = sv[XPRE ? c : 0];
-                    } else {
-                        const int off = c * CHUNK + j * BPL;
-                        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow_q + off), xc);
-                        sc = xsr[off / QBLOCK];
-                    }
+                    for (int b = 0; b < TB; ++b) {
+                        if (tm + b < tn) {
+                            uint32_t xc[APL];
+                            float sc;
+                            if (XPRE) {
 #pragma unroll
-                    for (int i = 0; i < APL; ++i) {
-                        acc[i] = __fmaf_rn(dp4_lane(wv[c][i], xc[i]), sc, acc[i]);
-                        if (TWO) acc2[i] = __fmaf_rn(dp4_lane(wv2[c][i], xc[i]), sc, acc2[i]);
+                                for (int i = 0; i < APL; ++i) xc[i] = xv[XPRE ? c : 0][i];
+                                sc = sv[XPRE ? c : 0];
+                            } else {
+                                Seg<BPL>::split(*reinterpret_cast<const SegT *>(xq_t + (tm + b) * K + off), xc);
+                                sc = xs_t[(tm + b) * bl4 + off / QBLOCK];
+                            }
+#pragma unroll
+                            for (int i = 0; i < APL; ++i) {
+                                acc[b][i] = __fmaf_rn(dp4_lane(wv[c][i], xc[i]), sc, acc[b][i]);
+                                if (TWO) acc2[b][i] = __fmaf_rn(dp4_lane(wv2[c][i], xc[i]), sc, acc2[b][i]);
+                            }
+                        }
                     }
                 }
             }
@@ -488,39 +493,60 @@ gemv_i8_fused_kernel(FusedI8Args f) {
             for (int k1 = 0; k1 < MAXG; ++k1) {
                 if (k1 < groups && tail_lane) {
                     const int off = stride + k1 * 32 + j * BPL;
-                    uint32_t tx[APL];
-                    Seg<BPL>::split(*reinterpret_cast<const SegT *>(xrow_q + off), tx);
-                    const float s = xsr[off / QBLOCK];
 #pragma unroll
-                    for (int i = 0; i < APL; ++i) {
-                        acc[i] = __fmaf_rn(dp4_lane(tw[MAXG ? k1 : 0][i], tx[i]), s, acc[i]);
-                        if (TWO) acc2[i] = __fmaf_rn(dp4_lane(tw2[TWO && MAXG ? k1 : 0][i], tx[i]), s, acc2[i]);
+                    for (int b = 0; b < TB; ++b) {
+                        if (tm + b < tn) {
+                            uint32_t tx[APL];
+                            Seg<BPL>::split(*reinterpret_cast<const SegT *>(xq_t + (tm + b) * K + off), tx);
+                            const float s = xs_t[(tm + b) * bl4 + off / QBLOCK];
+#pragma unroll
+                            for (int i = 0; i < APL; ++i) {
+                                acc[b][i] = __fmaf_rn(dp4_lane(tw[MAXG ? k1 : 0][i], tx[i]), s, acc[b][i]);
+                                if (TWO) acc2[b][i] = __fmaf_rn(dp4_lane(tw2[TWO && MAXG ? k1 : 0][i], tx[i]), s, acc2[b][i]);
+                            }
+                        }
                     }
                 }
             }
-            const float sum = combine_lanes<APL>(acc);
-            const float sum2 = TWO ? combine_lanes<APL>(acc2) : 0.0f;
-            float out = 0.0f;
-            if (j == 0) {
-                const float off = offs[m];
-                const float y = fmul(fsub(sum, off), scale);
-                if (EPI == EPI_BIAS) out = fadd(y, bias);
-                else if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)m * a.n + rowc], y);
-                else if (TWO) out = swiglu(y, fmul(fsub(sum2, off), scale2), tab);
-                else out = y;
-                if (EPI != EPI_SWIGLU_QUANT && row_ok) a.out[(int64_t)m * a.n + row] = out;
+            // the residuals of these tokens, requested before the combine
+            float res[TB];
+#pragma unroll
+            for (int b = 0; b < TB; ++b) {
+                const int m = t0 + tm + b;
+                res[b] = (EPI == EPI_RESIDUAL && j == 0 && tm + b < tn) ? a.residual[(int64_t)m * a.n + rowc] : 0.0f;
+            }
+            float sum[TB], sum2[TB];
+#pragma unroll
+            for (int b = 0; b < TB; ++b) {
+                sum[b] = combine_lanes<APL>(acc[b]);
+                sum2[b] = TWO ? combine_lanes<APL>(acc2[b]) : 0.0f;
+            }
+#pragma unroll
+            for (int b = 0; b < TB; ++b) {
+                const int m = t0 + tm + b;
+                float out = 0.0f;
+                if (j == 0 && tm + b < tn) {
+                    const float off = offs[m];
+                    const float y = fmul(fsub(sum[b], off), scale);
+                    if (EPI == EPI_BIAS) out = fadd(y, bias);
+                    else if (EPI == EPI_RESIDUAL) out = fadd(res[b], y);
+                    else if (TWO) out = swiglu(y, fmul(fsub(sum2[b], off), scale2), tab);
+                    else out = y;
+                    if (EPI != EPI_SWIGLU_QUANT && row_ok) a.out[(int64_t)m * a.n + row] = out;
+                }
+                if (EPI == EPI_SWIGLU_QUANT && j == 0) hq[b][row - row0] = out;
             }
             if (EPI == EPI_SWIGLU_QUANT) {
-                // the CTA's rows are whole blocks: gather them, then one warp per block
-                const int rows_cta = nwarps * (32 / LPR);
-                if (j == 0) hq[row - row0] = out;
+                // the CTA's rows are whole blocks: one warp per (token, block)
+                const int rows_cta = nwarps * (32 / LPR), cblocks = rows_cta / QBLOCK;
                 __syncthreads();
-                for (int blk = warp; blk < rows_cta / QBLOCK; blk += nwarps) {
-                    const int gb = row0 / QBLOCK + blk;
-                    if (gb < a.n / QBLOCK) {
+                for (int wb = warp; wb < TB * cblocks; wb += nwarps) {
+                    const int b = wb / cblocks, blk = wb % cblocks;
+                    const int gb = row0 / QBLOCK + blk, m = t0 + tm + b;
+                    if (tm + b < tn && gb < a.n / QBLOCK) {
                         int8_t qv;
                         int bs;
-                        const float sc = quantize_block_warp(hq[blk * QBLOCK + lane], &qv, &bs);
+                        const float sc = quantize_block_warp(hq[b][blk * QBLOCK + lane], &qv, &bs);
                         f.q_out[(int64_t)m * a.n + gb * QBLOCK + lane] = qv;
                         if (lane == 0) {
                             f.xs_out[(int64_t)m * (a.n / QBLOCK) + gb] = sc;
