@@ -827,7 +827,7 @@ attention_kernel(AttnArgs a) {
     float *kn = q + G * D, *vn = kn + D;                           // [D] each
     __shared__ uint64_t tab[32];
     __shared__ float s_max[G], s_sum[G];
-    __shared__ float wmax[T / 32][G];
+    __shared__ float wmax[T / 32][1];
     const int t = threadIdx.x;
     if (t < 32) tab[t] = kExpTab[t];
 
@@ -863,14 +863,18 @@ attention_kernel(AttnArgs a) {
     const bool own_new = a.mode == 0;       // position pos comes from kn / vn, not the cache
 
     const int nk = (len + ATTN_CHUNK - 1) / ATTN_CHUNK;
+    // K chunks are XOR-swizzled by piece (a scoring thread reads a whole row); V chunks are plain
+    // (a warp reads consecutive dimensions of one row).
     auto stage = [&](int idx) {             // chunk idx < nk: K chunk idx; else V chunk idx - nk
         if (idx < 2 * nk) {
-            const float *src = idx < nk ? K : V;
-            const int j0 = (idx < nk ? idx : idx - nk) * ATTN_CHUNK;
+            const bool is_k = idx < nk;
+            const float *src = is_k ? K : V;
+            const int j0 = (is_k ? idx : idx - nk) * ATTN_CHUNK;
             float4 *dst = ring + (idx % ATTN_STAGES) * ATTN_CHUNK * PPR;
             for (int pc = t; pc < ATTN_CHUNK * PPR; pc += T) {
                 const int row = pc / PPR, col = pc % PPR;
-                if (j0 + row < len) cp_async16(dst + row * PPR + (col ^ (row % PPR)), src + (int64_t)(j0 + row) * D + col * 4);
+                if (j0 + row < len)
+                    cp_async16(dst + row * PPR + (is_k ? (col ^ (row % PPR)) : col), src + (int64_t)(j0 + row) * D + col * 4);
             }
         }
         cp_async_commit();
@@ -878,50 +882,48 @@ attention_kernel(AttnArgs a) {
 #pragma unroll
     for (int i = 0; i < ATTN_STAGES - 1; ++i) stage(i);
 
-    // scores: (head, position) pairs of each chunk spread over the threads
-    float mx[G];
+    // scores: thread t scores head t / SPH's positions t % SPH, t % SPH + SPH, ... of each chunk,
+    // with its head's q in registers
+    constexpr int SPH = (T / G) / 32 * 32 >= ATTN_CHUNK ? ATTN_CHUNK : (T / G) / 32 * 32;   // whole warps per head
+    const int hh = t / SPH, pl = t % SPH;
+    const bool scorer = hh < G;
+    float4 qr[PPR];
 #pragma unroll
-    for (int h = 0; h < G; ++h) mx[h] = __uint_as_float(0xff800000u);
+    for (int c = 0; c < PPR; ++c) qr[c] = reinterpret_cast<const float4 *>(q + (scorer ? hh : 0) * D)[c];
+    float mx = __uint_as_float(0xff800000u);
     for (int ci = 0; ci < nk; ++ci) {
         cp_async_wait<ATTN_STAGES - 2>();
         __syncthreads();
         stage(ci + ATTN_STAGES - 1);
         const float4 *ck = ring + (ci % ATTN_STAGES) * ATTN_CHUNK * PPR;
-#pragma unroll
-        for (int pair0 = 0; pair0 < G * ATTN_CHUNK; pair0 += T) {
-            const int pair = pair0 + t;
-            const int hh = pair / ATTN_CHUNK, row = pair % ATTN_CHUNK, j = ci * ATTN_CHUNK + row;
-            if (pair < G * ATTN_CHUNK && j < len) {
+        if (scorer) {
+            for (int row = pl; row < ATTN_CHUNK; row += SPH) {
+                const int j = ci * ATTN_CHUNK + row;
+                if (j >= len) break;
                 const bool fresh = own_new && j == pos;
-                const float4 *qh = reinterpret_cast<const float4 *>(q + hh * D);
                 float acc = 0.0f;
 #pragma unroll
                 for (int c = 0; c < PPR; ++c) {
                     const float4 kv4 = fresh ? reinterpret_cast<const float4 *>(kn)[c] : ck[row * PPR + (c ^ (row % PPR))];
-                    const float4 q4 = qh[c];
-                    acc = fadd(acc, fmul(q4.x, kv4.x));
-                    acc = fadd(acc, fmul(q4.y, kv4.y));
-                    acc = fadd(acc, fmul(q4.z, kv4.z));
-                    acc = fadd(acc, fmul(q4.w, kv4.w));
+                    acc = fadd(acc, fmul(qr[c].x, kv4.x));
+                    acc = fadd(acc, fmul(qr[c].y, kv4.y));
+                    acc = fadd(acc, fmul(qr[c].z, kv4.z));
+                    acc = fadd(acc, fmul(qr[c].w, kv4.w));
                 }
                 const float sc = fadd(fmul(acc, a.scale), 0.0f);
                 e[hh * cap4 + j] = sc;
-#pragma unroll
-                for (int h = 0; h < G; ++h)
-                    if (h == hh) mx[h] = nan_max(mx[h], sc);
+                mx = nan_max(mx, sc);
             }
         }
     }
-    // per-head maxima
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-        const float m = warp_nan_max(mx[h]);
-        if ((t & 31) == 0) wmax[t / 32][h] = m;
-    }
+    // per-head maxima: the warps of each head's scoring threads
+    mx = warp_nan_max(mx);
+    if ((t & 31) == 0) wmax[t / 32][0] = mx;
     __syncthreads();
     if (t < G) {
-        float m = wmax[0][t];
-        for (int w = 1; w < T / 32; ++w) m = nan_max(m, wmax[w][t]);
+        constexpr int WPH = SPH / 32 > 0 ? SPH / 32 : 1;
+        float m = wmax[t * WPH][0];
+        for (int w = 1; w < WPH; ++w) m = nan_max(m, wmax[t * WPH + w][0]);
         s_max[t] = m;
     }
     __syncthreads();
@@ -947,25 +949,28 @@ attention_kernel(AttnArgs a) {
         __syncthreads();
         stage(idx + ATTN_STAGES - 1);
         if (pv) {
-            const float *cv = reinterpret_cast<const float *>(ring + (idx % ATTN_STAGES) * ATTN_CHUNK * PPR);
+            const float *cv = reinterpret_cast<const float *>(ring + (idx % ATTN_STAGES) * ATTN_CHUNK * PPR) + dim;
             const float *p = e + ph * cap4 + ci * ATTN_CHUNK;
             const int n = min(ATTN_CHUNK, len - ci * ATTN_CHUNK);
             const bool last = ci == nk - 1;
             const int stop = (own_new && last) ? n - 1 : n;           // the new row comes from vn
-            const int piece = dim / 4, within = dim % 4;
             int jj = 0;
             for (; jj + 8 <= stop; jj += 8) {
-                float pw[8], vw[8];
+                const float4 p0 = *reinterpret_cast<const float4 *>(p + jj);
+                const float4 p1 = *reinterpret_cast<const float4 *>(p + jj + 4);
+                float vw[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int row = jj + u;
-                    pw[u] = p[row];
-                    vw[u] = cv[(row * PPR + (piece ^ (row % PPR))) * 4 + within];
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) acc = fadd(acc, fmul(pw[u], vw[u]));
+                for (int u = 0; u < 8; ++u) vw[u] = cv[(jj + u) * D];
+                acc = fadd(acc, fmul(p0.x, vw[0]));
+                acc = fadd(acc, fmul(p0.y, vw[1]));
+                acc = fadd(acc, fmul(p0.z, vw[2]));
+                acc = fadd(acc, fmul(p0.w, vw[3]));
+                acc = fadd(acc, fmul(p1.x, vw[4]));
+                acc = fadd(acc, fmul(p1.y, vw[5]));
+                acc = fadd(acc, fmul(p1.z, vw[6]));
+                acc = fadd(acc, fmul(p1.w, vw[7]));
             }
-            for (; jj < stop; ++jj) acc = fadd(acc, fmul(p[jj], cv[(jj * PPR + (piece ^ (jj % PPR))) * 4 + within]));
+            for (; jj < stop; ++jj) acc = fadd(acc, fmul(p[jj], cv[jj * D]));
             if (stop != n) acc = fadd(acc, fmul(p[n - 1], vn[dim]));
         }
     }
