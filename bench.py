@@ -1,0 +1,370 @@
+"""Benchmark: int8 Qwen2.5-0.5B-architecture decode on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-bs1]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+One JSON line on rank 0. The workload is the batched-decode configuration: 64 independent
+sequences per GPU, each from a 2048-position KV cache of N(0, 1) float32 values, one greedy
+decode step for all of them per timed step (one replay of the captured step graph). Sequences
+are sharded across ranks with no data-path collective ("weak" scaling: per-GPU work fixed);
+torch.distributed (NCCL) is used only for the barrier and the max-over-ranks of the timing.
+
+``value`` is device-timed (CUDA events on the model's stream) with every input resident in
+HBM; ``e2e`` is the same workload through the public decode call with host buffers: each step
+copies that step's input tokens host->device from pinned memory and the step's argmax tokens
+device->host, then synchronizes. At N = 1 a ``bs1`` object adds the batch-1 decode of the
+same model (32-token prompt, then greedy decode up to 1024 positions).
+
+Weights are synthetic (random init, N(0, 0.02), seed 0), int8-quantized on the host by the
+reference's scheme; token ids and caches are seeded. The weights (0.9 GB) and the KV caches
+(3.3 GB per GPU) are larger than L2 (126 MB), so no flush is needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "int8 Qwen2-0.5B decode tok/s (bs1; bs64×1/2/4/8 GPU); % of HBM roofline"
+BATCH = 64            # sequences per GPU (configuration 5)
+PAST = 2048           # cached positions per sequence at the first step
+BS1_PROMPT, BS1_END = 32, 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+# -- plumbing ---------------------------------------------------------------------------------
+
+
+class Dist:
+    """Rank / world from the torchrun environment; NCCL only for barrier and max-reduce."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.torch = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.torch = torch
+
+    def barrier(self):
+        if self.torch is not None:
+            self.torch.distributed.barrier()
+
+    def max(self, value: float) -> float:
+        if self.torch is None:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
+        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj):
+        if self.torch is None:
+            return [obj]
+        out = [None] * self.world
+        self.torch.distributed.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.torch is not None:
+            self.torch.distributed.destroy_process_group()
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def dram_traffic(kind: str, workload: str) -> float | None:
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/traffic.txt)."""
+    path = ROOT / "profiles" / "traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 3 and not line.startswith("#") and parts[0] == workload and parts[1] == kind:
+            return float(parts[2])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of the GPU's clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.gpu)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sms, maxes, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# -- the model ------------------------------------------------------------------------------
+
+
+def build_model(dev: int, slots: int, capacity: int):
+    from nanocompile_b200 import quantize as q
+    from nanocompile_b200 import runtime
+    from nanocompile_b200.qwen2 import QWEN2_0_5B, build_qwen2, quantize, synthetic_weights
+
+    cfg = QWEN2_0_5B
+    weights = synthetic_weights(cfg, seed=0)
+    graph = quantize(build_qwen2(cfg, last_only=True), "int8", keep=("lm_head.weight",))
+    wq = q.quantized_weights(graph, weights)
+    model = runtime.DeviceModel(cfg, wq, "int8", max_rows=BATCH, slots=slots, capacity=capacity, device=dev)
+    return cfg, wq, model
+
+
+def algorithmic_bytes(kind: str, cfg, rows: int, past: int) -> float:
+    """Bytes a launch of `kind` must move at least (weights / cache / activations, once each)."""
+    H, I, d, V = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim, cfg.vocab_size
+    heads, kv = cfg.num_attention_heads, cfg.num_key_value_heads
+    nqkv = (heads + 2 * kv) * d
+    if kind == "lm_head_argmax":
+        return V * H * 4 + rows * H * 4 + rows * V * 4
+    if kind == "attention":
+        return rows * (2 * kv * (past + 1) * d * 4 + nqkv * 4 + heads * d * 1.25)
+    if kind == "down_projection":
+        return H * I + H * 4 + rows * (I * 1.25 + H * 8)
+    if kind == "gate_up_projection":
+        return 2 * I * H + 2 * I * 4 + rows * (H * 4 + I * 1.25)
+    if kind == "qkv_projection":
+        return nqkv * H + nqkv * 8 + rows * (H * 4 + nqkv * 4)
+    if kind == "o_projection":
+        return H * heads * d + H * 4 + rows * (heads * d * 1.25 + H * 8)
+    return 0.0
+
+
+def roofline(profile: dict, cfg, rows: int, past: int, workload: str) -> dict:
+    peak, source = measured_peaks()
+    kind = max(profile, key=lambda k: profile[k][0])
+    total_ms = sum(v[0] for v in profile.values())
+    ms, launches = profile[kind]
+    per_launch_s = ms / 1000.0 / launches
+    alg = algorithmic_bytes(kind, cfg, rows, past)
+    achieved = alg / per_launch_s / 1e9
+    out = {"kernel": kind, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+           "frac": round(achieved / peak, 4), "peak_source": source, "algorithmic_bytes_per_launch": alg,
+           "avg_launch_us": round(per_launch_s * 1e6, 2), "share_of_step": round(ms / total_ms, 3),
+           "traffic": dram_traffic(kind, workload),
+           "kernel_shares": {k: round(v[0] / total_ms, 3) for k, v in sorted(profile.items(), key=lambda x: -x[1][0])}}
+    return out
+
+
+# -- the CPU baseline (test-infrastructure oracle or the reference's own generated C) ----------
+
+
+def cpu_sample(cfg, wq, steps: int, threads: int) -> dict:
+    """Greedy decode of one sequence of the batched workload on the host cores."""
+    from nanocompile_b200.qwen2 import synthetic_cache
+
+    ref = ROOT / "oracle" / "_ref"
+    keys, values, first = synthetic_cache(cfg, 0, PAST)
+    if (ref / "plan.json").exists():
+        from oracle import ref_runner
+
+        model = ref_runner.ReferenceModel(ref, wq, threads=threads)
+        kind = "reference"
+    else:
+        from oracle.oracle import OracleModel
+
+        model = OracleModel(cfg, wq, "int8", threads=threads)
+        kind = "port"
+    model.step([first], keys, values, last_only=True)                # warm (compiles / first touch)
+    started = time.perf_counter()
+    model.greedy([first], steps, past_keys=keys, past_values=values)
+    elapsed = time.perf_counter() - started
+    return {"value": round(steps / elapsed, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+            "sample": f"{steps} greedy decode steps of one sequence of the batched workload (past {PAST}), "
+                      f"sequences run one after another as the reference runs them"}
+
+
+# -- the two arms ------------------------------------------------------------------------------
+
+
+def run_ours(args, dist: Dist) -> dict | None:
+    dev = dist.local
+    capacity = max(PAST, BS1_END) + args.warmup + args.steps + 16
+    cfg, wq, model = build_model(dev, BATCH, capacity)
+    from nanocompile_b200.qwen2 import synthetic_cache
+
+    first, slots, starts = [], list(range(BATCH)), [PAST] * BATCH
+    for b in range(BATCH):
+        k, v, t = synthetic_cache(cfg, dist.rank * BATCH + b, PAST)
+        model.kv_write(b, 0, k, v)
+        first.append(t)
+
+    model.decode(first, slots, starts, args.warmup)                 # warm-up: capture + W replays
+    dist.barrier()
+    with ClockSampler(dev) as clocks:
+        ms = model.decode_timed(first, slots, starts, args.steps)   # K replays, CUDA events
+    dist.barrier()
+    ms_max = dist.max(ms)
+    value = BATCH * dist.world * args.steps / (ms_max / 1000.0)
+
+    # e2e: the public decode call with host buffers, host round trip every step
+    dist.barrier()
+    started = time.perf_counter()
+    model.decode(first, slots, starts, args.steps, per_step=True)
+    e2e_s = dist.max(time.perf_counter() - started)
+    e2e = {"value": round(BATCH * dist.world * args.steps / e2e_s, 1), "unit": "tok/s",
+           "h2d_bytes_per_step": BATCH * 8, "d2h_bytes_per_step": BATCH * 8}
+
+    # per-kernel times for the roofline (eager steps with events around every launch)
+    profile = model.profile(first, slots, starts, 3)
+    launches = sum(n for _, n in profile.values()) // 3 + 1          # + the step-advance kernel
+    roof = roofline(profile, cfg, BATCH, PAST, "bs64")
+    clock_all = dist.gather(clocks.summary())
+
+    bs1 = None
+    if dist.world == 1 and not args.no_bs1:
+        bs1 = run_bs1(cfg, model)
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = cpu_sample(cfg, wq, args.cpu_steps, os.cpu_count() or 1)
+    model.close()
+    if dist.rank != 0:
+        return None
+    return {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"batched greedy decode: {BATCH} sequences per GPU, each from a {PAST}-position "
+                                   f"N(0,1) KV cache (configuration 5), one decode step of all per timed step",
+                       "model": "Qwen2.5-0.5B architecture, random init N(0,0.02) seed 0, int8-vnni projections, "
+                                "fp32 tied LM head", "global_batch": BATCH * dist.world, "past": PAST,
+                       "parallelism": f"dp{dist.world} (independent sequences, no collective)",
+                       "l2": "inputs larger than L2 (weights 0.9 GB, KV cache 3.3 GB per GPU); no flush"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "clocks": clock_all[0] | {"per_rank": clock_all if dist.world > 1 else None},
+            "gpu_launches": launches * args.steps, "bs1": bs1}
+
+
+def run_bs1(cfg, model) -> dict:
+    """Configuration 3 on slot 0: 32-token prompt, then greedy decode up to 1024 positions."""
+    from nanocompile_b200.qwen2 import synthetic_prompt
+
+    prompt = synthetic_prompt(cfg.vocab_size, BS1_PROMPT)
+    _, tok = model.step(prompt, [0] * BS1_PROMPT, list(range(BS1_PROMPT)), [BS1_PROMPT - 1], want_logits=False)
+    first = int(tok[0])
+    steps = BS1_END - BS1_PROMPT
+    model.decode([first], [0], [BS1_PROMPT], 8)                         # warm-up / capture
+    with ClockSampler(model.device) as clocks:
+        ms = model.decode_timed([first], [0], [BS1_PROMPT], steps)
+    profile = model.profile([first], [0], [512], 4)
+    return {"value": round(steps / (ms / 1000.0), 1), "unit": "tok/s", "ms_per_token": round(ms / steps, 4),
+            "workload": f"batch 1: {BS1_PROMPT}-token prompt, then {steps} greedy decode steps (past "
+                        f"{BS1_PROMPT}..{BS1_END - 1}) (configuration 3)",
+            "roofline": roofline(profile, cfg, 1, 512, "bs1"), "clocks": clocks.summary()}
+
+
+def run_reference(args, dist: Dist) -> dict | None:
+    """The reference's CPU implementation of the path (rank 0 only), on this arm's metric."""
+    if dist.rank != 0:
+        return None
+    from nanocompile_b200 import quantize as q
+    from nanocompile_b200.qwen2 import QWEN2_0_5B, build_qwen2, quantize, synthetic_weights
+
+    cfg = QWEN2_0_5B
+    graph = quantize(build_qwen2(cfg, last_only=True), "int8", keep=("lm_head.weight",))
+    wq = q.quantized_weights(graph, synthetic_weights(cfg, seed=0))
+    threads = os.cpu_count() or 1
+    for _ in range(max(args.warmup, 0)):
+        pass
+    base = cpu_sample(cfg, wq, max(args.steps, 1), threads)
+    return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"batched greedy decode from {PAST}-position N(0,1) KV caches (configuration 5), "
+                                   f"sequences decoded one after another on the host",
+                       "model": "Qwen2.5-0.5B architecture, random init N(0,0.02) seed 0, int8-vnni"},
+            "cpu_baseline": base, "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=64)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--no-bs1", action="store_true", help="skip the batch-1 measurement")
+    parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    parser.add_argument("--cpu-steps", type=int, default=8)
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    dist = Dist()
+    try:
+        line = run_reference(args, dist) if args.impl == "reference" else run_ours(args, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

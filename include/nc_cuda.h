@@ -172,18 +172,26 @@ int32_t nc_qwen2_step(nc_model *model, int32_t rows, const int64_t *ids, const i
  * starts from token first[b] at position start[b] of slot[b].  Each step is one replay of a
  * captured CUDA graph; the argmax feeds the next step on the device.  tokens (host)
  * [steps, batch]; logits (host, nullable) [batch, vocab] of the last step.
- * Per-step streaming: with per_step != 0 every step copies its tokens to the host and
- * synchronizes (the host-visible path); otherwise one copy at the end. */
+ * With per_step != 0 the host is in the loop: every step copies its input tokens host -> device
+ * from pinned memory, replays the graph, copies the step's argmax back and synchronizes;
+ * otherwise the argmax feeds the next step on the device and the tokens come back once. */
 int32_t nc_qwen2_decode(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
                         const int32_t *start, int32_t steps, int32_t per_step, int64_t *tokens,
                         float *logits);
 
-/* Timing hook for benchmarks: runs `steps` replays of the captured decode graph for the
- * current device-side state, timed with CUDA events on the model's stream; *ms gets the
- * elapsed milliseconds.  Also reports the average duration of the LM-head kernel and the
- * i8 GEMV of the last replay window (nullable). */
+/* Timing hook for benchmarks: runs `steps` replays of the captured decode graph from the given
+ * state, timed with CUDA events on the model's stream; *ms gets the elapsed milliseconds. */
 int32_t nc_qwen2_decode_timed(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
                               const int32_t *start, int32_t steps, float *ms);
+
+/* Kernel-time probe: runs `steps` decode steps eagerly (not as a graph) with CUDA events around
+ * every launch, and sums the milliseconds and launches per fused-group kind into the
+ * [NC_KINDS] arrays (kinds: 0 gather, 1 q/k/v projection, 2 attention, 3 o projection,
+ * 4 gate/up projection, 5 down projection, 6 rms_norm row kernel, 7 block quantization,
+ * 8 LM head + argmax). */
+#define NC_KINDS 9
+int32_t nc_qwen2_profile(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
+                         const int32_t *start, int32_t steps, float *ms_per_kind, int32_t *launches_per_kind);
 
 #ifdef __cplusplus
 }

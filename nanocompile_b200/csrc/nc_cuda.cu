@@ -502,13 +502,51 @@ struct nc_model {
     unsigned long long *err = nullptr;
     unsigned int *counter = nullptr;
     int history_steps = 0;
+    int64_t *pinned = nullptr;      // host staging [2][max_rows] for the per-step decode mode
 
     std::map<int, cudaGraphExec_t> decode_graphs;   // by batch size
+
+    // kernel-time probe: CUDA events around every launch of an eager step, by fused-group kind
+    bool probing = false;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> probe_marks;
+    std::vector<cudaEvent_t> event_pool;
+    size_t event_next = 0;
+};
+
+enum ProbeKind : int {
+    K_GATHER = 0, K_QKV = 1, K_ATTENTION = 2, K_O = 3, K_GATE_UP = 4, K_DOWN = 5, K_NORM = 6, K_QUANT = 7,
+    K_LM_HEAD = 8, K_KINDS = 9
 };
 
 namespace {
 
 int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+cudaEvent_t probe_event(nc_model *m) {
+    if (m->event_next == m->event_pool.size()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        m->event_pool.push_back(e);
+    }
+    return m->event_pool[m->event_next++];
+}
+
+// Brackets one launch with events when the model is probing (eager steps only).
+struct Probe {
+    nc_model *m;
+    int kind;
+    cudaEvent_t end = nullptr;
+    Probe(nc_model *model, int k) : m(model), kind(k) {
+        if (!m->probing) return;
+        cudaEvent_t begin = probe_event(m);
+        end = probe_event(m);
+        cudaEventRecord(begin, m->stream);
+        m->probe_marks.push_back({kind, {begin, end}});
+    }
+    ~Probe() {
+        if (end) cudaEventRecord(end, m->stream);
+    }
+};
 
 // Arena layout: a bump allocator over one cudaMalloc, 256-byte aligned pieces.
 struct Layout {
@@ -538,8 +576,11 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
     const bool norm_fused = rows <= PRO_NORM_ROWS && H <= 8 * CHUNK;
     const bool attn_quant = q8 && d % QBLOCK == 0;
 
-    CUDA_TRY(launch_k(gather_kernel, rows, 256, 0, st, m->x, m->ids, m->embed, m->err, c.vocab, H));
-    NC_TRY(check_launch("gather_kernel"));
+    {
+        Probe pr(m, K_GATHER);
+        CUDA_TRY(launch_k(gather_kernel, rows, 256, 0, st, m->x, m->ids, m->embed, m->err, c.vocab, H));
+        NC_TRY(check_launch("gather_kernel"));
+    }
 
     for (int l = 0; l < (int)c.layers; ++l) {
         const nc_model::Layer &L = m->layers[l];
@@ -550,9 +591,14 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
             f.g.scales = L.sqkv; f.g.bias = L.bqkv; f.g.m = rows; f.g.n = Nqkv; f.g.k = H;
             if (norm_fused) {
                 f.x = m->x; f.norm_w = L.in_norm; f.eps = c.eps;
+                Probe pr(m, K_QKV);
                 NC_TRY(launch_i8_fused(st, f, PRO_NORM, EPI_BIAS));
             } else {
-                NC_TRY(launch_norm(st, nullptr, m->x, L.in_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
+                {
+                    Probe pr(m, K_NORM);
+                    NC_TRY(launch_norm(st, nullptr, m->x, L.in_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
+                }
+                Probe pr(m, K_QKV);
                 NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_BIAS));
             }
         } else {
@@ -570,6 +616,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
         if (attn_quant) { at.q_out = m->xq; at.xs_out = m->xs; at.bsums_out = m->bsums; }
         if (fused) {
             at.mode = 0;
+            Probe pr(m, K_ATTENTION);
             NC_TRY(launch_attention(st, at, rows));
         } else {
             at.mode = 1;
@@ -584,6 +631,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
             f.g.residual = m->x; f.g.m = rows; f.g.n = H; f.g.k = Hq;
             if (attn_quant) {
                 f.bsums_in = m->bsums;
+                Probe pr(m, K_O);
                 NC_TRY(launch_i8_fused(st, f, PRO_OFFSET, EPI_RESIDUAL));
             } else {
                 NC_TRY(launch_quant(st, m->xq, m->ctx, m->xs, m->off, nullptr, rows, Hq));
@@ -602,14 +650,20 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
             f.q_out = m->hq; f.xs_out = m->hxs; f.bsums_out = m->bsums;
             if (norm_fused) {
                 f.x = m->x; f.norm_w = L.post_norm; f.eps = c.eps;
+                Probe pr(m, K_GATE_UP);
                 NC_TRY(launch_i8_fused(st, f, PRO_NORM, EPI_SWIGLU_QUANT));
             } else {
-                NC_TRY(launch_norm(st, nullptr, m->x, L.post_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
+                {
+                    Probe pr(m, K_NORM);
+                    NC_TRY(launch_norm(st, nullptr, m->x, L.post_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
+                }
+                Probe pr(m, K_GATE_UP);
                 NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_SWIGLU_QUANT));
             }
             FusedI8Args b{};
             b.g.out = m->x; b.g.xq = m->hq; b.g.xs = m->hxs; b.g.w = L.wd; b.g.scales = L.sd;
             b.g.residual = m->x; b.g.m = rows; b.g.n = H; b.g.k = I; b.bsums_in = m->bsums;
+            Probe pr(m, K_DOWN);
             NC_TRY(launch_i8_fused(st, b, PRO_OFFSET, EPI_RESIDUAL));
         } else {
             NC_TRY(launch_norm(st, m->normed, m->x, L.post_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
@@ -622,11 +676,15 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
         }
     }
     // final norm of the rows that need logits, then the tied LM head with the argmax
-    NC_TRY(launch_norm(st, m->normed, m->x, m->final_norm, nullptr, nullptr, nullptr, nullptr, m->logit_row,
-                       logit_rows, H, c.eps));
+    {
+        Probe pr(m, K_NORM);
+        NC_TRY(launch_norm(st, m->normed, m->x, m->final_norm, nullptr, nullptr, nullptr, nullptr, m->logit_row,
+                           logit_rows, H, c.eps));
+    }
     GemvF32Args a{};
     a.out = m->logits; a.x = m->normed; a.w = m->embed; a.m = logit_rows; a.n = (int)c.vocab; a.k = H;
     a.part_val = m->part_val; a.part_idx = m->part_idx; a.counter = m->counter; a.tokens = m->tokens;
+    Probe pr(m, K_LM_HEAD);
     NC_TRY(launch_f32(st, a, EPI_NONE, true));
     return NC_OK;
 }
@@ -781,6 +839,8 @@ extern "C" int32_t nc_qwen2_destroy(nc_model *m) {
     if (!m) return NC_OK;
     cudaSetDevice(m->dev);
     for (auto &g : m->decode_graphs) cudaGraphExecDestroy(g.second);
+    for (auto e : m->event_pool) cudaEventDestroy(e);
+    if (m->pinned) cudaFreeHost(m->pinned);
     if (m->arena) cudaFree(m->arena);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -979,18 +1039,57 @@ extern "C" int32_t nc_qwen2_decode(nc_model *m, int32_t batch, const int32_t *sl
     cudaGraphExec_t graph;
     NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
     cudaStream_t st = m->stream;
-    for (int s = 0; s < steps; ++s) {
-        CUDA_TRY(cudaGraphLaunch(graph, st));
-        if (per_step && tokens) {
-            CUDA_TRY(cudaMemcpyAsync(tokens + (int64_t)s * batch, m->tokens, batch * 8, cudaMemcpyDeviceToHost, st));
+    if (per_step) {
+        // the host in the loop: each step's input tokens go host -> device from pinned memory,
+        // its argmax comes back, and the host waits for it
+        if (!m->pinned) CUDA_TRY(cudaHostAlloc((void **)&m->pinned, 2 * sizeof(int64_t) * m->c.max_rows, 0));
+        int64_t *in = m->pinned, *out = m->pinned + m->c.max_rows;
+        std::memcpy(in, first, batch * sizeof(int64_t));
+        for (int s = 0; s < steps; ++s) {
+            CUDA_TRY(cudaMemcpyAsync(m->ids, in, batch * 8, cudaMemcpyHostToDevice, st));
+            CUDA_TRY(cudaGraphLaunch(graph, st));
+            CUDA_TRY(cudaMemcpyAsync(out, m->tokens, batch * 8, cudaMemcpyDeviceToHost, st));
             CUDA_TRY(cudaStreamSynchronize(st));
+            if (tokens) std::memcpy(tokens + (int64_t)s * batch, out, batch * sizeof(int64_t));
+            std::memcpy(in, out, batch * sizeof(int64_t));
         }
+    } else {
+        for (int s = 0; s < steps; ++s) CUDA_TRY(cudaGraphLaunch(graph, st));
     }
     if (!per_step && tokens && steps)
         CUDA_TRY(cudaMemcpyAsync(tokens, m->history, (size_t)steps * batch * 8, cudaMemcpyDeviceToHost, st));
     if (logits && steps)
         CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaStreamSynchronize(st));
+    return NC_OK;
+}
+
+extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
+                                    const int32_t *start, int32_t steps, float *ms_per_kind, int32_t *launches_per_kind) {
+    cudaGraphExec_t graph;
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
+    for (int k = 0; k < K_KINDS; ++k) {
+        ms_per_kind[k] = 0.0f;
+        launches_per_kind[k] = 0;
+    }
+    cudaStream_t st = m->stream;
+    for (int s = 0; s < steps; ++s) {
+        m->probing = true;
+        m->event_next = 0;
+        m->probe_marks.clear();
+        int32_t status = enqueue_step(m, batch, batch, true);
+        m->probing = false;
+        NC_TRY(status);
+        if (launch_k(advance_kernel, 1, 1024, 0, st, m->ids, m->pos, m->tokens, m->history, m->step, batch) != cudaSuccess)
+            return fail(NC_ERR_CUDA, "launching advance_kernel");
+        CUDA_TRY(cudaStreamSynchronize(st));
+        for (auto &pm : m->probe_marks) {
+            float ms = 0.0f;
+            CUDA_TRY(cudaEventElapsedTime(&ms, pm.second.first, pm.second.second));
+            ms_per_kind[pm.first] += ms;
+            launches_per_kind[pm.first] += 1;
+        }
+    }
     return NC_OK;
 }
 

@@ -96,6 +96,8 @@ def library() -> ctypes.CDLL:
         L.nc_qwen2_step.argtypes = [_vp, _i32, _P64, _P32, _P32, _i32, _P32, _PF, _P64, _P32]
         L.nc_qwen2_decode.argtypes = [_vp, _i32, _P32, _P64, _P32, _i32, _i32, _P64, _PF]
         L.nc_qwen2_decode_timed.argtypes = [_vp, _i32, _P32, _P64, _P32, _i32, _PF]
+        L.nc_qwen2_profile.argtypes = [_vp, _i32, _P32, _P64, _P32, _i32, _PF, _P32]
+        L.nc_qwen2_profile.restype = _i32
         for fn in ("nc_device_count", "nc_set_device", "nc_device_alloc", "nc_device_free", "nc_copy_to_device",
                    "nc_copy_to_host", "nc_pack_int8_weights", "nc_qwen2_create", "nc_qwen2_destroy",
                    "nc_qwen2_upload", "nc_qwen2_missing_weights", "nc_qwen2_kv_write", "nc_qwen2_kv_read",
@@ -228,6 +230,22 @@ class DeviceModel:
         check(library().nc_qwen2_decode(self._h, first.size, _p(slot, _P32), _p(first, _P64), _p(start, _P32), steps,
                                         1 if per_step else 0, _p(tokens, _P64), _p(logits, _PF)))
         return tokens, logits
+
+    KINDS = ("gather", "qkv_projection", "attention", "o_projection", "gate_up_projection", "down_projection",
+             "rms_norm", "block_quantize", "lm_head_argmax")
+
+    def profile(self, first: Sequence[int], slot: Sequence[int], start: Sequence[int], steps: int
+                ) -> dict[str, tuple[float, int]]:
+        """Per fused-group kind: (total milliseconds, launches) over ``steps`` eager steps with a
+        CUDA event pair around every launch."""
+        first = np.ascontiguousarray(first, np.int64)
+        slot = np.ascontiguousarray(slot, np.int32)
+        start = np.ascontiguousarray(start, np.int32)
+        ms = np.zeros(len(self.KINDS), np.float32)
+        n = np.zeros(len(self.KINDS), np.int32)
+        check(library().nc_qwen2_profile(self._h, first.size, _p(slot, _P32), _p(first, _P64), _p(start, _P32), steps,
+                                         _p(ms, _PF), _p(n, _P32)))
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KINDS) if n[i]}
 
     def decode_timed(self, first: Sequence[int], slot: Sequence[int], start: Sequence[int], steps: int) -> float:
         """Milliseconds for ``steps`` graph replays, timed with CUDA events on the model's stream."""
