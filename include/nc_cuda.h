@@ -101,6 +101,19 @@ int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream);
 int32_t nc_lm_head_argmax(void **p, const int64_t *s, void *stream);
 int64_t nc_lm_head_scratch_bytes(int64_t rows, int64_t vocab);
 
+/* nc_lm_head_argmax for callers that cannot allocate device memory (a host that fixes this
+ * library's memory budget, another thread capturing a graph in global capture mode, a loop that
+ * cannot take an allocation's implicit synchronization).  No counterpart in the reference: its
+ * CPU kernels never needed device scratch.  Same p[] as nc_lm_head_argmax without p[4]: the
+ * scratch is a static device array of the library, so nothing is allocated, ever.
+ *  - Limit: rows * ceil(vocab / 128) <= 32768 (e.g. 27 rows of a 151,936-token vocabulary);
+ *    larger calls fail with NC_ERR_ARGUMENT and a message.
+ *  - The first call on each device looks the array's address up (cudaGetSymbolAddress, with
+ *    that device current); make that first call before any stream capture.
+ *  - Every call shares the array: calls that overlap on the GPU (other streams, other host
+ *    threads) race.  Each call clears the finish counter on its stream before the kernel. */
+int32_t nc_lm_head_argmax_noalloc(void **p, const int64_t *s, void *stream);
+
 /* Decode attention over a KV cache (calls 14-17 with RoPE calls 9-13 fused in): for one new
  * token per row, bias is already in qkv; RoPE q and k, append k/v to the cache at the row's
  * position, scores in index order, softmax (NaN-propagating max, in-order sum of expf),

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <set>
 #include <string>
 #include <vector>
@@ -1109,4 +1110,69 @@ extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32
     cudaEventDestroy(a);
     cudaEventDestroy(b);
     return NC_OK;
+}
+
+// ---- the LM head + argmax without any allocation ---------------------------------------------
+// Some callers cannot call cudaMalloc: a host that gives this library a fixed device-memory
+// budget and forbids allocations it did not make, code that runs while another thread captures
+// a CUDA graph in global capture mode (an allocation there breaks the capture), or a latency-
+// critical loop that cannot afford an allocation's implicit synchronization.  For them the
+// LM head's scratch (a finish counter and one (value, index) pair per row and CTA) lives in
+// this file-scope device array instead of caller-provided memory.  Every GPU that loads the
+// library holds it until the process exits.
+constexpr int64_t NOALLOC_PARTIALS = 32768;    // rows * ceil(vocab / 128) at most
+constexpr size_t NOALLOC_SCRATCH_BYTES = 256 + NOALLOC_PARTIALS * (sizeof(float) + sizeof(int32_t));
+static __device__ __align__(256) unsigned char g_lm_head_scratch[NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// The array's device address, looked up once per device with that device current.  In host
+// code g_lm_head_scratch names a host-side stand-in, not device memory.
+constexpr int NOALLOC_MAX_DEVICES = 64;
+void *g_scratch_addr[NOALLOC_MAX_DEVICES] = {};
+std::mutex g_scratch_mutex;
+
+int32_t noalloc_scratch(void **out) {
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(NC_ERR_ARGUMENT, "device %d beyond the scratch table", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+        void *p = nullptr;
+        CUDA_TRY(cudaGetSymbolAddress(&p, g_lm_head_scratch));
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return NC_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t nc_lm_head_argmax_noalloc(void **p, const int64_t *s, void *stream) {
+    const int64_t rows = s[0], vocab = s[1], hidden = s[2];
+    if (rows <= 0 || vocab <= 0) return NC_OK;
+    const int64_t partials = rows * ((vocab + F32_ROWS - 1) / F32_ROWS);
+    if (partials > NOALLOC_PARTIALS)
+        return fail(NC_ERR_ARGUMENT,
+                    "nc_lm_head_argmax_noalloc: %lld rows of a %lld-token vocabulary need %lld partial results; the "
+                    "static scratch holds %lld (rows * ceil(vocab / 128) <= %lld)",
+                    (long long)rows, (long long)vocab, (long long)partials, (long long)NOALLOC_PARTIALS,
+                    (long long)NOALLOC_PARTIALS);
+    if (hidden % F32_TILE) return fail(NC_ERR_ARGUMENT, "hidden %lld is not a multiple of %d", (long long)hidden, F32_TILE);
+    void *scratch = nullptr;
+    NC_TRY(noalloc_scratch(&scratch));
+    // the finish counter must start at zero (a call that failed midway could leave it set)
+    CUDA_TRY(cudaMemsetAsync(scratch, 0, 256, (cudaStream_t)stream));
+    GemvF32Args a{};
+    a.out = (float *)p[0];
+    a.x = (const float *)p[1];
+    a.w = (const float *)p[2];
+    a.tokens = (int64_t *)p[3];
+    a.m = (int)rows;
+    a.n = (int)vocab;
+    a.k = (int)hidden;
+    a.counter = (unsigned int *)scratch;
+    a.part_val = (float *)((char *)scratch + 256);
+    a.part_idx = (int32_t *)((char *)scratch + 256 + partials * sizeof(float));
+    return launch_f32((cudaStream_t)stream, a, EPI_NONE, a.tokens != nullptr);
 }

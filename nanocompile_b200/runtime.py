@@ -70,7 +70,8 @@ def library() -> ctypes.CDLL:
         L.nc_last_error.argtypes = [ctypes.c_char_p, _i64]
         L.nc_last_error.restype = _i32
         for name in ("nc_gather_rows", "nc_rms_norm_quantize", "nc_quantize_blocks", "nc_matmul_i8_vnni",
-                     "nc_matmul_f32", "nc_lm_head_argmax", "nc_attention", "nc_expf_exact"):
+                     "nc_matmul_f32", "nc_lm_head_argmax", "nc_lm_head_argmax_noalloc", "nc_attention",
+                     "nc_expf_exact"):
             fn = getattr(L, name)
             fn.argtypes = [ctypes.POINTER(_vp), _P64, _vp]
             fn.restype = _i32
