@@ -36,6 +36,8 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from nanocompile_b200.shard import RankGroup, rank_sequences  # noqa: E402
+
 METRIC = "int8 Qwen2-0.5B decode tok/s (bs1; bs64×1/2/4/8 GPU); % of HBM roofline"
 BATCH = 64            # sequences per GPU (configuration 5)
 PAST = 2048           # cached positions per sequence at the first step
@@ -44,48 +46,6 @@ FALLBACK_HBM_GBS = 6650.0
 
 
 # -- plumbing ---------------------------------------------------------------------------------
-
-
-class Dist:
-    """Rank / world from the torchrun environment; NCCL only for barrier and max-reduce."""
-
-    def __init__(self):
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
-        self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.torch = None
-        if self.world > 1:
-            import datetime
-
-            import torch
-            import torch.distributed as dist
-
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
-            self.torch = torch
-
-    def barrier(self):
-        if self.torch is not None:
-            self.torch.distributed.barrier()
-
-    def max(self, value: float) -> float:
-        if self.torch is None:
-            return value
-        t = self.torch.tensor([value], dtype=self.torch.float64, device="cuda")
-        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
-        return float(t.item())
-
-    def gather(self, obj):
-        if self.torch is None:
-            return [obj]
-        out = [None] * self.world
-        self.torch.distributed.all_gather_object(out, obj)
-        return out
-
-    def close(self):
-        if self.torch is not None:
-            self.torch.distributed.destroy_process_group()
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -217,8 +177,9 @@ def roofline(profile: dict, cfg, rows: int, past: int, workload: str) -> dict:
 # -- the CPU baseline (test-infrastructure oracle or the reference's own generated C) ----------
 
 
-def cpu_sample(cfg, wq, steps: int, threads: int) -> dict:
-    """Greedy decode of one sequence of the batched workload on the host cores."""
+def cpu_sample(cfg, wq, steps: int, threads: int, warmup: int = 1) -> dict:
+    """Greedy decode of one sequence of the batched workload on the host cores (``warmup``
+    untimed steps first)."""
     from nanocompile_b200.qwen2 import synthetic_cache
 
     ref = ROOT / "oracle" / "_ref"
@@ -233,7 +194,8 @@ def cpu_sample(cfg, wq, steps: int, threads: int) -> dict:
 
         model = OracleModel(cfg, wq, "int8", threads=threads)
         kind = "port"
-    model.step([first], keys, values, last_only=True)                # warm (compiles / first touch)
+    for _ in range(max(warmup, 1)):                                   # warm (first touch, packed weights)
+        model.step([first], keys, values, last_only=True)
     started = time.perf_counter()
     model.greedy([first], steps, past_keys=keys, past_values=values)
     elapsed = time.perf_counter() - started
@@ -245,15 +207,15 @@ def cpu_sample(cfg, wq, steps: int, threads: int) -> dict:
 # -- the two arms ------------------------------------------------------------------------------
 
 
-def run_ours(args, dist: Dist) -> dict | None:
+def run_ours(args, dist: RankGroup) -> dict | None:
     dev = dist.local
     capacity = max(PAST, BS1_END) + args.warmup + args.steps + 16
     cfg, wq, model = build_model(dev, BATCH, capacity)
     from nanocompile_b200.qwen2 import synthetic_cache
 
     first, slots, starts = [], list(range(BATCH)), [PAST] * BATCH
-    for b in range(BATCH):
-        k, v, t = synthetic_cache(cfg, dist.rank * BATCH + b, PAST)
+    for b, sequence in enumerate(rank_sequences(dist.rank, dist.world, BATCH)):
+        k, v, t = synthetic_cache(cfg, sequence, PAST)
         model.kv_write(b, 0, k, v)
         first.append(t)
 
@@ -320,9 +282,11 @@ def run_bs1(cfg, model) -> dict:
             "roofline": roofline(profile, cfg, 1, 512, "bs1"), "clocks": clocks.summary()}
 
 
-def run_reference(args, dist: Dist) -> dict | None:
-    """The reference's CPU implementation of the path (rank 0 only), on this arm's metric."""
-    if dist.rank != 0:
+def run_reference(args) -> dict | None:
+    """The reference's CPU implementation of the path, on this arm's metric. Under torchrun only
+    rank 0 works and prints; the other ranks exit at once (no process group is made)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
         return None
     from nanocompile_b200 import quantize as q
     from nanocompile_b200.qwen2 import QWEN2_0_5B, build_qwen2, quantize, synthetic_weights
@@ -331,10 +295,8 @@ def run_reference(args, dist: Dist) -> dict | None:
     graph = quantize(build_qwen2(cfg, last_only=True), "int8", keep=("lm_head.weight",))
     wq = q.quantized_weights(graph, synthetic_weights(cfg, seed=0))
     threads = os.cpu_count() or 1
-    for _ in range(max(args.warmup, 0)):
-        pass
-    base = cpu_sample(cfg, wq, max(args.steps, 1), threads)
-    return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": dist.world,
+    base = cpu_sample(cfg, wq, max(args.steps, 1), threads, warmup=args.warmup)
+    return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"batched greedy decode from {PAST}-position N(0,1) KV caches (configuration 5), "
@@ -356,9 +318,14 @@ def main() -> int:
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    dist = Dist()
+    if args.impl == "reference":
+        line = run_reference(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    dist = RankGroup("nccl")
     try:
-        line = run_reference(args, dist) if args.impl == "reference" else run_ours(args, dist)
+        line = run_ours(args, dist)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:
