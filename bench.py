@@ -170,7 +170,8 @@ def roofline(profile: dict, cfg, rows: int, past: int, workload: str) -> dict:
            "frac": round(achieved / peak, 4), "peak_source": source, "algorithmic_bytes_per_launch": alg,
            "avg_launch_us": round(per_launch_s * 1e6, 2), "share_of_step": round(ms / total_ms, 3),
            "traffic": dram_traffic(kind, workload),
-           "kernel_shares": {k: round(v[0] / total_ms, 3) for k, v in sorted(profile.items(), key=lambda x: -x[1][0])}}
+           "kernel_shares": {k: round(v[0] / total_ms, 3) for k, v in sorted(profile.items(), key=lambda x: -x[1][0])},
+           "kernel_us": {k: round(v[0] * 1000.0 / v[1], 2) for k, v in sorted(profile.items(), key=lambda x: -x[1][0])}}
     return out
 
 
@@ -315,7 +316,10 @@ def main() -> int:
     parser.add_argument("--no-bs1", action="store_true", help="skip the batch-1 measurement")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     parser.add_argument("--cpu-steps", type=int, default=8)
+    parser.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (profiling runs only)")
+    parser.add_argument("--past", type=int, default=PAST, help="cached positions at the first step (profiling runs only)")
     args = parser.parse_args()
+    globals().update(BATCH=args.batch, PAST=args.past)
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":

@@ -7,7 +7,7 @@
 // same fixed sequence of fused kernels reading its sizes from device memory, and decode
 // steps replay one captured CUDA graph.
 #include "../../include/nc_cuda.h"
-#include "nc_kernels.cuh"
+#include "nc_gemm_i8.cuh"
 
 #include <cmath>
 #include <cstdarg>
@@ -217,14 +217,53 @@ int32_t launch_fused_pro(cudaStream_t st, const FusedI8Args &f, int pro, int epi
     return launch_fused_pro_g<LPR, NCH, 3>(st, f, pro, epi, smem);
 }
 
-// The int8-vnni projection: weights-stationary, lanes per row chosen by shape (a row's slices
-// must fit in registers: up to 8 chunks of 16 or 8 bytes per lane, or 40 chunks of 4 bytes).
+// Batched projection (more than four rows): R rows x T tokens per warp, 8 warps per CTA.
+template <int R, int T, int MAXG, int PRO, int EPI>
+int32_t launch_gemm_t(cudaStream_t st, const FusedI8Args &f) {
+    constexpr int ROWS = GEMM_WARPS * R;
+    auto kernel = gemm_i8_kernel<R, T, MAXG, PRO, EPI>;
+    const size_t smem = gemm_i8_smem(T, ROWS, f.g.k, PRO == PRO_OFFSET, EPI == EPI_SWIGLU_QUANT);
+    if (smem > 200 * 1024) return fail(NC_ERR_ARGUMENT, "int8 width %d too wide for the batched projection", f.g.k);
+    CUDA_TRY(allow_smem(kernel, smem));
+    const dim3 grid((f.g.n + ROWS - 1) / ROWS, (f.g.m + T - 1) / T);
+    CUDA_TRY(launch_k(kernel, grid, GEMM_WARPS * 32, smem, st, f));
+    return check_launch("gemm_i8_kernel");
+}
+
+template <int MAXG, int PRO>
+int32_t launch_gemm_epi(cudaStream_t st, const FusedI8Args &f, int epi) {
+    switch (epi) {
+        case EPI_NONE: return launch_gemm_t<4, 8, MAXG, PRO, EPI_NONE>(st, f);
+        case EPI_BIAS: return launch_gemm_t<4, 8, MAXG, PRO, EPI_BIAS>(st, f);
+        case EPI_RESIDUAL: return launch_gemm_t<4, 8, MAXG, PRO, EPI_RESIDUAL>(st, f);
+        case EPI_SWIGLU: return launch_gemm_t<4, 4, MAXG, PRO, EPI_SWIGLU>(st, f);
+        case EPI_SWIGLU_QUANT: return launch_gemm_t<4, 4, MAXG, PRO, EPI_SWIGLU_QUANT>(st, f);
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+}
+
+template <int MAXG>
+int32_t launch_gemm_pro(cudaStream_t st, const FusedI8Args &f, int pro, int epi) {
+    switch (pro) {
+        case PRO_NONE: return launch_gemm_epi<MAXG, PRO_NONE>(st, f, epi);
+        case PRO_OFFSET: return launch_gemm_epi<MAXG, PRO_OFFSET>(st, f, epi);
+        default: return fail(NC_ERR_ARGUMENT, "prologue %d is not a batched one", pro);
+    }
+}
+
+// The int8-vnni projection. More than four rows: the batched kernel. Otherwise
+// weights-stationary, lanes per row chosen by shape (a row's slices must fit in registers: up
+// to 8 chunks of 16 or 8 bytes per lane, or 40 chunks of 4 bytes).
 int32_t launch_i8_fused(cudaStream_t st, const FusedI8Args &f, int pro, int epi) {
     const GemvI8Args &a = f.g;
     if (a.m <= 0 || a.n <= 0) return NC_OK;
     if (a.k % QBLOCK) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a whole number of 32-blocks", a.k);
     if (pro == PRO_NORM && a.m > PRO_NORM_ROWS) return fail(NC_ERR_ARGUMENT, "the norm prologue takes up to 4 rows");
     if (epi == EPI_SWIGLU_QUANT && a.n % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized output width %d", a.n);
+    if (pro != PRO_NORM && a.m > PRO_NORM_ROWS) {
+        if (a.k % CHUNK == 0) return launch_gemm_pro<0>(st, f, pro, epi);
+        return launch_gemm_pro<3>(st, f, pro, epi);
+    }
     const int blocks = a.k / QBLOCK, bl4 = (blocks + 3) & ~3, chunks = a.k / CHUNK;
     if (a.k % 16) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a multiple of 16", a.k);
     const int tile = pro == PRO_NORM ? PRO_NORM_ROWS : std::min(a.m, act_tile_tokens(a.k));
