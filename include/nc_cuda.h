@@ -125,6 +125,16 @@ int32_t nc_lm_head_argmax_noalloc(void **p, const int64_t *s, void *stream);
  *    attention scale as float32 bits */
 int32_t nc_attention(void **p, const int64_t *s, void *stream);
 
+/* nc_attention for a cache whose extent is known: s[8] = slots in the cache (p[2] holds
+ * s[8] * slot stride floats).  More than eight rows then stream K/V chunks by TMA from a tensor
+ * map over the cache (head dims that are multiples of 32).  Same reference interface as
+ * nc_attention. */
+int32_t nc_attention_cache(void **p, const int64_t *s, void *stream);
+
+/* NC_ERR_KERNEL if a kernel recorded a device-side fault since the last call (a TMA stage of
+ * the grouped attention kernel that did not arrive within its bounded wait); clears it. */
+int32_t nc_device_faults(void);
+
 /* int8 weights as the kernels read them: u8 = int8 + 128 (one XOR per byte). */
 int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t bytes);
 

@@ -1,0 +1,432 @@
+// Grouped decode attention for batches (more than eight rows): one CTA per (row, KV head) with
+// all G query heads of its group (repeat_kv, nanocompile/nn.py:109-120).
+//
+// The arithmetic is attention_kernel's, which follows nanocompile/models/qwen2.py:143-150 and
+// nanocompile/nn.py:57-66 step for step: RoPE of q and the new k, scores acc = acc + q*k over d in
+// order, t = score * scale + 0, NaN-propagating max, in-order sum of expf(t - max),
+// p = expf(t - max) / sum, ctx = in-order sum over positions of p * v.
+//
+// What changes is the data movement, built for many rows sharing the GPU:
+//  * K and V chunks stream through a ring of shared-memory stages by TMA: a chunk is D/32 tensor
+//    copies of 128 rows x 128 bytes from one 2-D tensor map over the whole KV arena, with 128-byte
+//    swizzling, completion counted in bytes on an mbarrier. Many chunks are in flight per SM at no
+//    instruction cost, and the swizzle lets a thread read one whole K row without bank conflicts.
+//    Where no tensor map can describe the cache (its extent is not known, or the head dimension is
+//    not a multiple of 32) the same kernel stages by cp.async: per thread eight 16-byte copies per
+//    chunk at offsets computed once, K pieces XOR-swizzled by row.
+//  * 512 threads (16 warps) per CTA: every phase is a chain of dependent float operations, and
+//    warps are what hides their latency.
+//  * Scores: two threads per position of a 256-row chunk (four heads each), the K row in
+//    registers once, the four heads' dot products interleaved (q broadcast from shared memory).
+//  * Probabilities are kept head-major ([8][cap]): the in-order sums read them contiguously and a
+//    P.V thread -- one dimension, two heads, two chains -- reads four positions of a head with one
+//    broadcast load; V is read through offsets precomputed for the eight swizzle phases.
+//  * The division by the softmax sum is a reciprocal multiply with a residual check that proves
+//    the correctly rounded quotient (fdiv_recip), the IEEE divide where it cannot.
+#pragma once
+
+#include <cuda.h>
+
+#include "nc_kernels.cuh"
+
+namespace nc {
+
+__device__ unsigned int g_attention_fault;     // set when a TMA stage never completed (bounded wait)
+
+constexpr int ATB_THREADS = 512;
+constexpr int ATB_CHUNK = 256;     // positions per stage; two scoring threads per position
+constexpr int ATB_STAGES = 2;
+constexpr int ATB_HEADS = 8;       // query heads per CTA at most
+
+constexpr int ATB_BOX = 32;        // floats per 128-byte swizzled TMA box row
+
+__host__ __device__ constexpr int atb_cap4(int cap) { return (cap + 3) & ~3; }
+
+// Dynamic shared memory: 1 KB of alignment slack (128-byte swizzled TMA boxes start on 1 KB
+// boundaries), the ring, probabilities [8][cap4], q [8][D], new k and v.
+__host__ __device__ inline size_t attention_batched_smem(int d, int cap) {
+    return 1024 + sizeof(float) * ((size_t)ATB_STAGES * ATB_CHUNK * d + (size_t)ATB_HEADS * atb_cap4(cap) +
+                                   (size_t)(ATB_HEADS + 2) * d);
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Bounded: gives up after 2^31 SM cycles (about a second).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity) {
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - start > (1ll << 31)) return false;
+    return true;
+}
+// One 2-D tile of the tensor map (x = column, y = row) into shared memory, counted on bar.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// In-order sum of p[0], p[stride], p[2*stride], ... (n terms), one thread; the next eight loads
+// are issued before the current eight dependent adds.
+__device__ __forceinline__ float chain_sum_strided(const float *p, int n, int stride) {
+    float acc = 0.0f, a[8], b[8];
+    int j = 0;
+    const int n8 = n & ~7;
+    if (n8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a[u] = p[u * stride];
+        for (; j < n8; j += 8) {
+            if (j + 8 < n8) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) b[u] = p[(j + 8 + u) * stride];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = fadd(acc, a[u]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) a[u] = b[u];
+        }
+    }
+    for (; j < n; ++j) acc = fadd(acc, p[j * stride]);
+    return acc;
+}
+
+// Logical piece c (16 bytes) of row `row` of a staged K chunk, and element `dim` of a V row.
+template <int D, bool TMA>
+__device__ __forceinline__ float4 staged_piece(const float *stage, int row, int c) {
+    if constexpr (TMA) {
+        const int b = c / (ATB_BOX / 4), u = c % (ATB_BOX / 4);
+        return *reinterpret_cast<const float4 *>(stage + b * ATB_CHUNK * ATB_BOX + row * ATB_BOX + ((u ^ (row & 7)) << 2));
+    } else {
+        return reinterpret_cast<const float4 *>(stage)[row * (D / 4) + (c ^ (row % (D / 4)))];
+    }
+}
+template <int D, bool TMA>
+__device__ __forceinline__ float staged_elem(const float *stage, int row, int dim) {
+    if constexpr (TMA) {
+        const int b = dim / ATB_BOX, col = dim % ATB_BOX;
+        return stage[b * ATB_CHUNK * ATB_BOX + row * ATB_BOX + ((((col >> 2) ^ (row & 7)) << 2) | (col & 3))];
+    } else {
+        return stage[row * D + dim];
+    }
+}
+
+template <int D, int G, bool TMA>
+__global__ void __launch_bounds__(ATB_THREADS, 1)
+attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap kvmap) {
+    static_assert(G >= 2 && G <= ATB_HEADS, "group of 2..8 query heads");
+    static_assert(D % 4 == 0 && D <= 128, "head dim");
+    static_assert(!TMA || D % ATB_BOX == 0, "TMA staging takes 32-float boxes");
+    constexpr int PPR = D / 4, HALF = D / 2;
+    constexpr int NP = ATB_CHUNK * PPR / ATB_THREADS; // cp.async: 16-byte pieces a thread copies per chunk
+    static_assert(ATB_THREADS % PPR == 0 && NP >= 1, "piece layout");
+    constexpr int STAGE = ATB_CHUNK * D;              // floats per stage
+    constexpr int SH = 4;                             // heads per scoring thread (two threads per position)
+    constexpr int PV_THREADS = D * ATB_HEADS / 2;     // P.V: (dimension, head pair)
+    extern __shared__ __align__(16) unsigned char smraw[];
+    __shared__ uint64_t bars[ATB_STAGES];
+    __shared__ uint64_t tab[32];
+    __shared__ float s_max[ATB_HEADS], s_sum[ATB_HEADS], s_rcp[ATB_HEADS];
+    __shared__ float wmax[ATB_THREADS / 32][SH];
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    release_dependents();
+    wait_for_producer();
+
+    const int r = blockIdx.x / a.kv, g = blockIdx.x % a.kv, h0 = g * G;
+    const int pos = a.pos[r], len = pos + 1, slot = a.slot[r], cap4 = atb_cap4(a.cap);
+    float *ring = reinterpret_cast<float *>(smraw + ((1024 - (smem_addr(smraw) & 1023)) & 1023));   // [STAGES][STAGE]
+    float *e = ring + ATB_STAGES * STAGE;                         // [8][cap4]
+    float *q = e + ATB_HEADS * cap4;                              // [8][D], heads past G zero
+    float *kn = q + ATB_HEADS * D, *vn = kn + D;
+    if (t < 32) tab[t] = kExpTab[t];
+    if (TMA && t == 0) {
+        for (int s = 0; s < ATB_STAGES; ++s) mbar_init(&bars[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kvmap)) : "memory");
+    }
+
+    float *base = a.cache + (int64_t)slot * a.slot_stride;
+    float *K = base + (int64_t)g * a.cap * D;
+    float *V = base + ((int64_t)a.kv + g) * a.cap * D;
+    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
+    const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
+    // RoPE of the group's q heads (rows past G zero) and of the new k; the new v
+    for (int i = t; i < (ATB_HEADS + 2) * D; i += ATB_THREADS) {
+        const int h = i / D, c = i % D;
+        if (h < ATB_HEADS && h >= G) {
+            q[h * D + c] = 0.0f;
+            continue;
+        }
+        const float *src = h < ATB_HEADS ? qkv + (h0 + h) * D
+                                         : (h == ATB_HEADS ? qkv + (a.heads + g) * D : qkv + (a.heads + a.kv + g) * D);
+        if (h == ATB_HEADS + 1) {
+            vn[c] = src[c];
+            continue;
+        }
+        const float t1 = src[c];
+        const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
+        const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
+        if (h < ATB_HEADS) q[h * D + c] = v;
+        else kn[c] = v;
+    }
+    __syncthreads();
+    if (a.mode != 2) {
+        for (int c = t; c < D; c += ATB_THREADS) {
+            K[(int64_t)pos * D + c] = kn[c];
+            V[(int64_t)pos * D + c] = vn[c];
+        }
+        if (a.mode == 1) return;
+    }
+    const bool own_new = a.mode == 0;    // position pos comes from kn / vn, not the cache
+
+    // The ring sequence: K chunks 0..nk-1, then V chunks 0..nk-1.
+    const int nk = (len + ATB_CHUNK - 1) / ATB_CHUNK;
+    const int64_t krow0 = a.cache_row0 + (int64_t)slot * (a.slot_stride / D) + (int64_t)g * a.cap;
+    const int64_t vrow0 = krow0 + (int64_t)a.kv * a.cap;
+    // cp.async: thread t copies column t % PPR of rows t / PPR + i * (THREADS / PPR); K pieces go
+    // to column col ^ (row % PPR) (the rows of one thread agree modulo PPR).
+    const int pcol = t % PPR, prow0 = t / PPR;
+    const int kcol = pcol ^ (prow0 % PPR);
+    int next = 0;                                   // next ring index to issue
+    auto issue = [&](int idx) {
+        if constexpr (TMA) {
+            if (t == 0 && idx < 2 * nk) {
+                const bool is_k = idx < nk;
+                const int j0 = (is_k ? idx : idx - nk) * ATB_CHUNK;
+                float *dst = ring + (idx % ATB_STAGES) * STAGE;
+                uint64_t *bar = &bars[idx % ATB_STAGES];
+                mbar_expect_tx(bar, (unsigned)(STAGE * sizeof(float)));
+#pragma unroll
+                for (int b = 0; b < D / ATB_BOX; ++b)
+                    tma_load_2d(dst + b * ATB_CHUNK * ATB_BOX, &kvmap, b * ATB_BOX, (int)((is_k ? krow0 : vrow0) + j0), bar);
+            }
+        } else {
+            if (idx < 2 * nk) {
+                const bool is_k = idx < nk;
+                const int j0 = (is_k ? idx : idx - nk) * ATB_CHUNK;
+                const float *src = (is_k ? K : V) + (int64_t)(j0 + prow0) * D + pcol * 4;
+                float4 *dst = reinterpret_cast<float4 *>(ring + (idx % ATB_STAGES) * STAGE) + prow0 * PPR + (is_k ? kcol : pcol);
+#pragma unroll
+                for (int i = 0; i < NP; ++i) {
+                    const int row = prow0 + i * (ATB_THREADS / PPR);
+                    if (j0 + row < len) cp_async16(dst + i * (ATB_THREADS / PPR) * PPR, src + (int64_t)i * (ATB_THREADS / PPR) * D);
+                }
+            }
+            cp_async_commit();
+        }
+        next = idx + 1;
+    };
+    auto ready = [&](int idx) -> bool {
+        if constexpr (TMA) return mbar_wait_bounded(&bars[idx % ATB_STAGES], (unsigned)((idx / ATB_STAGES) & 1));
+        cp_async_wait<ATB_STAGES - 2>();
+        return true;
+    };
+    for (int i = 0; i < ATB_STAGES - 1; ++i) issue(i);
+
+    // ---- scores: thread (position of the chunk, half of the 8 head rows), four chains ----
+    const int srow = t % ATB_CHUNK, hb = (t / ATB_CHUNK) * SH;
+    float mx[SH];
+#pragma unroll
+    for (int h = 0; h < SH; ++h) mx[h] = __uint_as_float(0xff800000u);
+    int failed_at = -1;
+    for (int ci = 0; ci < nk; ++ci) {
+        const bool ok = ready(ci);
+        if (__syncthreads_or(!ok)) { failed_at = ci; break; }
+        issue(ci + ATB_STAGES - 1);
+        const int j = ci * ATB_CHUNK + srow;
+        if (j < len) {
+            float4 kr[PPR];
+            if (own_new && j == pos) {
+#pragma unroll
+                for (int c = 0; c < PPR; ++c) kr[c] = reinterpret_cast<const float4 *>(kn)[c];
+            } else {
+                const float *st = ring + (ci % ATB_STAGES) * STAGE;
+#pragma unroll
+                for (int c = 0; c < PPR; ++c) kr[c] = staged_piece<D, TMA>(st, srow, c);
+            }
+            float acc[SH];
+#pragma unroll
+            for (int h = 0; h < SH; ++h) acc[h] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < PPR; ++c) {
+#pragma unroll
+                for (int h = 0; h < SH; ++h) {
+                    const float4 x = reinterpret_cast<const float4 *>(q + (hb + h) * D)[c];
+                    acc[h] = fadd(acc[h], fmul(x.x, kr[c].x));
+                    acc[h] = fadd(acc[h], fmul(x.y, kr[c].y));
+                    acc[h] = fadd(acc[h], fmul(x.z, kr[c].z));
+                    acc[h] = fadd(acc[h], fmul(x.w, kr[c].w));
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < SH; ++h) {
+                const float sc = fadd(fmul(acc[h], a.scale), 0.0f);
+                e[(hb + h) * cap4 + j] = sc;
+                mx[h] = nan_max(mx[h], sc);
+            }
+        }
+    }
+    if (failed_at >= 0) goto fault;
+    {
+        // per-head maxima: warps 0..7 hold heads 0..3, warps 8..15 heads 4..7
+#pragma unroll
+        for (int h = 0; h < SH; ++h) {
+            const float m = warp_nan_max(mx[h]);
+            if (lane == 0) wmax[warp][h] = m;
+        }
+        __syncthreads();
+        constexpr int WPH = ATB_CHUNK / 32;
+        if (t < G) {
+            const int w0 = (t / SH) * WPH, h = t % SH;
+            float m = wmax[w0][h];
+            for (int w = 1; w < WPH; ++w) m = nan_max(m, wmax[w0 + w][h]);
+            s_max[t] = m;
+        }
+        __syncthreads();
+        // exps, four independent positions per thread in flight
+        for (int h = 0; h < G; ++h) {
+            const float mh = s_max[h];
+            float *eh = e + h * cap4;
+            for (int j = 4 * t; j < len; j += 4 * ATB_THREADS) {
+                float4 v = *reinterpret_cast<float4 *>(eh + j);
+                v.x = expf_exact(fsub(v.x, mh), tab);
+                v.y = expf_exact(fsub(v.y, mh), tab);
+                v.z = expf_exact(fsub(v.z, mh), tab);
+                v.w = expf_exact(fsub(v.w, mh), tab);
+                *reinterpret_cast<float4 *>(eh + j) = v;      // positions past len are never read
+            }
+        }
+        __syncthreads();
+        if (t < G) {
+            const float sum = chain_sum(e + t * cap4, len);      // the in-order sums
+            s_sum[t] = sum;
+            s_rcp[t] = __frcp_rn(sum);
+        }
+        __syncthreads();
+        for (int h = 0; h < G; ++h) {
+            const float sh = s_sum[h], rh = s_rcp[h];
+            float *eh = e + h * cap4;
+            for (int j = 4 * t; j < len; j += 4 * ATB_THREADS) {
+                float4 v = *reinterpret_cast<float4 *>(eh + j);
+                v.x = fdiv_recip(v.x, sh, rh);
+                v.y = fdiv_recip(v.y, sh, rh);
+                v.z = fdiv_recip(v.z, sh, rh);
+                v.w = fdiv_recip(v.w, sh, rh);
+                *reinterpret_cast<float4 *>(eh + j) = v;
+            }
+        }
+    }
+    {
+        // ---- probabilities @ V: thread (dimension, head pair), positions in order ----
+        const bool pv = t < PV_THREADS;
+        const int dim = t % D, hp = 2 * (t / D);
+        const float *p0 = e + min(hp, G - 1) * cap4, *p1 = e + min(hp + 1, G - 1) * cap4;   // past G: discarded
+        // where row k (mod 8) of a staged V chunk keeps this thread's dimension
+        int voff[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if constexpr (TMA) {
+                const int col = dim % ATB_BOX;
+                voff[k] = (dim / ATB_BOX) * ATB_CHUNK * ATB_BOX + k * ATB_BOX + ((((col >> 2) ^ k) << 2) | (col & 3));
+            } else {
+                voff[k] = k * D + dim;
+            }
+        }
+        constexpr int VROW8 = TMA ? 8 * ATB_BOX : 8 * D;  // floats from row j to row j + 8 (same box)
+        float acc0 = 0.0f, acc1 = 0.0f;
+        for (int ci = 0; ci < nk; ++ci) {
+            const int idx = nk + ci;
+            const bool ok = ready(idx);
+            if (__syncthreads_or(!ok)) { failed_at = idx; break; }
+            issue(idx + ATB_STAGES - 1);
+            if (pv) {
+                const float *st = ring + (idx % ATB_STAGES) * STAGE;
+                const int j0 = ci * ATB_CHUNK;
+                const int n = min(ATB_CHUNK, len - j0);
+                const int stop = (own_new && ci == nk - 1) ? n - 1 : n;   // the new row comes from vn
+                int jj = 0;
+                for (; jj + 8 <= stop; jj += 8) {
+                    const float4 a0 = *reinterpret_cast<const float4 *>(p0 + j0 + jj);
+                    const float4 a1 = *reinterpret_cast<const float4 *>(p0 + j0 + jj + 4);
+                    const float4 b0 = *reinterpret_cast<const float4 *>(p1 + j0 + jj);
+                    const float4 b1 = *reinterpret_cast<const float4 *>(p1 + j0 + jj + 4);
+                    const float *vr = st + (jj / 8) * VROW8;
+                    float v[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) v[k] = vr[voff[k]];
+                    const float pa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const float pb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        acc0 = fadd(acc0, fmul(pa[k], v[k]));
+                        acc1 = fadd(acc1, fmul(pb[k], v[k]));
+                    }
+                }
+                for (; jj < stop; ++jj) {
+                    const float v = staged_elem<D, TMA>(st, jj, dim);
+                    acc0 = fadd(acc0, fmul(p0[j0 + jj], v));
+                    acc1 = fadd(acc1, fmul(p1[j0 + jj], v));
+                }
+                if (stop != n) {
+                    acc0 = fadd(acc0, fmul(p0[j0 + n - 1], vn[dim]));
+                    acc1 = fadd(acc1, fmul(p1[j0 + n - 1], vn[dim]));
+                }
+            }
+        }
+        if (failed_at >= 0) goto fault;
+        if (!TMA) cp_async_wait<0>();
+        // ---- outputs: ctx, or the block quantization of o_proj's input ----
+        const int width = a.heads * D;
+        __syncthreads();
+        if (pv) {
+            if (hp < G) {
+                if (a.ctx) a.ctx[(int64_t)r * width + (h0 + hp) * D + dim] = acc0;
+                q[hp * D + dim] = acc0;
+            }
+            if (hp + 1 < G) {
+                if (a.ctx) a.ctx[(int64_t)r * width + (h0 + hp + 1) * D + dim] = acc1;
+                q[(hp + 1) * D + dim] = acc1;
+            }
+        }
+        if (a.q_out) {
+            __syncthreads();
+            for (int w = warp; w < G * D / QBLOCK; w += ATB_THREADS / 32) {
+                int8_t qv;
+                int bs;
+                const float sc = quantize_block_warp(q[w * QBLOCK + lane], &qv, &bs);
+                const int col = h0 * D + w * QBLOCK;
+                a.q_out[(int64_t)r * width + col + lane] = qv;
+                if (lane == 0) {
+                    a.xs_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = sc;
+                    a.bsums_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = bs;
+                }
+            }
+        }
+        return;
+    }
+fault:
+    // a TMA stage never completed: record it, let the copies in flight land (bounded), leave
+    if (t == 0) {
+        atomicOr(&g_attention_fault, 1u);
+        for (int idx = failed_at; idx < min(next, 2 * nk); ++idx) ready(idx);
+    }
+}
+
+}  // namespace nc

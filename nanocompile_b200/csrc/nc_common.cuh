@@ -132,6 +132,27 @@ __device__ __forceinline__ float div127(float mag) {
     return __fmaf_rn(r, y, q0);
 }
 __device__ __forceinline__ float block_scale(float mag) { return (mag <= 0.0f) ? 1.0f : div127(mag); }
+
+// a / b, correctly rounded, for many a over one b > 0 (softmax's division by the sum), given
+// y = RN(1/b): q = RN(a*y) corrected once by its residual (Markstein), and accepted only when
+// the residual a - b*q -- exact, because q is within an ulp of a/b -- proves q nearest:
+// |a - b*q| < b * ulp(q)/2 (ulp(q)/4 at a power of two, where the spacing below halves).
+// Anything else (huge or tiny quotients, NaN, an undecided residual) takes the IEEE divide.
+// The fallback is a call so the compiler cannot hoist the IEEE divide into the common path.
+__device__ __noinline__ float fdiv_slow(float a, float b) { return __fdiv_rn(a, b); }
+
+__device__ __forceinline__ float fdiv_recip(float a, float b, float y) {
+    const float q0 = fmul(a, y);
+    const float q = __fmaf_rn(__fmaf_rn(-b, q0, a), y, q0);
+    const uint32_t uq = __float_as_uint(q) & 0x7fffffffu;
+    if (uq >= 0x0d800000u && uq < 0x71800000u) {            // 2^-100 <= |q| < 2^100
+        const float r = __fmaf_rn(-b, q, a);
+        const float half_ulp = __uint_as_float((uq & 0x7f800000u) - (24u << 23));
+        const float lim = fmul(b, (uq & 0x7fffffu) ? half_ulp : fmul(half_ulp, 0.5f));
+        if (fabsf(r) < lim) return q;
+    }
+    return fdiv_slow(a, b);
+}
 // xq = (int8)clamp(roundf(v / scale), -127, 127).  Only the rounded integer is kept, so the
 // quotient may come from the fast approximate divide (error <= 2 ulp, |v / scale| <= 128): the
 // rounding can only differ from IEEE division's when the quotient is within 2 ulp of a

@@ -7,6 +7,7 @@
 // same fixed sequence of fused kernels reading its sizes from device memory, and decode
 // steps replay one captured CUDA graph.
 #include "../../include/nc_cuda.h"
+#include "nc_attention.cuh"
 #include "nc_gemm_i8.cuh"
 
 #include <cmath>
@@ -336,12 +337,83 @@ int32_t launch_attention_g(cudaStream_t st, const AttnArgs &a, int rows) {
     return check_launch("attention_kernel");
 }
 
+// A 2-D tensor map over a KV arena seen as rows of d floats (rows < 2^31): 128-row x 32-float
+// boxes, 128-byte swizzle. cuTensorMapEncodeTiled comes from the driver through the runtime.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int32_t make_kv_map(CUtensorMap *map, float *base, int64_t rows, int d) {
+    static EncodeTiledFn encode = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(fn);
+    }();
+    if (!encode) return fail(NC_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (rows <= 0 || rows >= (int64_t(1) << 31) || d % ATB_BOX || ((uintptr_t)base & 15))
+        return fail(NC_ERR_ARGUMENT, "no tensor map for %lld rows of %d floats", (long long)rows, d);
+    const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)d * sizeof(float)};
+    const cuuint32_t box[2] = {ATB_BOX, ATB_CHUNK};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, elem,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return NC_OK;
+}
+
+template <int D, int G, bool TMA>
+int32_t launch_attention_batched(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap &map) {
+    auto kernel = attention_batched_kernel<D, G, TMA>;
+    const size_t smem = attention_batched_smem(D, a.cap);
+    CUDA_TRY(allow_smem(kernel, smem));
+    CUDA_TRY(launch_k(kernel, rows * a.kv, ATB_THREADS, smem, st, a, map));
+    return check_launch("attention_batched_kernel");
+}
+
+template <int D, bool TMA>
+int32_t launch_attention_group(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap &map, bool *done) {
+    *done = true;
+    switch (a.heads / a.kv) {
+        case 2: return launch_attention_batched<D, 2, TMA>(st, a, rows, map);
+        case 4: return launch_attention_batched<D, 4, TMA>(st, a, rows, map);
+        case 7: return launch_attention_batched<D, 7, TMA>(st, a, rows, map);
+        case 8: return launch_attention_batched<D, 8, TMA>(st, a, rows, map);
+        default: *done = false; return NC_OK;
+    }
+}
+
+// Many rows: one CTA per (row, KV head) with its whole group, while its shared memory (a
+// probability per cached position and head) fits; K/V by TMA when a tensor map describes the
+// cache, by cp.async otherwise.
+template <int D>
+int32_t launch_attention_grouped(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap *map, bool *done) {
+    *done = false;
+    if constexpr (D == 16 || D == 64) {
+        if (attention_batched_smem(D, a.cap) > 225 * 1024) return NC_OK;
+        if constexpr (D % ATB_BOX == 0) {
+            if (map) return launch_attention_group<D, true>(st, a, rows, *map, done);
+        }
+        CUtensorMap none;
+        std::memset(&none, 0, sizeof(none));
+        return launch_attention_group<D, false>(st, a, rows, none, done);
+    }
+    return NC_OK;
+}
+
 // Few rows (decode of a handful of sequences): one CTA per query head, for parallelism.  Many
 // rows: one CTA per KV head, reading each KV row once for its group of query heads.
 template <int D>
-int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows) {
+int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap *map) {
     const int group = a.heads / a.kv;
     if (rows <= 8 || group == 1) return launch_attention_g<D, 1>(st, a, rows);
+    bool done;
+    const int32_t s = launch_attention_grouped<D>(st, a, rows, map, &done);
+    if (done || s != NC_OK) return s;
     switch (group) {
         case 2: return launch_attention_g<D, 2>(st, a, rows);
         case 4: return launch_attention_g<D, 4>(st, a, rows);
@@ -351,7 +423,8 @@ int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows) {
     }
 }
 
-int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
+// map: a tensor map over the KV arena that holds a.cache (a.cache_row0 its row), or null.
+int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap *map = nullptr) {
     if (rows <= 0) return NC_OK;
     const int group = a.heads / a.kv;
     if (a.heads % a.kv || group > ATTN_MAX_GROUP || group * a.d > attention_threads(group))
@@ -359,11 +432,24 @@ int32_t launch_attention(cudaStream_t st, const AttnArgs &a, int rows) {
                     a.kv, a.d);
     if (a.q_out && a.d % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized attention output needs whole blocks");
     switch (a.d) {
-        case 16: return launch_attention_d<16>(st, a, rows);
-        case 64: return launch_attention_d<64>(st, a, rows);
-        case 128: return launch_attention_d<128>(st, a, rows);
+        case 16: return launch_attention_d<16>(st, a, rows, map);
+        case 64: return launch_attention_d<64>(st, a, rows, map);
+        case 128: return launch_attention_d<128>(st, a, rows, map);
         default: return fail(NC_ERR_ARGUMENT, "head dim %d unsupported (16, 64, 128)", a.d);
     }
+}
+
+// A grouped-attention CTA whose TMA stage never completed (bounded wait) records it in
+// g_attention_fault; the host reads and clears the flag after a step.
+int32_t check_device_faults() {
+    unsigned int fault = 0;
+    CUDA_TRY(cudaMemcpyFromSymbol(&fault, g_attention_fault, sizeof(fault)));
+    if (fault) {
+        const unsigned int zero = 0;
+        CUDA_TRY(cudaMemcpyToSymbol(g_attention_fault, &zero, sizeof(zero)));
+        return fail(NC_ERR_KERNEL, "attention: a K/V stage did not arrive within its wait limit");
+    }
+    return NC_OK;
 }
 
 float f32_from_bits(int64_t bits) {
@@ -475,6 +561,36 @@ extern "C" int32_t nc_attention(void **p, const int64_t *s, void *stream) {
     return launch_attention((cudaStream_t)stream, a, rows);
 }
 
+extern "C" int32_t nc_attention_cache(void **p, const int64_t *s, void *stream) {
+    AttnArgs a{};
+    a.ctx = (float *)p[0];
+    a.qkv = (const float *)p[1];
+    a.cache = (float *)p[2];
+    a.cos_tab = (const float *)p[3];
+    a.sin_tab = (const float *)p[4];
+    a.slot = (const int32_t *)p[5];
+    a.pos = (const int32_t *)p[6];
+    const int rows = (int)s[0];
+    a.heads = (int)s[1];
+    a.kv = (int)s[2];
+    a.d = (int)s[3];
+    a.cap = (int)s[4];
+    a.slot_stride = s[5];
+    a.mode = s[6] ? 0 : 2;
+    a.scale = f32_from_bits(s[7]);
+    const int64_t slots = s[8];
+    if (slots <= 0 || a.d <= 0 || a.slot_stride % a.d) return fail(NC_ERR_ARGUMENT, "bad cache extent");
+    CUtensorMap map;
+    if (a.d % ATB_BOX == 0 && slots * (a.slot_stride / a.d) < (int64_t(1) << 31)) {
+        NC_TRY(make_kv_map(&map, a.cache, slots * (a.slot_stride / a.d), a.d));
+        a.cache_row0 = 0;
+        return launch_attention((cudaStream_t)stream, a, rows, &map);
+    }
+    return launch_attention((cudaStream_t)stream, a, rows);
+}
+
+extern "C" int32_t nc_device_faults(void) { return check_device_faults(); }
+
 extern "C" int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t bytes) {
     CUDA_TRY(cudaMemcpy(dst_device, src_host, (size_t)bytes, cudaMemcpyHostToDevice));
     xor80_kernel<<<1024, 256>>>((uint8_t *)dst_device, bytes);
@@ -530,6 +646,8 @@ struct nc_model {
     std::vector<Layer> layers;
     float *kv = nullptr;            // [slot][layer][2][kv][cap][d]
     int64_t slot_stride = 0, layer_stride = 0;
+    CUtensorMap kv_map;             // the whole KV arena as rows of d floats (has_kv_map)
+    bool has_kv_map = false;
 
     // activations and step state
     float *x = nullptr, *normed = nullptr, *xs = nullptr, *off = nullptr, *qkv = nullptr, *ctx = nullptr,
@@ -652,17 +770,18 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
         at.ctx = attn_quant ? nullptr : m->ctx; at.qkv = m->qkv; at.cache = m->kv + (int64_t)l * m->layer_stride;
         at.cos_tab = m->cos_tab; at.sin_tab = m->sin_tab; at.slot = m->slot; at.pos = m->pos;
         at.slot_stride = m->slot_stride; at.heads = (int)c.heads; at.kv = (int)c.kv_heads; at.d = d;
+        at.cache_row0 = (int64_t)l * m->layer_stride / d;
         at.cap = c.capacity; at.scale = c.attn_scale;
         if (attn_quant) { at.q_out = m->xq; at.xs_out = m->xs; at.bsums_out = m->bsums; }
         if (fused) {
             at.mode = 0;
             Probe pr(m, K_ATTENTION);
-            NC_TRY(launch_attention(st, at, rows));
+            NC_TRY(launch_attention(st, at, rows, m->has_kv_map ? &m->kv_map : nullptr));
         } else {
             at.mode = 1;
-            NC_TRY(launch_attention(st, at, rows));
+            NC_TRY(launch_attention(st, at, rows, m->has_kv_map ? &m->kv_map : nullptr));
             at.mode = 2;
-            NC_TRY(launch_attention(st, at, rows));
+            NC_TRY(launch_attention(st, at, rows, m->has_kv_map ? &m->kv_map : nullptr));
         }
         // o_proj with the residual add
         if (q8) {
@@ -817,6 +936,10 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     m->arena = (char *)base;
     for (auto &pc : lay.pieces) *pc.first = m->arena + pc.second;
     CUDA_TRY(cudaMemsetAsync(m->arena, 0, (size_t)lay.top, m->stream));
+    // the KV arena as one tensor of rows for the grouped attention kernel's TMA loads
+    const int64_t kv_rows = c.slots * m->slot_stride / d;
+    if (d % ATB_BOX == 0 && kv_rows < (int64_t(1) << 31))
+        m->has_kv_map = make_kv_map(&m->kv_map, m->kv, kv_rows, (int)d) == NC_OK;
 
     // RoPE tables: angle = float(position) * inv_freq[i] (nanocompile/nn.py:78-94), evaluated with
     // the C library's cosf/sinf -- the functions the reference's generated C calls for them.
@@ -1010,7 +1133,7 @@ extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, 
         return fail(NC_ERR_KERNEL, "gather index %lld is outside 0..%lld", (long long)ids[err],
                     (long long)(m->c.vocab - 1));
     }
-    return NC_OK;
+    return check_device_faults();
 }
 
 static int32_t decode_graph(nc_model *m, int batch, cudaGraphExec_t *out) {
@@ -1101,7 +1224,7 @@ extern "C" int32_t nc_qwen2_decode(nc_model *m, int32_t batch, const int32_t *sl
     if (logits && steps)
         CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaStreamSynchronize(st));
-    return NC_OK;
+    return check_device_faults();
 }
 
 extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
@@ -1130,7 +1253,7 @@ extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *s
             launches_per_kind[pm.first] += 1;
         }
     }
-    return NC_OK;
+    return check_device_faults();
 }
 
 extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
@@ -1148,7 +1271,7 @@ extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32
     CUDA_TRY(cudaEventElapsedTime(ms, a, b));
     cudaEventDestroy(a);
     cudaEventDestroy(b);
-    return NC_OK;
+    return check_device_faults();
 }
 
 // ---- the LM head + argmax without any allocation ---------------------------------------------

@@ -787,6 +787,7 @@ struct AttnArgs {
     int8_t *q_out;             // nullable: block-quantize ctx (d % 32 == 0) into xq / xs / block sums
     float *xs_out;
     int32_t *bsums_out;
+    int64_t cache_row0;        // grouped kernel with a tensor map: the map's row of cache[0]
 };
 
 constexpr int ATTN_CHUNK = 128;      // positions per staged K or V chunk

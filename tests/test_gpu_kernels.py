@@ -192,25 +192,29 @@ def rope_np(t1, cos, sin):
     return (t1 * np.concatenate([cos, cos])) + (rot * np.concatenate([sin, sin]))
 
 
+# Up to eight rows: one CTA per query head. More: the grouped kernel (bulk-copied K/V stages).
 @pytest.mark.parametrize("rows,past,heads,kv,d", [(1, 0, 14, 2, 64), (1, 1024, 14, 2, 64), (3, 37, 4, 2, 16),
-                                                  (2, 2048, 14, 2, 64)])
-def test_decode_attention(cuda, rows, past, heads, kv, d):
+                                                  (2, 2048, 14, 2, 64), (12, 300, 14, 2, 64), (9, 0, 14, 2, 64),
+                                                  (10, 127, 8, 1, 64), (16, 129, 4, 2, 16), (9, 2100, 14, 2, 64)])
+@pytest.mark.parametrize("entry", ["nc_attention", "nc_attention_cache"])   # the second: K/V by TMA
+def test_decode_attention(cuda, rows, past, heads, kv, d, entry):
     rng = np.random.default_rng(past + rows)
-    cap = past + 8
+    cap = past + 37 * rows + 8
     n_qkv = (heads + 2 * kv) * d
     qkv = rng.standard_normal((rows, n_qkv)).astype(np.float32)
     cache = rng.standard_normal((rows, 2, kv, cap, d)).astype(np.float32)
     inv = (1.0 / (1e6 ** (np.arange(0, d, 2) / d))).astype(np.float32)
-    pos = np.array([past + r for r in range(rows)], np.int32)     # one sequence per row
+    pos = np.array([past + 37 * r for r in range(rows)], np.int32)   # one sequence per row, ragged lengths
     table_pos = np.arange(cap, dtype=np.float32)[:, None] * inv[None, :]
     cos, sin = oracle.cosf_libm(table_pos), oracle.sinf_libm(table_pos)
     slot = np.arange(rows, dtype=np.int32)
     scale = np.float32(d ** -0.5)
     dctx = DeviceArray(cuda, shape=(rows, heads * d), dtype=np.float32)
     dcache = DeviceArray(cuda, cache)
-    call(cuda, "nc_attention", [dctx, DeviceArray(cuda, qkv), dcache, DeviceArray(cuda, cos), DeviceArray(cuda, sin),
-                                DeviceArray(cuda, slot), DeviceArray(cuda, pos)],
-         [rows, heads, kv, d, cap, 2 * kv * cap * d, 1, f32_bits(scale)])
+    call(cuda, entry, [dctx, DeviceArray(cuda, qkv), dcache, DeviceArray(cuda, cos), DeviceArray(cuda, sin),
+                       DeviceArray(cuda, slot), DeviceArray(cuda, pos)],
+         [rows, heads, kv, d, cap, 2 * kv * cap * d, 1, f32_bits(scale), rows])
+    assert cuda.library().nc_device_faults() == 0
     got_ctx, got_cache = dctx.numpy(), dcache.numpy()
     for r in range(rows):
         p = pos[r]
@@ -223,6 +227,34 @@ def test_decode_attention(cuda, rows, past, heads, kv, d):
         assert same_bits(got_cache[r, 0, :, p], kr) and same_bits(got_cache[r, 1, :, p], vv)
         out, _ = oracle.attention_decode(qr, keys, values, heads, kv, p + 1, scale)
         assert same_bits(got_ctx[r], out.reshape(-1))
+
+
+@pytest.mark.parametrize("rows,heads,kv,d", [(3, 14, 2, 64), (11, 14, 2, 64), (12, 4, 2, 16)])
+@pytest.mark.parametrize("entry", ["nc_attention", "nc_attention_cache"])
+def test_attention_over_the_cache_only(cuda, rows, heads, kv, d, entry):
+    """The prompt path's second pass (mode 2): every position, the row's own included, from the cache."""
+    rng = np.random.default_rng(rows + d)
+    cap = 64 * rows + 8
+    qkv = rng.standard_normal((rows, (heads + 2 * kv) * d)).astype(np.float32)
+    cache = rng.standard_normal((rows, 2, kv, cap, d)).astype(np.float32)
+    inv = (1.0 / (1e6 ** (np.arange(0, d, 2) / d))).astype(np.float32)
+    pos = np.array([61 * r + 5 for r in range(rows)], np.int32)
+    table_pos = np.arange(cap, dtype=np.float32)[:, None] * inv[None, :]
+    cos, sin = oracle.cosf_libm(table_pos), oracle.sinf_libm(table_pos)
+    scale = np.float32(d ** -0.5)
+    dctx = DeviceArray(cuda, shape=(rows, heads * d), dtype=np.float32)
+    dcache = DeviceArray(cuda, cache)
+    call(cuda, entry, [dctx, DeviceArray(cuda, qkv), dcache, DeviceArray(cuda, cos), DeviceArray(cuda, sin),
+                       DeviceArray(cuda, np.arange(rows, dtype=np.int32)), DeviceArray(cuda, pos)],
+         [rows, heads, kv, d, cap, 2 * kv * cap * d, 0, f32_bits(scale), rows])
+    assert cuda.library().nc_device_faults() == 0
+    got = dctx.numpy()
+    assert same_bits(dcache.numpy(), cache)                          # nothing appended
+    for r in range(rows):
+        p = pos[r]
+        qr = rope_np(qkv[r].reshape(heads + 2 * kv, d)[:heads], cos[p], sin[p])
+        out, _ = oracle.attention_decode(qr, cache[r, 0], cache[r, 1], heads, kv, p + 1, scale)
+        assert same_bits(got[r], out.reshape(-1))
 
 
 def test_gather_reports_the_first_bad_row(cuda):
