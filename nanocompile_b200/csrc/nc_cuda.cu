@@ -8,6 +8,7 @@
 // steps replay one captured CUDA graph.
 #include "../../include/nc_cuda.h"
 #include "nc_attention.cuh"
+#include "nc_gemm_f32.cuh"
 #include "nc_gemm_i8.cuh"
 
 #include <cmath>
@@ -312,10 +313,34 @@ int32_t launch_f32_tok(cudaStream_t st, const GemvF32Args &a, int epi, bool argm
     }
 }
 
+// Many rows: one pass over the weights for up to 2*T rows (T = 16 or 32).
+template <int T, int EPI, bool ARGMAX>
+int32_t launch_gemm_f32_t(cudaStream_t st, const GemvF32Args &a) {
+    auto kernel = gemm_f32_kernel<T, EPI, ARGMAX>;
+    const size_t smem = gemm_f32_smem(T);
+    CUDA_TRY(allow_smem(kernel, smem));
+    const dim3 grid((a.n + F32_ROWS - 1) / F32_ROWS, (a.m + 2 * T - 1) / (2 * T));
+    CUDA_TRY(launch_k(kernel, grid, GF_THREADS, smem, st, a));
+    return check_launch("gemm_f32_kernel");
+}
+
+template <int T>
+int32_t launch_gemm_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) {
+    if (argmax) return launch_gemm_f32_t<T, EPI_NONE, true>(st, a);
+    switch (epi) {
+        case EPI_NONE: return launch_gemm_f32_t<T, EPI_NONE, false>(st, a);
+        case EPI_BIAS: return launch_gemm_f32_t<T, EPI_BIAS, false>(st, a);
+        case EPI_RESIDUAL: return launch_gemm_f32_t<T, EPI_RESIDUAL, false>(st, a);
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+}
+
 int32_t launch_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) {
     if (a.m <= 0 || a.n <= 0) return NC_OK;
     if (a.k % F32_TILE) return fail(NC_ERR_ARGUMENT, "float32 width %d is not a multiple of %d", a.k, F32_TILE);
     if (argmax && epi != EPI_NONE) return fail(NC_ERR_ARGUMENT, "argmax takes no epilogue");
+    if (a.m > 16 && epi != EPI_SWIGLU)
+        return a.m <= 32 ? launch_gemm_f32<16>(st, a, epi, argmax) : launch_gemm_f32<32>(st, a, epi, argmax);
     return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<16>(st, a, epi, argmax);
 }
 

@@ -126,7 +126,8 @@ def test_matmul_i8_vnni_epilogues(cuda, rows, n, k, epi):
     assert same_bits(dout.numpy(), expect)
 
 
-@pytest.mark.parametrize("rows,n,k,epi", [(1, 1152, 896, 1), (3, 896, 4864, 2), (2, 4864, 896, 3), (9, 100, 64, 0)])
+@pytest.mark.parametrize("rows,n,k,epi", [(1, 1152, 896, 1), (3, 896, 4864, 2), (2, 4864, 896, 3), (9, 100, 64, 0),
+                                          (20, 300, 896, 1), (70, 257, 128, 2), (33, 129, 64, 0)])
 def test_matmul_f32_in_order(cuda, rows, n, k, epi):
     rng = np.random.default_rng(n * k + rows)
     x = rng.standard_normal((rows, k)).astype(np.float32)
@@ -151,7 +152,8 @@ def test_matmul_f32_in_order(cuda, rows, n, k, epi):
     assert same_bits(dout.numpy(), expect)
 
 
-@pytest.mark.parametrize("rows,vocab,hidden", [(1, 151936, 896), (3, 5000, 64), (64, 3000, 896)])
+@pytest.mark.parametrize("rows,vocab,hidden", [(1, 151936, 896), (3, 5000, 64), (64, 3000, 896), (17, 4099, 96),
+                                               (40, 151936, 896), (100, 2500, 64)])
 def test_lm_head_argmax(cuda, rows, vocab, hidden):
     rng = np.random.default_rng(vocab + rows)
     x = rng.standard_normal((rows, hidden)).astype(np.float32)
