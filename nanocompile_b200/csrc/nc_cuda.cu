@@ -238,8 +238,8 @@ int32_t launch_gemm_epi(cudaStream_t st, const FusedI8Args &f, int epi) {
         case EPI_NONE: return launch_gemm_t<4, 8, MAXG, PRO, EPI_NONE>(st, f);
         case EPI_BIAS: return launch_gemm_t<4, 8, MAXG, PRO, EPI_BIAS>(st, f);
         case EPI_RESIDUAL: return launch_gemm_t<4, 8, MAXG, PRO, EPI_RESIDUAL>(st, f);
-        case EPI_SWIGLU: return launch_gemm_t<4, 4, MAXG, PRO, EPI_SWIGLU>(st, f);
-        case EPI_SWIGLU_QUANT: return launch_gemm_t<4, 4, MAXG, PRO, EPI_SWIGLU_QUANT>(st, f);
+        case EPI_SWIGLU: return launch_gemm_t<4, 8, MAXG, PRO, EPI_SWIGLU>(st, f);
+        case EPI_SWIGLU_QUANT: return launch_gemm_t<4, 8, MAXG, PRO, EPI_SWIGLU_QUANT>(st, f);
         default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
     }
 }
