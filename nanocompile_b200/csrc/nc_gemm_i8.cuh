@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(GEMM_WARPS * 32, 2) gemm_i8_kernel(FusedI8Args
     constexpr bool TWO = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT;
     constexpr int NM = TWO ? 2 : 1, ROWS = GEMM_WARPS * R;
     constexpr int NACC = NM * R * T, P = NACC / 32;
-    constexpr int D = NM * R >= 8 ? 3 : 4;
+    constexpr int D = NM * R >= 8 ? 3 : 8;             // weight chunks in flight per warp
     static_assert(NACC % 32 == 0, "the butterfly needs a multiple of 32 chains per lane");
     static_assert(EPI != EPI_SWIGLU_QUANT || ROWS % QBLOCK == 0, "quantized outputs need whole 32-row blocks");
     static_assert(PRO != PRO_NORM, "the norm prologue is the few-row kernel's");
