@@ -9,6 +9,7 @@
 #include "../../include/nc_cuda.h"
 #include "nc_attention.cuh"
 #include "nc_gemm_f32.cuh"
+#include "nc_lm_head_tc.cuh"
 #include "nc_gemm_i8.cuh"
 
 #include <cmath>
@@ -99,6 +100,15 @@ namespace {
 bool pdl_enabled() {
     static const bool on = [] {
         const char *v = std::getenv("NC_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// NC_TC_HEAD=0 keeps every LM head on the CUDA cores.
+bool tc_head_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NC_TC_HEAD");
         return !(v && v[0] == '0');
     }();
     return on;
@@ -673,6 +683,13 @@ struct nc_model {
     int64_t slot_stride = 0, layer_stride = 0;
     CUtensorMap kv_map;             // the whole KV arena as rows of d floats (has_kv_map)
     bool has_kv_map = false;
+    // the tensor-core LM head (batched decode steps that need only the tokens)
+    float *lm_tiles = nullptr;      // the embedding as pre-swizzled 128 x 32 tiles (lm_tiles_kernel)
+    float *lm_xhi = nullptr, *lm_xlo = nullptr;   // the normed rows as pre-swizzled 64 x 32 tiles
+    bool tc_head = false;
+    float wmax = 0.0f;              // max |w| of the embedding (set when it is uploaded)
+    float *cand_val = nullptr, *cta_best = nullptr, *lm_delta = nullptr;
+    int32_t *cand_idx = nullptr, *cand_cnt = nullptr;
 
     // activations and step state
     float *x = nullptr, *normed = nullptr, *xs = nullptr, *off = nullptr, *qkv = nullptr, *ctx = nullptr,
@@ -687,7 +704,7 @@ struct nc_model {
     int history_steps = 0;
     int64_t *pinned = nullptr;      // host staging [2][max_rows] for the per-step decode mode
 
-    std::map<int, cudaGraphExec_t> decode_graphs;   // by batch size
+    std::map<int, cudaGraphExec_t> decode_graphs;   // by 2 * batch size + tokens_only
 
     // kernel-time probe: CUDA events around every launch of an eager step, by fused-group kind
     bool probing = false;
@@ -750,7 +767,7 @@ struct Layout {
 //   gate/up projection (rms_norm + quantize prologue, silu*up + quantize epilogue)
 //   down projection (offset prologue, residual epilogue)
 // With more rows the norms run as their own row kernels (one CTA per row, in parallel).
-int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
+int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tokens_only) {
     const nc_qwen2_config &c = m->c;
     cudaStream_t st = m->stream;
     const int H = (int)c.hidden, I = (int)c.inter, d = (int)c.head_dim;
@@ -865,10 +882,31 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused) {
         NC_TRY(launch_norm(st, m->normed, m->x, m->final_norm, nullptr, nullptr, nullptr, nullptr, m->logit_row,
                            logit_rows, H, c.eps));
     }
+    Probe pr(m, K_LM_HEAD);
+    if (tokens_only && m->tc_head && logit_rows > 16 && tc_head_enabled()) {
+        // tensor-core logits, then the exact in-order logits of the argmax candidates
+        LmHeadTcArgs la{};
+        la.m = logit_rows; la.n = (int)c.vocab; la.k = H; la.wmax = m->wmax;
+        la.cand_val = m->cand_val; la.cand_idx = m->cand_idx; la.cand_cnt = m->cand_cnt;
+        la.cta_best = m->cta_best; la.delta = m->lm_delta; la.tiles = m->lm_tiles;
+        la.xhi = m->lm_xhi; la.xlo = m->lm_xlo;
+        const int ctas = (int)((c.vocab + LMT_ROWS - 1) / LMT_ROWS);
+        CUDA_TRY(launch_k(lm_prep_kernel, logit_rows, 256, 0, st, m->lm_xhi, m->lm_xlo, m->lm_delta,
+                          (const float *)m->normed, H, m->wmax));
+        NC_TRY(check_launch("lm_prep_kernel"));
+        CUDA_TRY(allow_smem(lm_head_tc_kernel, LMT_SMEM));
+        CUDA_TRY(launch_k(lm_head_tc_kernel, dim3(ctas, (logit_rows + LMT_TOK - 1) / LMT_TOK), LMT_THREADS, LMT_SMEM,
+                          st, la));
+        NC_TRY(check_launch("lm_head_tc_kernel"));
+        const size_t psmem = lm_pick_smem(H);
+        CUDA_TRY(allow_smem(lm_head_pick_kernel, psmem));
+        CUDA_TRY(launch_k(lm_head_pick_kernel, logit_rows, LMP_THREADS, psmem, st, la, (const float *)m->normed,
+                          (const float *)m->embed, ctas, m->tokens));
+        return check_launch("lm_head_pick_kernel");
+    }
     GemvF32Args a{};
     a.out = m->logits; a.x = m->normed; a.w = m->embed; a.m = logit_rows; a.n = (int)c.vocab; a.k = H;
     a.part_val = m->part_val; a.part_idx = m->part_idx; a.counter = m->counter; a.tokens = m->tokens;
-    Probe pr(m, K_LM_HEAD);
     NC_TRY(launch_f32(st, a, EPI_NONE, true));
     return NC_OK;
 }
@@ -944,6 +982,18 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     const int64_t ctas = (V + F32_ROWS - 1) / F32_ROWS;
     lay.add(&m->part_val, R * ctas * 4);
     lay.add(&m->part_idx, R * ctas * 4);
+    const int64_t tc_ctas = (c.vocab + LMT_ROWS - 1) / LMT_ROWS;
+    const bool tc_head = H % LMT_KT == 0 && R > 16;
+    if (tc_head) {
+        lay.add(&m->lm_tiles, tc_ctas * LMT_ROWS * H * 4);
+        lay.add(&m->lm_xhi, (R + LMT_TOK - 1) / LMT_TOK * LMT_TOK * H * 4);
+        lay.add(&m->lm_xlo, (R + LMT_TOK - 1) / LMT_TOK * LMT_TOK * H * 4);
+        lay.add(&m->cand_val, R * tc_ctas * LMT_CAND * 4);
+        lay.add(&m->cand_idx, R * tc_ctas * LMT_CAND * 4);
+        lay.add(&m->cand_cnt, R * tc_ctas * 4);
+        lay.add(&m->cta_best, R * tc_ctas * 4);
+        lay.add(&m->lm_delta, R * 4);
+    }
     lay.add(&m->ids, R * 8);
     lay.add(&m->tokens, R * 8);
     lay.add(&m->slot, R * 4);
@@ -965,6 +1015,7 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     const int64_t kv_rows = c.slots * m->slot_stride / d;
     if (d % ATB_BOX == 0 && kv_rows < (int64_t(1) << 31))
         m->has_kv_map = make_kv_map(&m->kv_map, m->kv, kv_rows, (int)d) == NC_OK;
+    m->tc_head = tc_head;
 
     // RoPE tables: angle = float(position) * inv_freq[i] (nanocompile/nn.py:78-94), evaluated with
     // the C library's cosf/sinf -- the functions the reference's generated C calls for them.
@@ -1046,6 +1097,23 @@ extern "C" int32_t nc_qwen2_upload(nc_model *m, const char *name, const void *ho
                     (long long)it->second.bytes);
     CUDA_TRY(cudaSetDevice(m->dev));
     CUDA_TRY(cudaMemcpyAsync(it->second.dst, host, (size_t)bytes, cudaMemcpyHostToDevice, m->stream));
+    if ((float *)it->second.dst == m->embed) {      // the LM head's candidate margin needs max |w|
+        const float *w = (const float *)host;
+        float mx = 0.0f;
+        for (int64_t i = 0; i < bytes / 4; ++i) {
+            const float a = std::fabs(w[i]);
+            if (a != a) {                          // a NaN weight: every CTA then rechecks its rows
+                mx = a;
+                break;
+            }
+            if (a > mx) mx = a;
+        }
+        m->wmax = mx;
+        if (m->tc_head) {
+            lm_tiles_kernel<<<1184, 256, 0, m->stream>>>(m->lm_tiles, m->embed, (int)m->c.vocab, (int)m->c.hidden);
+            NC_TRY(check_launch("lm_tiles_kernel"));
+        }
+    }
     if (it->second.int8) {
         xor80_kernel<<<592, 256, 0, m->stream>>>((uint8_t *)it->second.dst, bytes);
         NC_TRY(check_launch("xor80_kernel"));
@@ -1146,7 +1214,7 @@ extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, 
     CUDA_TRY(cudaMemcpyAsync(m->pos, pos, rows * 4, cudaMemcpyHostToDevice, st));
     if (logit_rows) CUDA_TRY(cudaMemcpyAsync(m->logit_row, logit_row, logit_rows * 4, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
-    NC_TRY(enqueue_step(m, rows, logit_rows, fused));
+    NC_TRY(enqueue_step(m, rows, logit_rows, fused, logits == nullptr));
     unsigned long long err = 0;
     CUDA_TRY(cudaMemcpyAsync(&err, m->err, 8, cudaMemcpyDeviceToHost, st));
     if (logits && logit_rows)
@@ -1161,15 +1229,18 @@ extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, 
     return check_device_faults();
 }
 
-static int32_t decode_graph(nc_model *m, int batch, cudaGraphExec_t *out) {
-    auto it = m->decode_graphs.find(batch);
+// tokens_only: the step needs no logits (the last step's logits are not read back), so a batch
+// may take the tensor-core LM head.
+static int32_t decode_graph(nc_model *m, int batch, bool tokens_only, cudaGraphExec_t *out) {
+    const int key = 2 * batch + (tokens_only ? 1 : 0);
+    auto it = m->decode_graphs.find(key);
     if (it != m->decode_graphs.end()) {
         *out = it->second;
         return NC_OK;
     }
     cudaGraph_t graph;
     CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    int32_t s = enqueue_step(m, batch, batch, true);
+    int32_t s = enqueue_step(m, batch, batch, true, tokens_only);
     if (s == NC_OK) {
         if (launch_k(advance_kernel, 1, 1024, 0, m->stream, m->ids, m->pos, m->tokens, m->history, m->step, batch) !=
             cudaSuccess)
@@ -1183,13 +1254,13 @@ static int32_t decode_graph(nc_model *m, int batch, cudaGraphExec_t *out) {
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return fail(NC_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
-    m->decode_graphs[batch] = exec;
+    m->decode_graphs[key] = exec;
     *out = exec;
     return NC_OK;
 }
 
 static int32_t decode_setup(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
-                            const int32_t *start, int32_t steps, cudaGraphExec_t *graph) {
+                            const int32_t *start, int32_t steps, bool tokens_only, cudaGraphExec_t *graph) {
     if (!m || !slot || !first || !start) return fail(NC_ERR_ARGUMENT, "null argument");
     NC_TRY(check_ready(m));
     if (batch <= 0 || batch > m->c.max_rows || batch > 1024)
@@ -1216,7 +1287,7 @@ static int32_t decode_setup(nc_model *m, int32_t batch, const int32_t *slot, con
     CUDA_TRY(cudaMemcpyAsync(m->pos, start, batch * 4, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemcpyAsync(m->logit_row, rows.data(), batch * 4, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemsetAsync(m->step, 0, 4, st));
-    NC_TRY(decode_graph(m, batch, graph));
+    NC_TRY(decode_graph(m, batch, tokens_only, graph));
     CUDA_TRY(cudaStreamSynchronize(st));
     return NC_OK;
 }
@@ -1225,7 +1296,7 @@ extern "C" int32_t nc_qwen2_decode(nc_model *m, int32_t batch, const int32_t *sl
                                    const int32_t *start, int32_t steps, int32_t per_step, int64_t *tokens,
                                    float *logits) {
     cudaGraphExec_t graph;
-    NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, logits == nullptr, &graph));
     cudaStream_t st = m->stream;
     if (per_step) {
         // the host in the loop: each step's input tokens go host -> device from pinned memory,
@@ -1255,7 +1326,7 @@ extern "C" int32_t nc_qwen2_decode(nc_model *m, int32_t batch, const int32_t *sl
 extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
                                     const int32_t *start, int32_t steps, float *ms_per_kind, int32_t *launches_per_kind) {
     cudaGraphExec_t graph;
-    NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, true, &graph));
     for (int k = 0; k < K_KINDS; ++k) {
         ms_per_kind[k] = 0.0f;
         launches_per_kind[k] = 0;
@@ -1265,7 +1336,7 @@ extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *s
         m->probing = true;
         m->event_next = 0;
         m->probe_marks.clear();
-        int32_t status = enqueue_step(m, batch, batch, true);
+        int32_t status = enqueue_step(m, batch, batch, true, true);
         m->probing = false;
         NC_TRY(status);
         if (launch_k(advance_kernel, 1, 1024, 0, st, m->ids, m->pos, m->tokens, m->history, m->step, batch) != cudaSuccess)
@@ -1284,7 +1355,7 @@ extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *s
 extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
                                          const int32_t *start, int32_t steps, float *ms) {
     cudaGraphExec_t graph;
-    NC_TRY(decode_setup(m, batch, slot, first, start, steps, &graph));
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, true, &graph));
     cudaStream_t st = m->stream;
     cudaEvent_t a, b;
     CUDA_TRY(cudaEventCreate(&a));
