@@ -114,6 +114,21 @@ int64_t nc_lm_head_scratch_bytes(int64_t rows, int64_t vocab);
  *    threads) race.  Each call clears the finish counter on its stream before the kernel. */
 int32_t nc_lm_head_argmax_noalloc(void **p, const int64_t *s, void *stream);
 
+/* The same tokens as nc_lm_head_argmax (np.argmax of the in-order float32 logits,
+ * nanocompile/models/qwen2.py:364) for 1..16 rows and a hidden width that is a multiple of 128
+ * up to 1024, reading an int8 copy of the embedding instead of the float32 one: approximate
+ * logits from the copy, then the exact logits of every row the approximation's error bound
+ * cannot rule out.
+ *  nc_lm_head_q8_prepare:  p: [0] embedding f32[vocab, hidden]  [1] copy i8[vocab, hidden]
+ *                             [2] row scales f32[vocab]    s: [0] vocab  [1] hidden
+ *  nc_lm_head_q8_argmax:   p: [0] x f32[rows, hidden]  [1] embedding  [2] copy  [3] row scales
+ *                             [4] tokens i64[rows]  [5] scratch (device, >= nc_lm_head_q8_scratch_bytes)
+ *                          s: [0] rows  [1] vocab  [2] hidden
+ * The scratch's first word must be zero before the first call (it is zero again after each). */
+int32_t nc_lm_head_q8_prepare(void **p, const int64_t *s, void *stream);
+int32_t nc_lm_head_q8_argmax(void **p, const int64_t *s, void *stream);
+int64_t nc_lm_head_q8_scratch_bytes(int64_t rows, int64_t vocab);
+
 /* Decode attention over a KV cache (calls 14-17 with RoPE calls 9-13 fused in): for one new
  * token per row, bias is already in qkv; RoPE q and k, append k/v to the cache at the row's
  * position, scores in index order, softmax (NaN-propagating max, in-order sum of expf),

@@ -430,3 +430,191 @@ fault:
 }
 
 }  // namespace nc
+
+namespace nc {
+
+// ---- few-row decode attention: a CTA per (row, query head, 32-dimension slice) -------------------
+// Decode with a handful of rows has too few (row, head) pairs to fill the GPU, and each pair's
+// work is dominated by in-order chains. Splitting the output dimensions over CTAs multiplies the
+// CTAs by D/32: every CTA recomputes its head's scores and softmax (a few microseconds of
+// independent work over the K rows, which L2 serves to the other slices), then owns 32 P.V
+// chains over its slice of V -- streamed through a cp.async ring from the start of the kernel --
+// and the quantization of exactly one 32-value block of o_proj's input. Same arithmetic and
+// order as attention_kernel.
+constexpr int ATS_THREADS = 256;
+constexpr int ATS_CHUNK = 256;      // positions per staged V chunk
+constexpr int ATS_STAGES = 4;       // chunks in flight: a 1024-position slice is requested at once
+constexpr int ATS_SLICE = 32;       // output dimensions per CTA
+
+__host__ __device__ inline size_t attention_split_smem(int d, int cap) {
+    return sizeof(float) * ((size_t)atb_cap4(cap) + (size_t)ATS_STAGES * ATS_CHUNK * ATS_SLICE + 3 * (size_t)d);
+}
+
+template <int D>
+__global__ void __launch_bounds__(ATS_THREADS) attention_split_kernel(const AttnArgs a) {
+    static_assert(D % ATS_SLICE == 0 && D % 4 == 0, "head dim");
+    constexpr int PPR = D / 4, HALF = D / 2, SLICES = D / ATS_SLICE;
+    extern __shared__ __align__(16) float sms[];
+    __shared__ uint64_t tab[32];
+    __shared__ float s_red[ATS_THREADS / 32];
+    __shared__ float s_max, s_sum, s_rcp;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    release_dependents();
+    wait_for_producer();
+    const int ds = blockIdx.x % SLICES, rh = blockIdx.x / SLICES;
+    const int h = rh % a.heads, r = rh / a.heads, group = a.heads / a.kv, g = h / group;
+    const int pos = a.pos[r], len = pos + 1, slot = a.slot[r], cap4 = atb_cap4(a.cap);
+    float *e = sms;                                        // [cap4]
+    float *vring = e + cap4;                               // [STAGES][CHUNK][SLICE]
+    float *q = vring + ATS_STAGES * ATS_CHUNK * ATS_SLICE; // [D]
+    float *kn = q + D, *vn = kn + D;
+    if (t < 32) tab[t] = kExpTab[t];
+    float *base = a.cache + (int64_t)slot * a.slot_stride;
+    float *K = base + (int64_t)g * a.cap * D;
+    float *V = base + ((int64_t)a.kv + g) * a.cap * D;
+    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
+    const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
+    for (int i = t; i < 3 * D; i += ATS_THREADS) {
+        const int which = i / D, c = i % D;
+        const float *src = which == 0 ? qkv + h * D : (which == 1 ? qkv + (a.heads + g) * D : qkv + (a.heads + a.kv + g) * D);
+        if (which == 2) {
+            vn[c] = src[c];
+            continue;
+        }
+        const float t1 = src[c];
+        const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
+        const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
+        if (which == 0) q[c] = v;
+        else kn[c] = v;
+    }
+    __syncthreads();
+    if (a.mode != 2) {
+        if (h % group == 0 && ds == 0)
+            for (int c = t; c < D; c += ATS_THREADS) {
+                K[(int64_t)pos * D + c] = kn[c];
+                V[(int64_t)pos * D + c] = vn[c];
+            }
+        if (a.mode == 1) return;
+    }
+    const bool own_new = a.mode == 0;
+
+    // V slice chunks: position rows of 128 bytes, 8 pieces each, 8 pieces per thread per chunk
+    const int nv = (len + ATS_CHUNK - 1) / ATS_CHUNK;
+    auto stage_v = [&](int ci) {
+        if (ci < nv) {
+            float4 *dst = reinterpret_cast<float4 *>(vring + (ci % ATS_STAGES) * ATS_CHUNK * ATS_SLICE);
+            for (int i = t; i < ATS_CHUNK * (ATS_SLICE / 4); i += ATS_THREADS) {
+                const int row = i / (ATS_SLICE / 4), pc = i % (ATS_SLICE / 4), j = ci * ATS_CHUNK + row;
+                if (j < len) cp_async16(dst + i, V + (int64_t)j * D + ds * ATS_SLICE + pc * 4);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < ATS_STAGES; ++s) stage_v(s);
+
+    // scores: a thread per position, its head's q in registers, K rows from memory; the next
+    // row's K is requested before the current row's chain (head dims up to 64)
+    constexpr bool PREFETCH = D <= 64;
+    float4 qr[PPR];
+#pragma unroll
+    for (int c = 0; c < PPR; ++c) qr[c] = reinterpret_cast<const float4 *>(q)[c];
+    auto krow = [&](int j) {
+        return (own_new && j == pos) ? reinterpret_cast<const float4 *>(kn) : reinterpret_cast<const float4 *>(K + (int64_t)j * D);
+    };
+    float mx = __uint_as_float(0xff800000u);
+    float4 kv[PPR], kx[PREFETCH ? PPR : 1];
+    if (PREFETCH && t < len) {
+        const float4 *kr = krow(t);
+#pragma unroll
+        for (int c = 0; c < PPR; ++c) kx[c] = kr[c];
+    }
+    for (int j = t; j < len; j += ATS_THREADS) {
+        if (PREFETCH) {
+#pragma unroll
+            for (int c = 0; c < PPR; ++c) kv[c] = kx[PREFETCH ? c : 0];
+            if (j + ATS_THREADS < len) {
+                const float4 *kr = krow(j + ATS_THREADS);
+#pragma unroll
+                for (int c = 0; c < PPR; ++c) kx[PREFETCH ? c : 0] = kr[c];
+            }
+        } else {
+            const float4 *kr = krow(j);
+#pragma unroll
+            for (int c = 0; c < PPR; ++c) kv[c] = kr[c];
+        }
+        float acc = 0.0f;
+#pragma unroll
+        for (int c = 0; c < PPR; ++c) {
+            acc = fadd(acc, fmul(qr[c].x, kv[c].x));
+            acc = fadd(acc, fmul(qr[c].y, kv[c].y));
+            acc = fadd(acc, fmul(qr[c].z, kv[c].z));
+            acc = fadd(acc, fmul(qr[c].w, kv[c].w));
+        }
+        const float sc = fadd(fmul(acc, a.scale), 0.0f);
+        e[j] = sc;
+        mx = nan_max(mx, sc);
+    }
+    mx = warp_nan_max(mx);
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    if (t == 0) {
+        float m = s_red[0];
+        for (int w = 1; w < ATS_THREADS / 32; ++w) m = nan_max(m, s_red[w]);
+        s_max = m;
+    }
+    __syncthreads();
+    const float mh = s_max;
+    for (int j = t; j < len; j += ATS_THREADS) e[j] = expf_exact(fsub(e[j], mh), tab);
+    __syncthreads();
+    if (t == 0) {
+        const float sum = chain_sum(e, len);        // the in-order sum
+        s_sum = sum;
+        s_rcp = __frcp_rn(sum);
+    }
+    __syncthreads();
+    const float sh = s_sum, rh2 = s_rcp;
+    for (int j = t; j < len; j += ATS_THREADS) e[j] = fdiv_recip(e[j], sh, rh2);
+
+    // P.V: warp 0's lanes own the slice's 32 dimensions, positions in order
+    float acc = 0.0f;
+    for (int ci = 0; ci < nv; ++ci) {
+        cp_async_wait<ATS_STAGES - 1>();             // chunk ci has landed
+        __syncthreads();
+        if (warp == 0) {
+            const float *cv = vring + (ci % ATS_STAGES) * ATS_CHUNK * ATS_SLICE + lane;
+            const float *pp = e + ci * ATS_CHUNK;
+            const int n = min(ATS_CHUNK, len - ci * ATS_CHUNK);
+            const int stop = (own_new && ci == nv - 1) ? n - 1 : n;    // the new row comes from vn
+            int jj = 0;
+            for (; jj + 4 <= stop; jj += 4) {
+                const float4 p4 = *reinterpret_cast<const float4 *>(pp + jj);
+                acc = fadd(acc, fmul(p4.x, cv[(jj + 0) * ATS_SLICE]));
+                acc = fadd(acc, fmul(p4.y, cv[(jj + 1) * ATS_SLICE]));
+                acc = fadd(acc, fmul(p4.z, cv[(jj + 2) * ATS_SLICE]));
+                acc = fadd(acc, fmul(p4.w, cv[(jj + 3) * ATS_SLICE]));
+            }
+            for (; jj < stop; ++jj) acc = fadd(acc, fmul(pp[jj], cv[jj * ATS_SLICE]));
+            if (stop != n) acc = fadd(acc, fmul(pp[n - 1], vn[ds * ATS_SLICE + lane]));
+        }
+        __syncthreads();                             // the chunk is consumed before it is refilled
+        stage_v(ci + ATS_STAGES);
+    }
+    cp_async_wait<0>();
+    if (warp == 0) {
+        const int width = a.heads * D, col = h * D + ds * ATS_SLICE;
+        if (a.ctx) a.ctx[(int64_t)r * width + col + lane] = acc;
+        if (a.q_out) {
+            int8_t qv;
+            int bs;
+            const float sc = quantize_block_warp(acc, &qv, &bs);
+            a.q_out[(int64_t)r * width + col + lane] = qv;
+            if (lane == 0) {
+                a.xs_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = sc;
+                a.bsums_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = bs;
+            }
+        }
+    }
+}
+
+}  // namespace nc

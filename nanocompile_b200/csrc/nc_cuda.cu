@@ -10,6 +10,7 @@
 #include "nc_attention.cuh"
 #include "nc_gemm_f32.cuh"
 #include "nc_lm_head_tc.cuh"
+#include "nc_lm_head_q8.cuh"
 #include "nc_gemm_i8.cuh"
 
 #include <cmath>
@@ -100,6 +101,24 @@ namespace {
 bool pdl_enabled() {
     static const bool on = [] {
         const char *v = std::getenv("NC_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// NC_SPLIT_ATTENTION=0 keeps few-row attention at one CTA per query head.
+bool split_attention_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NC_SPLIT_ATTENTION");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// NC_Q8_HEAD=0 turns the int8-prefiltered LM head of small decode steps off.
+bool q8_head_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NC_Q8_HEAD");
         return !(v && v[0] == '0');
     }();
     return on;
@@ -443,8 +462,21 @@ int32_t launch_attention_grouped(cudaStream_t st, const AttnArgs &a, int rows, c
 // Few rows (decode of a handful of sequences): one CTA per query head, for parallelism.  Many
 // rows: one CTA per KV head, reading each KV row once for its group of query heads.
 template <int D>
+int32_t launch_attention_split(cudaStream_t st, const AttnArgs &a, int rows) {
+    const size_t smem = attention_split_smem(D, a.cap);
+    CUDA_TRY(allow_smem(attention_split_kernel<D>, smem));
+    CUDA_TRY(launch_k(attention_split_kernel<D>, rows * a.heads * (D / ATS_SLICE), ATS_THREADS, smem, st, a));
+    return check_launch("attention_split_kernel");
+}
+
+template <int D>
 int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap *map) {
     const int group = a.heads / a.kv;
+    if constexpr (D % ATS_SLICE == 0) {
+        // few rows: (row, head, 32-dimension slice) CTAs, while a probability per position fits
+        if (rows <= 8 && attention_split_smem(D, a.cap) <= 200 * 1024 && split_attention_enabled())
+            return launch_attention_split<D>(st, a, rows);
+    }
     if (rows <= 8 || group == 1) return launch_attention_g<D, 1>(st, a, rows);
     bool done;
     const int32_t s = launch_attention_grouped<D>(st, a, rows, map, &done);
@@ -553,6 +585,24 @@ extern "C" int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream) {
     return launch_f32((cudaStream_t)stream, a, epi, false);
 }
 
+namespace {
+
+// The int8-prefiltered LM head + argmax of up to LMQ_MAXM rows: prefilter, then pick.
+int32_t launch_lm_head_q8(cudaStream_t st, const LmHeadQ8Args &a) {
+    const int ctas = (a.n + LMQ_ROWS - 1) / LMQ_ROWS;
+    const int T = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
+    const dim3 grid(ctas, (a.m + T - 1) / T);
+    if (T == 1) CUDA_TRY(launch_k(lm_head_q8_kernel<1>, grid, LMQ_THREADS, 0, st, a));
+    else if (T == 2) CUDA_TRY(launch_k(lm_head_q8_kernel<2>, grid, LMQ_THREADS, 0, st, a));
+    else if (T == 4) CUDA_TRY(launch_k(lm_head_q8_kernel<4>, grid, LMQ_THREADS, 0, st, a));
+    else CUDA_TRY(launch_k(lm_head_q8_kernel<8>, grid, LMQ_THREADS, 0, st, a));
+    NC_TRY(check_launch("lm_head_q8_kernel"));
+    CUDA_TRY(launch_k(lm_head_q8_pick_kernel, LMQ_PICK_CTAS, LMQ_PICK_THREADS, (size_t)a.k * 4, st, a, ctas));
+    return check_launch("lm_head_q8_pick_kernel");
+}
+
+}  // namespace
+
 extern "C" int64_t nc_lm_head_scratch_bytes(int64_t rows, int64_t vocab) {
     const int64_t ctas = (vocab + F32_ROWS - 1) / F32_ROWS;
     return 256 + rows * ctas * (int64_t)(sizeof(float) + sizeof(int32_t));
@@ -574,6 +624,38 @@ extern "C" int32_t nc_lm_head_argmax(void **p, const int64_t *s, void *stream) {
     a.part_idx = (int32_t *)(scratch + 256 + a.m * ctas * sizeof(float));
     if (!a.tokens) return launch_f32((cudaStream_t)stream, a, EPI_NONE, false);
     return launch_f32((cudaStream_t)stream, a, EPI_NONE, true);
+}
+
+extern "C" int32_t nc_lm_head_q8_prepare(void **p, const int64_t *s, void *stream) {
+    const int64_t vocab = s[0], hidden = s[1];
+    if (vocab <= 0 || hidden <= 0 || vocab > INT32_MAX || hidden > INT32_MAX) return fail(NC_ERR_ARGUMENT, "bad shape");
+    lm_q8_kernel<<<(unsigned)((vocab + 7) / 8), 256, 0, (cudaStream_t)stream>>>((int8_t *)p[1], (float *)p[2],
+                                                                              (const float *)p[0], (int)vocab, (int)hidden);
+    return check_launch("lm_q8_kernel");
+}
+
+extern "C" int64_t nc_lm_head_q8_scratch_bytes(int64_t rows, int64_t vocab) {
+    const int64_t ctas = (vocab + LMQ_ROWS - 1) / LMQ_ROWS;
+    return 256 + 4 * (rows * vocab + rows * ctas + rows + 2 * rows * LMQ_PICK_CTAS);
+}
+
+extern "C" int32_t nc_lm_head_q8_argmax(void **p, const int64_t *s, void *stream) {
+    LmHeadQ8Args a{};
+    a.m = (int)s[0]; a.n = (int)s[1]; a.k = (int)s[2];
+    if (a.m <= 0 || a.m > LMQ_MAXM || a.k % 128 || a.k > LMQ_MAXK || a.n <= 0)
+        return fail(NC_ERR_ARGUMENT, "the int8 LM head takes 1..%d rows and a width that is a multiple of 128 up to %d",
+                    LMQ_MAXM, LMQ_MAXK);
+    a.x = (const float *)p[0]; a.w = (const float *)p[1]; a.q = (const int8_t *)p[2]; a.s = (const float *)p[3];
+    a.tokens = (int64_t *)p[4];
+    char *scratch = (char *)p[5];
+    const int64_t ctas = (a.n + LMQ_ROWS - 1) / LMQ_ROWS;
+    a.counter = (unsigned int *)scratch;
+    a.approx = (float *)(scratch + 256);
+    a.cta_low = a.approx + (int64_t)a.m * a.n;
+    a.bound = a.cta_low + a.m * ctas;
+    a.pick_val = a.bound + a.m;
+    a.pick_idx = (int32_t *)(a.pick_val + a.m * LMQ_PICK_CTAS);
+    return launch_lm_head_q8((cudaStream_t)stream, a);
 }
 
 extern "C" int32_t nc_attention(void **p, const int64_t *s, void *stream) {
@@ -690,6 +772,12 @@ struct nc_model {
     float wmax = 0.0f;              // max |w| of the embedding (set when it is uploaded)
     float *cand_val = nullptr, *cta_best = nullptr, *lm_delta = nullptr;
     int32_t *cand_idx = nullptr, *cand_cnt = nullptr;
+    // the int8-prefiltered LM head (decode steps of up to LMQ_MAXM rows that need only the tokens)
+    int8_t *lmq_q = nullptr;        // the embedding's rows quantized to int8 (lm_q8_kernel)
+    float *lmq_s = nullptr, *lmq_approx = nullptr, *lmq_low = nullptr, *lmq_bound = nullptr, *lmq_pval = nullptr;
+    int32_t *lmq_pidx = nullptr;
+    unsigned int *lmq_counter = nullptr;
+    bool q8_head = false;
 
     // activations and step state
     float *x = nullptr, *normed = nullptr, *xs = nullptr, *off = nullptr, *qkv = nullptr, *ctx = nullptr,
@@ -767,6 +855,16 @@ struct Layout {
 //   gate/up projection (rms_norm + quantize prologue, silu*up + quantize epilogue)
 //   down projection (offset prologue, residual epilogue)
 // With more rows the norms run as their own row kernels (one CTA per row, in parallel).
+// The int8-prefiltered LM head + argmax of the model's normed rows (m->normed -> m->tokens).
+int32_t launch_lm_head_q8(nc_model *m, int rows) {
+    LmHeadQ8Args a{};
+    a.m = rows; a.n = (int)m->c.vocab; a.k = (int)m->c.hidden;
+    a.q = m->lmq_q; a.s = m->lmq_s; a.x = m->normed; a.w = m->embed; a.approx = m->lmq_approx;
+    a.cta_low = m->lmq_low; a.bound = m->lmq_bound; a.pick_val = m->lmq_pval; a.pick_idx = m->lmq_pidx;
+    a.counter = m->lmq_counter; a.tokens = m->tokens;
+    return launch_lm_head_q8(m->stream, a);
+}
+
 int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tokens_only) {
     const nc_qwen2_config &c = m->c;
     cudaStream_t st = m->stream;
@@ -904,6 +1002,8 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tok
                           (const float *)m->embed, ctas, m->tokens));
         return check_launch("lm_head_pick_kernel");
     }
+    if (tokens_only && m->q8_head && logit_rows <= LMQ_MAXM && q8_head_enabled())
+        return launch_lm_head_q8(m, logit_rows);
     GemvF32Args a{};
     a.out = m->logits; a.x = m->normed; a.w = m->embed; a.m = logit_rows; a.n = (int)c.vocab; a.k = H;
     a.part_val = m->part_val; a.part_idx = m->part_idx; a.counter = m->counter; a.tokens = m->tokens;
@@ -994,6 +1094,18 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
         lay.add(&m->cta_best, R * tc_ctas * 4);
         lay.add(&m->lm_delta, R * 4);
     }
+    const bool q8_head = H % 128 == 0 && H <= LMQ_MAXK;
+    if (q8_head) {
+        const int64_t qr = std::min<int64_t>(R, LMQ_MAXM), qctas = (V + LMQ_ROWS - 1) / LMQ_ROWS;
+        lay.add(&m->lmq_q, V * H);
+        lay.add(&m->lmq_s, V * 4);
+        lay.add(&m->lmq_approx, qr * V * 4);
+        lay.add(&m->lmq_low, qr * qctas * 4);
+        lay.add(&m->lmq_bound, qr * 4);
+        lay.add(&m->lmq_pval, qr * LMQ_PICK_CTAS * 4);
+        lay.add(&m->lmq_pidx, qr * LMQ_PICK_CTAS * 4);
+        lay.add(&m->lmq_counter, 4);
+    }
     lay.add(&m->ids, R * 8);
     lay.add(&m->tokens, R * 8);
     lay.add(&m->slot, R * 4);
@@ -1016,6 +1128,7 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     if (d % ATB_BOX == 0 && kv_rows < (int64_t(1) << 31))
         m->has_kv_map = make_kv_map(&m->kv_map, m->kv, kv_rows, (int)d) == NC_OK;
     m->tc_head = tc_head;
+    m->q8_head = q8_head;
 
     // RoPE tables: angle = float(position) * inv_freq[i] (nanocompile/nn.py:78-94), evaluated with
     // the C library's cosf/sinf -- the functions the reference's generated C calls for them.
@@ -1112,6 +1225,11 @@ extern "C" int32_t nc_qwen2_upload(nc_model *m, const char *name, const void *ho
         if (m->tc_head) {
             lm_tiles_kernel<<<1184, 256, 0, m->stream>>>(m->lm_tiles, m->embed, (int)m->c.vocab, (int)m->c.hidden);
             NC_TRY(check_launch("lm_tiles_kernel"));
+        }
+        if (m->q8_head) {
+            lm_q8_kernel<<<(unsigned)((m->c.vocab + 7) / 8), 256, 0, m->stream>>>(m->lmq_q, m->lmq_s, m->embed,
+                                                                                 (int)m->c.vocab, (int)m->c.hidden);
+            NC_TRY(check_launch("lm_q8_kernel"));
         }
     }
     if (it->second.int8) {

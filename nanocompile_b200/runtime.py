@@ -71,7 +71,7 @@ def library() -> ctypes.CDLL:
         L.nc_last_error.restype = _i32
         for name in ("nc_gather_rows", "nc_rms_norm_quantize", "nc_quantize_blocks", "nc_matmul_i8_vnni",
                      "nc_matmul_f32", "nc_lm_head_argmax", "nc_lm_head_argmax_noalloc", "nc_attention",
-                     "nc_attention_cache", "nc_expf_exact"):
+                     "nc_attention_cache", "nc_expf_exact", "nc_lm_head_q8_prepare", "nc_lm_head_q8_argmax"):
             fn = getattr(L, name)
             fn.argtypes = [ctypes.POINTER(_vp), _P64, _vp]
             fn.restype = _i32
@@ -81,6 +81,8 @@ def library() -> ctypes.CDLL:
         L.nc_selfcheck_div127.restype = _i32
         L.nc_lm_head_scratch_bytes.argtypes = [_i64, _i64]
         L.nc_lm_head_scratch_bytes.restype = _i64
+        L.nc_lm_head_q8_scratch_bytes.argtypes = [_i64, _i64]
+        L.nc_lm_head_q8_scratch_bytes.restype = _i64
         L.nc_device_count.argtypes = [_P32]
         L.nc_set_device.argtypes = [_i32]
         L.nc_device_alloc.argtypes = [_i64, ctypes.POINTER(_vp)]

@@ -188,6 +188,57 @@ def test_lm_head_argmax_nan_is_the_maximum(cuda):
     assert int(dt.numpy()[0]) == 1500 == int(np.argmax(oracle.lm_head(x[0], embed)))
 
 
+def q8_head_tokens(cuda, x, embed):
+    rows, hidden = x.shape
+    vocab = embed.shape[0]
+    dx, de = DeviceArray(cuda, x), DeviceArray(cuda, embed)
+    dq = DeviceArray(cuda, shape=(vocab, hidden), dtype=np.int8)
+    ds = DeviceArray(cuda, shape=(vocab,), dtype=np.float32)
+    call(cuda, "nc_lm_head_q8_prepare", [de, dq, ds], [vocab, hidden])
+    dt = DeviceArray(cuda, shape=(rows,), dtype=np.int64)
+    scratch = DeviceArray(cuda, shape=(cuda.library().nc_lm_head_q8_scratch_bytes(rows, vocab),), dtype=np.uint8, fill=0)
+    out = []
+    for _ in range(2):                                # the finish counter resets itself
+        call(cuda, "nc_lm_head_q8_argmax", [dx, de, dq, ds, dt, scratch], [rows, vocab, hidden])
+        out.append([int(v) for v in dt.numpy()])
+    assert out[0] == out[1]
+    return out[0]
+
+
+# The int8-prefiltered head: approximate logits from an int8 copy, exact logits for the rows the
+# error bound keeps; the tokens must be np.argmax of the reference's float32 logits.
+@pytest.mark.parametrize("rows,vocab,hidden", [(1, 151936, 896), (2, 5000, 128), (4, 20000, 896), (7, 3000, 1024),
+                                               (16, 4099, 256)])
+def test_q8_lm_head_tokens(cuda, rows, vocab, hidden):
+    rng = np.random.default_rng(vocab + 3 * rows)
+    x = rng.standard_normal((rows, hidden)).astype(np.float32)
+    embed = (rng.standard_normal((vocab, hidden)) * 0.02).astype(np.float32)
+    logits = np.stack([oracle.lm_head(x[i], embed) for i in range(rows)])
+    if rows >= 2:
+        best = int(np.argmax(logits[0]))
+        embed[vocab - 5] = embed[best]                # an exact tie with the maximum: the first index wins
+        embed[vocab - 9] = embed[best]
+        embed[vocab - 9, 7] = np.nextafter(embed[best, 7], np.float32(1) if x[0, 7] > 0 else np.float32(-1))
+        x[1] = 0.0                                    # every logit +0: index 0 wins
+        logits = np.stack([oracle.lm_head(x[i], embed) for i in range(rows)])
+    tokens = [oracle.argmax(logits[i]) for i in range(rows)]
+    assert q8_head_tokens(cuda, x, embed) == tokens
+
+
+def test_q8_lm_head_non_finite(cuda):
+    rng = np.random.default_rng(11)
+    vocab, hidden = 3000, 128
+    embed = (rng.standard_normal((vocab, hidden)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((3, hidden)).astype(np.float32)
+    embed[2100, 3] = np.nan                           # a NaN logit is np.argmax's answer
+    embed[2500, 0] = np.inf
+    x[2, 5] = np.inf                                  # every logit of row 2 is +-inf or NaN
+    logits = np.stack([oracle.lm_head(x[i], embed) for i in range(3)])
+    tokens = [oracle.argmax(logits[i]) for i in range(3)]
+    assert tokens[0] == 2100
+    assert q8_head_tokens(cuda, x, embed) == tokens
+
+
 def rope_np(t1, cos, sin):
     half = t1.shape[-1] // 2
     rot = np.concatenate([-t1[..., half:], t1[..., :half]], -1)
