@@ -17,7 +17,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 SOURCES = [HERE / "csrc" / "nc_cuda.cu"]
-DEPENDS = SOURCES + [HERE / "csrc" / "nc_kernels.cuh", HERE / "csrc" / "nc_gemm_i8.cuh", HERE / "csrc" / "nc_gemm_f32.cuh", HERE / "csrc" / "nc_lm_head_tc.cuh", HERE / "csrc" / "nc_lm_head_q8.cuh", HERE / "csrc" / "nc_attention.cuh", HERE / "csrc" / "nc_common.cuh", ROOT / "include" / "nc_cuda.h"]
+DEPENDS = SOURCES + [HERE / "csrc" / "nc_kernels.cuh", HERE / "csrc" / "nc_gemm_i8.cuh", HERE / "csrc" / "nc_gemm_f32.cuh", HERE / "csrc" / "nc_lm_head_tc.cuh", HERE / "csrc" / "nc_lm_head_q8.cuh", HERE / "csrc" / "nc_decode_mk.cuh", HERE / "csrc" / "nc_attention.cuh", HERE / "csrc" / "nc_common.cuh", ROOT / "include" / "nc_cuda.h"]
 TARGET = HERE / "libnc_cuda.so"
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17", "-fmad=false",
               "-Xcompiler", "-fPIC", "-shared"]

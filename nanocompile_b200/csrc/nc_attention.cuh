@@ -108,6 +108,45 @@ __device__ __forceinline__ float chain_sum_strided(const float *p, int n, int st
     return acc;
 }
 
+// acc + p[0]*v(0) + p[1]*v(1) + ... + p[n-1]*v(n-1), strictly in order, one thread; the next
+// eight probabilities and values are loaded while the current eight are added. p is 16-byte aligned.
+__device__ __forceinline__ float pv_add8(float acc, const float4 &p0, const float4 &p1, const float *v) {
+    acc = fadd(acc, fmul(p0.x, v[0]));
+    acc = fadd(acc, fmul(p0.y, v[1]));
+    acc = fadd(acc, fmul(p0.z, v[2]));
+    acc = fadd(acc, fmul(p0.w, v[3]));
+    acc = fadd(acc, fmul(p1.x, v[4]));
+    acc = fadd(acc, fmul(p1.y, v[5]));
+    acc = fadd(acc, fmul(p1.z, v[6]));
+    acc = fadd(acc, fmul(p1.w, v[7]));
+    return acc;
+}
+template <typename V>
+__device__ __forceinline__ float pv_chain(float acc, const float *p, int n, V &&vat) {
+    int j = 0;
+    if (n >= 8) {
+        float4 a0 = *reinterpret_cast<const float4 *>(p), a1 = *reinterpret_cast<const float4 *>(p + 4);
+        float va[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) va[u] = vat(u);
+        for (; j + 16 <= n; j += 8) {
+            const float4 b0 = *reinterpret_cast<const float4 *>(p + j + 8), b1 = *reinterpret_cast<const float4 *>(p + j + 12);
+            float vb[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) vb[u] = vat(j + 8 + u);
+            acc = pv_add8(acc, a0, a1, va);
+            a0 = b0;
+            a1 = b1;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) va[u] = vb[u];
+        }
+        acc = pv_add8(acc, a0, a1, va);
+        j += 8;
+    }
+    for (; j < n; ++j) acc = fadd(acc, fmul(p[j], vat(j)));
+    return acc;
+}
+
 // Logical piece c (16 bytes) of row `row` of a staged K chunk, and element `dim` of a V row.
 template <int D, bool TMA>
 __device__ __forceinline__ float4 staged_piece(const float *stage, int row, int c) {
@@ -586,15 +625,7 @@ __global__ void __launch_bounds__(ATS_THREADS) attention_split_kernel(const Attn
             const float *pp = e + ci * ATS_CHUNK;
             const int n = min(ATS_CHUNK, len - ci * ATS_CHUNK);
             const int stop = (own_new && ci == nv - 1) ? n - 1 : n;    // the new row comes from vn
-            int jj = 0;
-            for (; jj + 4 <= stop; jj += 4) {
-                const float4 p4 = *reinterpret_cast<const float4 *>(pp + jj);
-                acc = fadd(acc, fmul(p4.x, cv[(jj + 0) * ATS_SLICE]));
-                acc = fadd(acc, fmul(p4.y, cv[(jj + 1) * ATS_SLICE]));
-                acc = fadd(acc, fmul(p4.z, cv[(jj + 2) * ATS_SLICE]));
-                acc = fadd(acc, fmul(p4.w, cv[(jj + 3) * ATS_SLICE]));
-            }
-            for (; jj < stop; ++jj) acc = fadd(acc, fmul(pp[jj], cv[jj * ATS_SLICE]));
+            acc = pv_chain(acc, pp, stop, [&](int j) { return cv[j * ATS_SLICE]; });
             if (stop != n) acc = fadd(acc, fmul(pp[n - 1], vn[ds * ATS_SLICE + lane]));
         }
         __syncthreads();                             // the chunk is consumed before it is refilled
@@ -617,4 +648,228 @@ __global__ void __launch_bounds__(ATS_THREADS) attention_split_kernel(const Attn
     }
 }
 
+
+// ---- one decode-attention item, head dim 64, K and V by TMA ------------------------------------
+// The (row, query head, 32-dimension slice) item of attention_split_kernel with the cache read by
+// the tensor map of rows of 64 floats (32 x 256 boxes, 128-byte swizzle): 256-position K chunks
+// (two boxes, 64 KB) through a 2-stage ring, one position per thread -- each thread reads its
+// row's 16-byte pieces from the swizzled stage without bank conflicts, where reading K rows from
+// global memory one row per thread touched 32 lines per warp load -- then, in the same 128 KB,
+// 4 stages of the V slice (one box each), requested while the softmax runs. Same arithmetic and
+// order as attention_split_kernel.
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_KSTAGE = ATB_CHUNK * 64;          // floats: 256 rows x 64
+constexpr int ATT_VSTAGE = ATB_CHUNK * ATB_BOX;     // floats: 256 rows x 32
+constexpr int ATT_RING_BYTES = 2 * ATT_KSTAGE * 4;  // = 4 V stages
+static_assert(ATT_RING_BYTES == 4 * ATT_VSTAGE * 4, "K and V stages share the ring");
+
+struct AttnItem {
+    const CUtensorMap *map;
+    int64_t krow0, vrow0;          // tensor-map rows of K[0] / V[0] of the item's (slot, layer, KV head)
+    int ds, pos, len;              // slice, the row's position, positions attended
+    bool own_new;                  // position pos from kn / vn (decode), not the cache
+    float scale;
+};
+
+// Thread 0 requests K chunk ci (stage ci % 2).
+__device__ __forceinline__ void att_issue_k(const AttnItem &it, float *ring, uint64_t *kbar, int ci) {
+    uint64_t *bar = &kbar[ci & 1];
+    float *dst = ring + (ci & 1) * ATT_KSTAGE;
+    mbar_expect_tx(bar, (unsigned)(ATT_KSTAGE * sizeof(float)));
+    tma_load_2d(dst, it.map, 0, (int)(it.krow0 + (int64_t)ci * ATB_CHUNK), bar);
+    tma_load_2d(dst + ATB_CHUNK * ATB_BOX, it.map, ATB_BOX, (int)(it.krow0 + (int64_t)ci * ATB_CHUNK), bar);
+}
+__device__ __forceinline__ void att_issue_v(const AttnItem &it, float *ring, uint64_t *vbar, int ci) {
+    uint64_t *bar = &vbar[ci & 3];
+    mbar_expect_tx(bar, (unsigned)(ATT_VSTAGE * sizeof(float)));
+    tma_load_2d(ring + (ci & 3) * ATT_VSTAGE, it.map, it.ds * ATB_BOX, (int)(it.vrow0 + (int64_t)ci * ATB_CHUNK), bar);
+}
+
+// Thread 0, before the item (its K rows do not depend on this step's q/k/v): the first two chunks.
+__device__ __forceinline__ void att_prefetch_k(const AttnItem &it, float *ring, uint64_t *kbar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const int nk = (it.len + ATB_CHUNK - 1) / ATB_CHUNK;
+    att_issue_k(it, ring, kbar, 0);
+    if (nk > 1) att_issue_k(it, ring, kbar, 1);
+}
+
+// Runs the item with ATT_THREADS threads; q, kn, vn (RoPE applied) in shared memory, e a [len]
+// scratch, ring 1024-byte aligned, kbar[2] / vbar[4] initialized mbarriers whose phases kpar /
+// vpar track (bit per stage), K chunks 0 and 1 already requested (att_prefetch_k). Warp 0's
+// lane c gets dimension ds*32 + c of the context in *acc. False when a wait gave up (then every
+// thread returns false).
+__device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q, const float *kn, const float *vn, float *e,
+                                             float *ring, uint64_t *kbar, uint64_t *vbar, unsigned &kpar, unsigned &vpar,
+                                             const uint64_t *tab, float *s_red, float *s_scal, float *acc_out) {
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int len = it.len, nk = (len + ATB_CHUNK - 1) / ATB_CHUNK;
+    float mx = __uint_as_float(0xff800000u);
+    float4 qr[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) qr[c] = reinterpret_cast<const float4 *>(q)[c];
+    for (int ci = 0; ci < nk; ++ci) {
+        const int s = ci & 1;
+        const bool ok = mbar_wait_bounded(&kbar[s], (kpar >> s) & 1u);
+        kpar ^= 1u << s;
+        if (__syncthreads_or(!ok)) return false;
+        const int j = ci * ATB_CHUNK + t;
+        if (j < len) {
+            const float *stage = ring + s * ATT_KSTAGE;
+            const bool fresh = it.own_new && j == it.pos;
+            float acc = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const float4 kv = fresh ? reinterpret_cast<const float4 *>(kn)[c] : staged_piece<64, true>(stage, t, c);
+                acc = fadd(acc, fmul(qr[c].x, kv.x));
+                acc = fadd(acc, fmul(qr[c].y, kv.y));
+                acc = fadd(acc, fmul(qr[c].z, kv.z));
+                acc = fadd(acc, fmul(qr[c].w, kv.w));
+            }
+            const float sc = fadd(fmul(acc, it.scale), 0.0f);
+            e[j] = sc;
+            mx = nan_max(mx, sc);
+        }
+        __syncthreads();                                    // stage s read
+        if (t == 0 && ci + 2 < nk) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            att_issue_k(it, ring, kbar, ci + 2);
+        }
+    }
+    // the ring now takes the V slice: four chunks in flight while the softmax runs
+    if (t == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int ci = 0; ci < nk && ci < 4; ++ci) att_issue_v(it, ring, vbar, ci);
+    }
+    mx = warp_nan_max(mx);
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    if (t == 0) {
+        float v = s_red[0];
+        for (int w = 1; w < ATT_THREADS / 32; ++w) v = nan_max(v, s_red[w]);
+        s_scal[0] = v;
+    }
+    __syncthreads();
+    const float mh = s_scal[0];
+    for (int j = t; j < len; j += ATT_THREADS) e[j] = expf_exact(fsub(e[j], mh), tab);
+    __syncthreads();
+    if (t == 0) {
+        const float sum = chain_sum(e, len);                // the in-order sum
+        s_scal[1] = sum;
+        s_scal[2] = __frcp_rn(sum);
+    }
+    __syncthreads();
+    const float shs = s_scal[1], rcp = s_scal[2];
+    for (int j = t; j < len; j += ATT_THREADS) e[j] = fdiv_recip(e[j], shs, rcp);
+    __syncthreads();
+    // P.V: warp 0's lanes own the slice's 32 dimensions, positions in order; element (row j,
+    // column c) of a swizzled stage sits at j*32 + ((c/4) ^ (j%8))*4 + c%4
+    float acc = 0.0f;
+    bool vok = true;
+    if (warp == 0) {
+        const int cl = lane & 3, cu = lane >> 2;
+        for (int ci = 0; ci < nk; ++ci) {
+            const int s = ci & 3;
+            vok = __all_sync(0xffffffffu, mbar_wait_bounded(&vbar[s], (vpar >> s) & 1u));
+            vpar ^= 1u << s;
+            if (!vok) break;
+            const float *cv = ring + s * ATT_VSTAGE + cl;
+            const float *pp = e + ci * ATB_CHUNK;
+            const int n = min(ATB_CHUNK, len - ci * ATB_CHUNK);
+            const int stop = (it.own_new && ci == nk - 1) ? n - 1 : n;    // the new row comes from vn
+            acc = pv_chain(acc, pp, stop, [&](int j) { return cv[j * ATB_BOX + ((cu ^ (j & 7)) << 2)]; });
+            if (stop != n) acc = fadd(acc, fmul(pp[n - 1], vn[it.ds * ATB_BOX + lane]));
+            __syncwarp();
+            if (lane == 0 && ci + 4 < nk) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                att_issue_v(it, ring, vbar, ci + 4);
+            }
+        }
+    }
+    *acc_out = acc;
+    return !__syncthreads_or(!vok);
+}
+
+__host__ __device__ inline size_t attention_tma_smem(int cap) {
+    return 1024 + (size_t)ATT_RING_BYTES + sizeof(float) * ((size_t)atb_cap4(cap) + 3 * 64);
+}
+
+// attention_split_kernel for head dim 64 with the cache read through the tensor map.
+__global__ void __launch_bounds__(ATT_THREADS) attention_split_tma_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap kvmap) {
+    extern __shared__ __align__(16) unsigned char att_sm[];
+    __shared__ uint64_t tab[32];
+    __shared__ __align__(8) uint64_t kbar[2], vbar[4];
+    __shared__ float s_red[ATT_THREADS / 32], s_scal[3];
+    constexpr int D = 64, HALF = 32, SLICES = 2;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    float *ring = reinterpret_cast<float *>(att_sm + ((1024 - (smem_addr(att_sm) & 1023)) & 1023));
+    float *e = ring + ATT_RING_BYTES / 4;
+    float *q = e + atb_cap4(a.cap), *kn = q + D, *vn = kn + D;
+    const int ds = blockIdx.x % SLICES, rh = blockIdx.x / SLICES;
+    const int h = rh % a.heads, r = rh / a.heads, group = a.heads / a.kv, g = h / group;
+    const int pos = a.pos[r], len = pos + 1;
+    const int64_t slot = a.slot[r];
+    if (t < 32) tab[t] = kExpTab[t];
+    AttnItem it;
+    it.map = &kvmap;
+    it.krow0 = a.cache_row0 + slot * (a.slot_stride / D) + (int64_t)g * a.cap;
+    it.vrow0 = a.cache_row0 + slot * (a.slot_stride / D) + (int64_t)(a.kv + g) * a.cap;
+    it.ds = ds; it.pos = pos; it.len = len; it.own_new = a.mode == 0; it.scale = a.scale;
+    if (t == 0) {
+        for (int i = 0; i < 2; ++i) mbar_init(&kbar[i], 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&vbar[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // decode: the cached rows come from earlier steps, not from the previous kernel
+        if (a.mode == 0) att_prefetch_k(it, ring, kbar);
+    }
+    release_dependents();
+    wait_for_producer();
+    if (t == 0 && a.mode == 2) att_prefetch_k(it, ring, kbar);   // the prompt's rows: just appended
+    float *base = a.cache + slot * a.slot_stride;
+    float *K = base + (int64_t)g * a.cap * D;
+    float *V = base + ((int64_t)a.kv + g) * a.cap * D;
+    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
+    const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
+    for (int i = t; i < 3 * D; i += ATT_THREADS) {
+        const int which = i / D, c = i % D;
+        const float *src = which == 0 ? qkv + h * D : (which == 1 ? qkv + (a.heads + g) * D : qkv + (a.heads + a.kv + g) * D);
+        if (which == 2) {
+            vn[c] = src[c];
+            continue;
+        }
+        const float t1 = src[c];
+        const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
+        const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
+        if (which == 0) q[c] = v;
+        else kn[c] = v;
+    }
+    __syncthreads();
+    if (a.mode != 2) {
+        if (h % group == 0 && ds == 0)
+            for (int c = t; c < D; c += ATT_THREADS) {
+                K[(int64_t)pos * D + c] = kn[c];
+                V[(int64_t)pos * D + c] = vn[c];
+            }
+        if (a.mode == 1) return;
+    }
+    unsigned kpar = 0, vpar = 0;
+    float acc;
+    if (!att_item_tma(it, q, kn, vn, e, ring, kbar, vbar, kpar, vpar, tab, s_red, s_scal, &acc)) {
+        if (t == 0) atomicExch(&g_attention_fault, 1u);
+        return;
+    }
+    if (warp == 0) {
+        const int width = a.heads * D, col = h * D + ds * ATB_BOX;
+        if (a.ctx) a.ctx[(int64_t)r * width + col + lane] = acc;
+        if (a.q_out) {
+            int8_t qv;
+            int bs;
+            const float sc = quantize_block_warp(acc, &qv, &bs);
+            a.q_out[(int64_t)r * width + col + lane] = qv;
+            if (lane == 0) {
+                a.xs_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = sc;
+                a.bsums_out[(int64_t)r * (width / QBLOCK) + col / QBLOCK] = bs;
+            }
+        }
+    }
+}
 }  // namespace nc

@@ -120,13 +120,17 @@ __device__ __forceinline__ float swiglu(float g, float u, const uint64_t *tab) {
 __device__ __forceinline__ float block_magnitude(float v) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu));
 }
+// The IEEE divide for rare fallbacks, as a call: inlined, the compiler may evaluate it on every
+// path before the branch that needs it.
+__device__ __noinline__ float fdiv_slow(float a, float b) { return __fdiv_rn(a, b); }
+
 // mag / 127 correctly rounded, without the IEEE divide's branchy slow path: q0 = mag * y with
 // y = RN(1/127), then one remainder correction r = mag - q0 * 127 (exact, by FMA), q = q0 + r * y
 // (the correction step of Markstein's FMA division).  Checked equal to IEEE division for every
 // non-negative float by nc_selfcheck_div127; non-finite and tiny magnitudes take the IEEE divide.
 __device__ __forceinline__ float div127(float mag) {
     const float y = 0x1.020408p-7f;                      // RN(1/127)
-    if (!(mag < 0x1p+120f) || mag < 0x1p-100f) return fdiv(mag, 127.0f);
+    if (!(mag < 0x1p+120f) || mag < 0x1p-100f) return fdiv_slow(mag, 127.0f);
     const float q0 = fmul(mag, y);
     const float r = __fmaf_rn(-q0, 127.0f, mag);
     return __fmaf_rn(r, y, q0);
@@ -138,8 +142,7 @@ __device__ __forceinline__ float block_scale(float mag) { return (mag <= 0.0f) ?
 // the residual a - b*q -- exact, because q is within an ulp of a/b -- proves q nearest:
 // |a - b*q| < b * ulp(q)/2 (ulp(q)/4 at a power of two, where the spacing below halves).
 // Anything else (huge or tiny quotients, NaN, an undecided residual) takes the IEEE divide.
-// The fallback is a call so the compiler cannot hoist the IEEE divide into the common path.
-__device__ __noinline__ float fdiv_slow(float a, float b) { return __fdiv_rn(a, b); }
+// The fallback is a call (fdiv_slow) so the compiler cannot hoist the IEEE divide into the common path.
 
 __device__ __forceinline__ float fdiv_recip(float a, float b, float y) {
     const float q0 = fmul(a, y);
@@ -160,17 +163,59 @@ __device__ __forceinline__ float fdiv_recip(float a, float b, float y) {
 __device__ __forceinline__ int8_t quantize_value(float v, float scale) {
     float t = __fdividef(v, scale);
     const float a = fabsf(t);
-    if (!(a < 256.0f) || !(scale >= 0x1p-100f) || fabsf(a - floorf(a) - 0.5f) < (1.0f / 512)) t = fdiv(v, scale);
+    if (!(a < 256.0f) || !(scale >= 0x1p-100f) || fabsf(a - floorf(a) - 0.5f) < (1.0f / 512)) t = fdiv_slow(v, scale);
     t = roundf(t);
     t = (t <= 127.0f) ? t : 127.0f;
     t = (-127.0f <= t) ? t : -127.0f;
     return (int8_t)t;
 }
+// N blocks at once by one warp (lane = position in each block): the same scales, int8 values and
+// block sums as N calls of quantize_block_warp, with the rare IEEE-divide fallbacks taken after
+// every block's fast path, so the N blocks' dependent chains overlap.
+template <int N>
+__device__ __forceinline__ void quantize_blocks_warp(const float *v, int8_t *q, float *scale, int *bsum) {
+    const float y = 0x1.020408p-7f;                      // RN(1/127), as in div127
+    float mag[N], t[N];
+    bool slow_scale = false, slow_q = false, sl[N];
+#pragma unroll
+    for (int u = 0; u < N; ++u) mag[u] = block_magnitude(v[u]);
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        const float q0 = fmul(mag[u], y);
+        scale[u] = (mag[u] <= 0.0f) ? 1.0f : __fmaf_rn(__fmaf_rn(-q0, 127.0f, mag[u]), y, q0);
+        slow_scale |= !(mag[u] <= 0.0f) && (!(mag[u] < 0x1p+120f) || mag[u] < 0x1p-100f);
+    }
+    if (slow_scale) {                                    // the same in every lane: mag is the block's
+#pragma unroll
+        for (int u = 0; u < N; ++u)
+            if (!(mag[u] <= 0.0f) && (!(mag[u] < 0x1p+120f) || mag[u] < 0x1p-100f)) scale[u] = fdiv_slow(mag[u], 127.0f);
+    }
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        t[u] = __fdividef(v[u], scale[u]);
+        const float a = fabsf(t[u]);
+        sl[u] = !(a < 256.0f) || !(scale[u] >= 0x1p-100f) || fabsf(a - floorf(a) - 0.5f) < (1.0f / 512);
+        slow_q |= sl[u];
+    }
+    if (__any_sync(0xffffffffu, slow_q)) {
+#pragma unroll
+        for (int u = 0; u < N; ++u)
+            if (sl[u]) t[u] = fdiv_slow(v[u], scale[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        float r = roundf(t[u]);
+        r = (r <= 127.0f) ? r : 127.0f;
+        r = (-127.0f <= r) ? r : -127.0f;
+        q[u] = (int8_t)r;
+    }
+#pragma unroll
+    for (int u = 0; u < N; ++u) bsum[u] = __reduce_add_sync(0xffffffffu, (int)q[u]);
+}
+
 __device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bsum) {
-    const float scale = block_scale(block_magnitude(v));
-    const int8_t qi = quantize_value(v, scale);
-    *q = qi;
-    *bsum = __reduce_add_sync(0xffffffffu, (int)qi);
+    float scale;
+    quantize_blocks_warp<1>(&v, q, &scale, bsum);
     return scale;
 }
 

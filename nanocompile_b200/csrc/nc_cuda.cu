@@ -11,6 +11,7 @@
 #include "nc_gemm_f32.cuh"
 #include "nc_lm_head_tc.cuh"
 #include "nc_lm_head_q8.cuh"
+#include "nc_decode_mk.cuh"
 #include "nc_gemm_i8.cuh"
 
 #include <cmath>
@@ -110,6 +111,15 @@ bool pdl_enabled() {
 bool split_attention_enabled() {
     static const bool on = [] {
         const char *v = std::getenv("NC_SPLIT_ATTENTION");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// NC_MK=0 keeps small int8 decode steps on the separate kernels.
+bool mk_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NC_MK");
         return !(v && v[0] == '0');
     }();
     return on;
@@ -472,6 +482,15 @@ int32_t launch_attention_split(cudaStream_t st, const AttnArgs &a, int rows) {
 template <int D>
 int32_t launch_attention_d(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap *map) {
     const int group = a.heads / a.kv;
+    if constexpr (D == 64) {
+        // few rows, the cache behind a tensor map: the split items with K and V by TMA
+        if (rows <= 8 && map && attention_tma_smem(a.cap) <= 220 * 1024 && split_attention_enabled()) {
+            const size_t smem = attention_tma_smem(a.cap);
+            CUDA_TRY(allow_smem(attention_split_tma_kernel, smem));
+            CUDA_TRY(launch_k(attention_split_tma_kernel, rows * a.heads * (D / ATS_SLICE), ATT_THREADS, smem, st, a, *map));
+            return check_launch("attention_split_tma_kernel");
+        }
+    }
     if constexpr (D % ATS_SLICE == 0) {
         // few rows: (row, head, 32-dimension slice) CTAs, while a probability per position fits
         if (rows <= 8 && attention_split_smem(D, a.cap) <= 200 * 1024 && split_attention_enabled())
@@ -515,6 +534,12 @@ int32_t check_device_faults() {
         const unsigned int zero = 0;
         CUDA_TRY(cudaMemcpyToSymbol(g_attention_fault, &zero, sizeof(zero)));
         return fail(NC_ERR_KERNEL, "attention: a K/V stage did not arrive within its wait limit");
+    }
+    CUDA_TRY(cudaMemcpyFromSymbol(&fault, g_mk_fault, sizeof(fault)));
+    if (fault) {
+        const unsigned int zero = 0;
+        CUDA_TRY(cudaMemcpyToSymbol(g_mk_fault, &zero, sizeof(zero)));
+        return fail(NC_ERR_KERNEL, "persistent decode step: a grid barrier was not reached within its wait limit");
     }
     return NC_OK;
 }
@@ -778,6 +803,13 @@ struct nc_model {
     int32_t *lmq_pidx = nullptr;
     unsigned int *lmq_counter = nullptr;
     bool q8_head = false;
+    // the persistent decode kernel (steps of up to MK_ROWS rows)
+    MkLayer *mk_layers = nullptr;   // per-layer weight pointers, on the device
+    unsigned int *mk_sync = nullptr;   // CTAs finished, launch number
+    unsigned long long *mk_xt = nullptr, *mk_qkvt = nullptr, *mk_aqt = nullptr, *mk_hqt = nullptr;   // tagged words
+    int64_t mk_tagged_bytes = 0;    // the four tagged buffers, contiguous from mk_xt
+    int mk_ctas = 0;                // one CTA per SM; 0: the kernel cannot serve this model
+    bool logit_identity = false;    // the step's logit rows are its rows 0..rows-1 (set per step)
 
     // activations and step state
     float *x = nullptr, *normed = nullptr, *xs = nullptr, *off = nullptr, *qkv = nullptr, *ctx = nullptr,
@@ -803,7 +835,7 @@ struct nc_model {
 
 enum ProbeKind : int {
     K_GATHER = 0, K_QKV = 1, K_ATTENTION = 2, K_O = 3, K_GATE_UP = 4, K_DOWN = 5, K_NORM = 6, K_QUANT = 7,
-    K_LM_HEAD = 8, K_KINDS = 9
+    K_LM_HEAD = 8, K_LAYERS = 9, K_KINDS = 10
 };
 
 namespace {
@@ -855,6 +887,73 @@ struct Layout {
 //   gate/up projection (rms_norm + quantize prologue, silu*up + quantize epilogue)
 //   down projection (offset prologue, residual epilogue)
 // With more rows the norms run as their own row kernels (one CTA per row, in parallel).
+// The persistent decode kernel's instance for a model's widths: exact register slices for the
+// 896 / 4864 widths of Qwen2.5-0.5B, the largest ones otherwise.
+using MkKernel = void (*)(MkArgs, CUtensorMap);
+MkKernel mk_kernel(int H, int I) {
+    if (H / CHUNK == 7 && I / CHUNK == 38) return decode_mk_kernel<7, 38>;
+    return decode_mk_kernel<MK_NCH, MK_NCH_DOWN>;
+}
+
+// The persistent decode kernel serves an int8 model whose widths fit its register slices, with
+// one CTA per SM, when every CTA can be resident; returns the CTA count (0: not served).
+int mk_capacity(const nc_qwen2_config &c, int dev) {
+    if (!mk_enabled()) return 0;
+    const int H = (int)c.hidden, I = (int)c.inter, d = (int)c.head_dim, Hq = (int)(c.heads * c.head_dim);
+    const int Nqkv = (int)((c.heads + 2 * c.kv_heads) * c.head_dim);
+    if (H % CHUNK || Hq % CHUNK || I % CHUNK || H > MK_NCH * CHUNK || Hq > MK_NCH * CHUNK || I > MK_NCH_DOWN * CHUNK)
+        return 0;
+    if (d != 64 || c.layers > MK_MAX_LAYERS) return 0;            // attention items of head dim 64
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 0;
+    const int G = sms;
+    if ((Nqkv + G - 1) / G > MK_WARPS || (H + G - 1) / G > MK_WARPS - 1 || (I / QBLOCK + G - 1) / G > 2 ||
+        QBLOCK != MK_WARPS * (32 / MK_GU_LPR))
+        return 0;
+    if (MK_ROWS * c.heads * (d / ATS_SLICE) > G) return 0;
+    const MkSmem L = mk_smem((int)c.layers, MK_ROWS, H, std::max(H, std::max(Hq, I)), d, (int)c.capacity);
+    if (L.bytes > 224 * 1024) return 0;                          // with the static shared memory: <= 227 KB
+    const auto kernel = mk_kernel(H, I);
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.bytes) != cudaSuccess) return 0;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, MK_THREADS, L.bytes) != cudaSuccess || per_sm < 1)
+        return 0;
+    return G;
+}
+
+// Gather, every layer and the final norm of a decode step of up to MK_ROWS rows as one
+// cooperative launch (m->x, m->normed; the LM head follows).
+int32_t launch_decode_mk(nc_model *m, int rows) {
+    const nc_qwen2_config &c = m->c;
+    MkArgs a{};
+    a.layers = m->mk_layers; a.nl = (int)c.layers; a.m = rows; a.H = (int)c.hidden; a.I = (int)c.inter;
+    a.heads = (int)c.heads; a.kv = (int)c.kv_heads; a.d = (int)c.head_dim; a.cap = (int)c.capacity;
+    a.eps = c.eps; a.scale = c.attn_scale; a.slot_stride = m->slot_stride; a.vocab = c.vocab;
+    a.slot_rows = m->slot_stride / c.head_dim;
+    a.embed = m->embed; a.ids = m->ids; a.err = m->err; a.slot = m->slot; a.pos = m->pos;
+    a.cos_tab = m->cos_tab; a.sin_tab = m->sin_tab; a.final_norm = m->final_norm;
+    a.normed = m->normed;
+    const int H = a.H, Hq = a.heads * a.d, Nqkv = (a.heads + 2 * a.kv) * a.d;
+    a.xt = m->mk_xt;
+    a.qkvt = a.xt + (int64_t)MK_ROWS * H;
+    a.aqt = a.qkvt + (int64_t)MK_ROWS * Nqkv;
+    a.hqt = a.aqt + (int64_t)MK_ROWS * (Hq / QBLOCK) * MK_BLOCK_WORDS;
+    a.sync = m->mk_sync;
+    const MkSmem L = mk_smem(a.nl, rows, H, std::max(H, std::max(Hq, a.I)), a.d, a.cap);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m->mk_ctas);
+    cfg.blockDim = dim3(MK_THREADS);
+    cfg.dynamicSmemBytes = L.bytes;
+    cfg.stream = m->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, mk_kernel(a.H, a.I), a, m->kv_map));
+    return check_launch("decode_mk_kernel");
+}
+
 // The int8-prefiltered LM head + argmax of the model's normed rows (m->normed -> m->tokens).
 int32_t launch_lm_head_q8(nc_model *m, int rows) {
     LmHeadQ8Args a{};
@@ -865,7 +964,8 @@ int32_t launch_lm_head_q8(nc_model *m, int rows) {
     return launch_lm_head_q8(m->stream, a);
 }
 
-int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tokens_only) {
+// Gather, the layers as separate fused-group kernels, and the final norm of the logit rows.
+int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
     const nc_qwen2_config &c = m->c;
     cudaStream_t st = m->stream;
     const int H = (int)c.hidden, I = (int)c.inter, d = (int)c.head_dim;
@@ -980,6 +1080,19 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tok
         NC_TRY(launch_norm(st, m->normed, m->x, m->final_norm, nullptr, nullptr, nullptr, nullptr, m->logit_row,
                            logit_rows, H, c.eps));
     }
+    return NC_OK;
+}
+
+int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tokens_only) {
+    const nc_qwen2_config &c = m->c;
+    cudaStream_t st = m->stream;
+    const int H = (int)c.hidden;
+    if (c.quant && m->mk_ctas && rows <= MK_ROWS && fused && m->logit_identity && logit_rows == rows) {
+        Probe pr(m, K_LAYERS);
+        NC_TRY(launch_decode_mk(m, rows));
+    } else {
+        NC_TRY(enqueue_layers(m, rows, logit_rows, fused));
+    }
     Probe pr(m, K_LM_HEAD);
     if (tokens_only && m->tc_head && logit_rows > 16 && tc_head_enabled()) {
         // tensor-core logits, then the exact in-order logits of the argmax candidates
@@ -1012,6 +1125,16 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tok
 }
 
 }  // namespace
+
+// A step's faults; a persistent step that gave up leaves its barrier counters behind: clear them.
+static int32_t model_faults(nc_model *m) {
+    const int32_t status = check_device_faults();
+    if (status != NC_OK && m->mk_sync) {
+        cudaMemset(m->mk_sync, 0, 16);
+        cudaMemset(m->mk_xt, 0, (size_t)m->mk_tagged_bytes);
+    }
+    return status;
+}
 
 extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_freq, nc_model **out) {
     if (!cfg || !out || !inv_freq) return fail(NC_ERR_ARGUMENT, "null argument");
@@ -1114,6 +1237,14 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     lay.add(&m->step, 4);
     lay.add(&m->err, 8);
     lay.add(&m->counter, 4);
+    lay.add(&m->mk_layers, c.layers * (int64_t)sizeof(MkLayer));
+    lay.add(&m->mk_sync, 16);
+    {
+        const int64_t xt = MK_ROWS * H * 8, qt = MK_ROWS * Nqkv * 8, at = MK_ROWS * (Hq / 32) * MK_BLOCK_WORDS * 8,
+                      ht = MK_ROWS * (I / 32) * MK_BLOCK_WORDS * 8;
+        lay.add(&m->mk_xt, xt + qt + at + ht);
+        m->mk_tagged_bytes = xt + qt + at + ht;
+    }
     m->history_steps = 8192;
     lay.add(&m->history, (int64_t)m->history_steps * R * 8);
 
@@ -1182,6 +1313,16 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
                 reg(base_name, pr.f, pr.n * pr.k * 4, false);
             }
         }
+    }
+    if (c.quant) {
+        std::vector<MkLayer> ml((size_t)c.layers);
+        for (int64_t l = 0; l < c.layers; ++l) {
+            const auto &L = m->layers[l];
+            ml[l] = MkLayer{L.wqkv, L.wo, L.wg, L.wu, L.wd, L.sqkv, L.so, L.sg, L.su, L.sd, L.bqkv, L.in_norm, L.post_norm,
+                            m->kv + l * m->layer_stride, l * m->layer_stride / d};
+        }
+        CUDA_TRY(cudaMemcpy(m->mk_layers, ml.data(), ml.size() * sizeof(MkLayer), cudaMemcpyHostToDevice));
+        m->mk_ctas = m->has_kv_map ? mk_capacity(c, m->dev) : 0;
     }
     *out = m.release();
     return NC_OK;
@@ -1332,6 +1473,8 @@ extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, 
     CUDA_TRY(cudaMemcpyAsync(m->pos, pos, rows * 4, cudaMemcpyHostToDevice, st));
     if (logit_rows) CUDA_TRY(cudaMemcpyAsync(m->logit_row, logit_row, logit_rows * 4, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
+    m->logit_identity = logit_rows == rows;
+    for (int i = 0; i < logit_rows; ++i) m->logit_identity = m->logit_identity && logit_row[i] == i;
     NC_TRY(enqueue_step(m, rows, logit_rows, fused, logits == nullptr));
     unsigned long long err = 0;
     CUDA_TRY(cudaMemcpyAsync(&err, m->err, 8, cudaMemcpyDeviceToHost, st));
@@ -1344,7 +1487,7 @@ extern "C" int32_t nc_qwen2_step(nc_model *m, int32_t rows, const int64_t *ids, 
         return fail(NC_ERR_KERNEL, "gather index %lld is outside 0..%lld", (long long)ids[err],
                     (long long)(m->c.vocab - 1));
     }
-    return check_device_faults();
+    return model_faults(m);
 }
 
 // tokens_only: the step needs no logits (the last step's logits are not read back), so a batch
@@ -1358,6 +1501,7 @@ static int32_t decode_graph(nc_model *m, int batch, bool tokens_only, cudaGraphE
     }
     cudaGraph_t graph;
     CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    m->logit_identity = true;                 // decode_setup makes the logit rows 0..batch-1
     int32_t s = enqueue_step(m, batch, batch, true, tokens_only);
     if (s == NC_OK) {
         if (launch_k(advance_kernel, 1, 1024, 0, m->stream, m->ids, m->pos, m->tokens, m->history, m->step, batch) !=
@@ -1438,7 +1582,7 @@ extern "C" int32_t nc_qwen2_decode(nc_model *m, int32_t batch, const int32_t *sl
     if (logits && steps)
         CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab * 4, cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaStreamSynchronize(st));
-    return check_device_faults();
+    return model_faults(m);
 }
 
 extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
@@ -1454,6 +1598,7 @@ extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *s
         m->probing = true;
         m->event_next = 0;
         m->probe_marks.clear();
+        m->logit_identity = true;
         int32_t status = enqueue_step(m, batch, batch, true, true);
         m->probing = false;
         NC_TRY(status);
@@ -1467,7 +1612,7 @@ extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *s
             launches_per_kind[pm.first] += 1;
         }
     }
-    return check_device_faults();
+    return model_faults(m);
 }
 
 extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
@@ -1485,7 +1630,7 @@ extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32
     CUDA_TRY(cudaEventElapsedTime(ms, a, b));
     cudaEventDestroy(a);
     cudaEventDestroy(b);
-    return check_device_faults();
+    return model_faults(m);
 }
 
 // ---- the LM head + argmax without any allocation ---------------------------------------------

@@ -38,32 +38,32 @@ __global__ void gather_kernel(float *__restrict__ out, const int64_t *__restrict
 }
 
 // ---- block quantization of a row held in shared memory --------------------------------------
-// Warp w quantizes blocks w, w + nwarps, ... (nanocompile/quantize.py:102-124), up to 8 of
+// Warp w quantizes blocks w, w + nwarps, ... (nanocompile/quantize.py:102-124), up to N of
 // them at once so their divisions overlap; writes xq / xs / block sums and leaves each block's
 // offset term float(sum_b) * scale_b in term[b].
+template <int N = 8>
 __device__ __forceinline__ void quantize_row_smem(const float *row, int n, int8_t *xq, float *xs, int32_t *bsums,
                                                   float *term, int warp, int nwarps, int lane) {
     const int blocks = n / QBLOCK;
-    for (int b0 = warp; b0 < blocks; b0 += 8 * nwarps) {
-        float v[8], scale[8];
+    for (int b0 = warp; b0 < blocks; b0 += N * nwarps) {
+        float v[N], scale[N];
+        int8_t q[N];
+        int bs[N];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < N; ++u) {
             const int b = b0 + u * nwarps;
             v[u] = b < blocks ? row[b * QBLOCK + lane] : 0.0f;
         }
+        quantize_blocks_warp<N>(v, q, scale, bs);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) scale[u] = block_scale(block_magnitude(v[u]));
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < N; ++u) {
             const int b = b0 + u * nwarps;
-            const int8_t qv = quantize_value(v[u], scale[u]);
-            const int bs = __reduce_add_sync(0xffffffffu, (int)qv);
             if (b < blocks) {
-                xq[b * QBLOCK + lane] = qv;
+                xq[b * QBLOCK + lane] = q[u];
                 if (lane == 0) {
                     xs[b] = scale[u];
-                    if (bsums) bsums[b] = bs;
-                    term[b] = fmul((float)bs, scale[u]);
+                    if (bsums) bsums[b] = bs[u];
+                    term[b] = fmul((float)bs[u], scale[u]);
                 }
             }
         }
@@ -177,12 +177,23 @@ struct Seg<4> {
     using T = uint32_t;
     __device__ static void split(const T &v, uint32_t *o) { o[0] = v; }
 };
+struct alignas(16) U32x8 {
+    uint4 lo, hi;
+};
+template <>
+struct Seg<32> {
+    using T = U32x8;
+    __device__ static void split(const T &v, uint32_t *o) {
+        o[0] = v.lo.x; o[1] = v.lo.y; o[2] = v.lo.z; o[3] = v.lo.w;
+        o[4] = v.hi.x; o[5] = v.hi.y; o[6] = v.hi.z; o[7] = v.hi.w;
+    }
+};
 
 // Butterfly over the accumulator index bits in _combine's pairing order: a^8, a^16, a^4,
 // a^1, a^2.  Bits below log2(APL) are inside a lane, the rest across lanes (xor shuffle).
 template <int APL>
 __device__ __forceinline__ float combine_lanes(float *v) {
-    constexpr int LG = APL == 4 ? 2 : (APL == 2 ? 1 : 0);
+    constexpr int LG = APL == 8 ? 3 : (APL == 4 ? 2 : (APL == 2 ? 1 : 0));
     const int order[5] = {3, 4, 2, 0, 1};
 #pragma unroll
     for (int s = 0; s < 5; ++s) {

@@ -237,7 +237,7 @@ class DeviceModel:
         return tokens, logits
 
     KINDS = ("gather", "qkv_projection", "attention", "o_projection", "gate_up_projection", "down_projection",
-             "rms_norm", "block_quantize", "lm_head_argmax")
+             "rms_norm", "block_quantize", "lm_head_argmax", "persistent_layers")
 
     def profile(self, first: Sequence[int], slot: Sequence[int], start: Sequence[int], steps: int
                 ) -> dict[str, tuple[float, int]]:

@@ -127,6 +127,24 @@ def test_05b_batched_decode_is_the_references(cuda, qwen05b_weights):
     assert np.array_equal(tokens, expected[:, 1:])
 
 
+@pytest.mark.parametrize("rows", [1, 3, 4])
+def test_05b_small_batched_decode_is_the_references(cuda, qwen05b_weights, rows):
+    """A few of config 5's sequences at once: the persistent decode step (up to four rows)."""
+    g = golden("batch")
+    past = int(g["past"])
+    backend = cuda.CUDABackend(device=0, capacity=past + 64, slots=8, max_rows=8)
+    model = Qwen2(QWEN2_0_5B, qwen05b_weights, run=backend, quantization="int8-vnni")
+    pick = [5, 17, 40, 63][:rows]
+    first, keys, values = [], [], []
+    for b in pick:
+        k, v, t = synthetic_cache(QWEN2_0_5B, b, past)
+        keys.append(k)
+        values.append(v)
+        first.append(t)
+    tokens = cuda.batched_greedy(model, first, keys, values, 64)
+    assert np.array_equal(tokens, g["tokens"][pick, 1:])
+
+
 def test_05b_fp32_greedy_is_the_references(cuda, qwen05b_weights):
     """Config 2: float32 projections, 32-token prompt, 128 greedy steps."""
     g = golden("qwen05b_fp32")
