@@ -138,13 +138,27 @@ def build_model(dev: int, slots: int, capacity: int):
     return cfg, wq, model
 
 
+def layer_bytes(cfg, rows: int, past: int) -> float:
+    """One decoder layer's int8 weights, scales, bias and gains, and its KV rows read for `rows` rows."""
+    H, I, d = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    heads, kv = cfg.num_attention_heads, cfg.num_key_value_heads
+    nqkv, hq = (heads + 2 * kv) * d, heads * d
+    weights = nqkv * H + H * hq + 2 * I * H + H * I
+    scales = 4 * (nqkv + H + 2 * I + H) + 4 * nqkv + 2 * 4 * H
+    return weights + scales + rows * 2 * kv * (past + 1) * d * 4
+
+
 def algorithmic_bytes(kind: str, cfg, rows: int, past: int) -> float:
     """Bytes a launch of `kind` must move at least (weights / cache / activations, once each)."""
     H, I, d, V = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim, cfg.vocab_size
     heads, kv = cfg.num_attention_heads, cfg.num_key_value_heads
     nqkv = (heads + 2 * kv) * d
     if kind == "lm_head_argmax":
+        if rows <= 16:        # int8 prefilter: the int8 copy, its row scales, approximations out and back
+            return V * H + V * 4 + rows * (H * 4 + 2 * V * 4)
         return V * H * 4 + rows * H * 4 + rows * V * 4
+    if kind == "persistent_layers":
+        return cfg.num_hidden_layers * layer_bytes(cfg, rows, past)
     if kind == "attention":
         return rows * (2 * kv * (past + 1) * d * 4 + nqkv * 4 + heads * d * 1.25)
     if kind == "down_projection":
@@ -277,10 +291,25 @@ def run_bs1(cfg, model) -> dict:
     with ClockSampler(model.device) as clocks:
         ms = model.decode_timed([first], [0], [BS1_PROMPT], steps)
     profile = model.profile([first], [0], [512], 4)
+    # the whole step against HBM: bytes a token must read (the layers' int8 weights and KV rows at
+    # the workload's mean position, the LM head as read) over the measured time per token
+    peak, source = measured_peaks()
+    mean_past = (BS1_PROMPT + BS1_END - 1) // 2
+    layers = cfg.num_hidden_layers * layer_bytes(cfg, 1, mean_past)
+    head_read = algorithmic_bytes("lm_head_argmax", cfg, 1, mean_past)
+    head_fp32 = cfg.vocab_size * cfg.hidden_size * 4
+    s_per_token = ms / steps / 1000.0
+    step = {"bytes_per_token": layers + head_read, "achieved": round((layers + head_read) / s_per_token / 1e9, 1),
+            "peak": peak, "unit": "GB/s", "frac": round((layers + head_read) / s_per_token / 1e9 / peak, 4),
+            "peak_source": source, "mean_past": mean_past,
+            "note": "the LM head reads an int8 copy of the embedding (plus exact rechecks); with the float32 "
+                    "embedding read instead the same time would be the frac_fp32_head fraction",
+            "bytes_per_token_fp32_head": layers + head_fp32,
+            "frac_fp32_head": round((layers + head_fp32) / s_per_token / 1e9 / peak, 4)}
     return {"value": round(steps / (ms / 1000.0), 1), "unit": "tok/s", "ms_per_token": round(ms / steps, 4),
             "workload": f"batch 1: {BS1_PROMPT}-token prompt, then {steps} greedy decode steps (past "
                         f"{BS1_PROMPT}..{BS1_END - 1}) (configuration 3)",
-            "roofline": roofline(profile, cfg, 1, 512, "bs1"), "clocks": clocks.summary()}
+            "roofline": roofline(profile, cfg, 1, 512, "bs1"), "step_roofline": step, "clocks": clocks.summary()}
 
 
 def run_reference(args) -> dict | None:
