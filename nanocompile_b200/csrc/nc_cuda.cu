@@ -614,15 +614,17 @@ namespace {
 
 // The int8-prefiltered LM head + argmax of up to LMQ_MAXM rows: prefilter, then pick.
 int32_t launch_lm_head_q8(cudaStream_t st, const LmHeadQ8Args &a) {
-    const int ctas = (a.n + LMQ_ROWS - 1) / LMQ_ROWS;
+    const int ctas = (a.n + LMQ_ROWS - 1) / LMQ_ROWS;   // 128-row blocks
     const int T = a.m <= 1 ? 1 : a.m <= 2 ? 2 : a.m <= 4 ? 4 : 8;
-    const dim3 grid(ctas, (a.m + T - 1) / T);
+    const dim3 grid(std::min(ctas, LMQ_PREFILTER_CTAS), (a.m + T - 1) / T);
     if (T == 1) CUDA_TRY(launch_k(lm_head_q8_kernel<1>, grid, LMQ_THREADS, 0, st, a));
     else if (T == 2) CUDA_TRY(launch_k(lm_head_q8_kernel<2>, grid, LMQ_THREADS, 0, st, a));
     else if (T == 4) CUDA_TRY(launch_k(lm_head_q8_kernel<4>, grid, LMQ_THREADS, 0, st, a));
     else CUDA_TRY(launch_k(lm_head_q8_kernel<8>, grid, LMQ_THREADS, 0, st, a));
     NC_TRY(check_launch("lm_head_q8_kernel"));
-    CUDA_TRY(launch_k(lm_head_q8_pick_kernel, LMQ_PICK_CTAS, LMQ_PICK_THREADS, (size_t)a.k * 4, st, a, ctas));
+    const size_t psmem = lmq_pick_smem(a.k);
+    CUDA_TRY(allow_smem(lm_head_q8_pick_kernel, psmem));
+    CUDA_TRY(launch_k(lm_head_q8_pick_kernel, LMQ_PICK_CTAS, LMQ_PICK_THREADS, psmem, st, a, ctas));
     return check_launch("lm_head_q8_pick_kernel");
 }
 

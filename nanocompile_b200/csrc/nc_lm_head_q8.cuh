@@ -31,7 +31,7 @@
 // 2^-100 for roundings in the subnormal range, and max|x| below 2^-100 also makes B infinite.
 #pragma once
 
-#include "nc_kernels.cuh"
+#include "nc_lm_head_tc.cuh"
 
 namespace nc {
 
@@ -43,6 +43,7 @@ constexpr int LMQ_MAXT = 8;         // tokens per prefilter pass
 constexpr int LMQ_MAXM = 16;        // rows of a step the int8 head serves
 constexpr int LMQ_PICK_THREADS = 256;
 constexpr int LMQ_PICK_CTAS = 148;     // one wave of the pick kernel
+constexpr int LMQ_PREFILTER_CTAS = 3 * 148;   // persistent prefilter: three CTAs per SM
 constexpr float LMQ_ABS = 0x1p-100f;   // absolute slack: roundings in the subnormal range
 constexpr float LMQ_BIG = 0x1p90f;     // a larger bound s_n B: the row is a candidate, not a lower bound
 
@@ -104,13 +105,17 @@ __global__ void __launch_bounds__(LMQ_THREADS) lm_head_q8_kernel(const LmHeadQ8A
     __shared__ float s_low[LMQ_THREADS / 32][T];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31, grp = lane >> 3, j = lane & 7;
     const int K = a.k, pieces = K / 128;
-    const int c = blockIdx.x, ctas = gridDim.x, t0 = blockIdx.y * T, tn = min(T, a.m - t0);
-    const int row0 = c * LMQ_ROWS + warp * 4 + grp;
+    // persistent: this CTA takes 128-row blocks blockIdx.x, blockIdx.x + gridDim.x, ... (4 passes of
+    // 32 rows each), the digits prepared once
+    const int ctas = (a.n + LMQ_ROWS - 1) / LMQ_ROWS, t0 = blockIdx.y * T, tn = min(T, a.m - t0);
+    constexpr int PASSES = LMQ_ROWS / 32;
+    const int my_blocks = blockIdx.x < ctas ? (ctas - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    auto pass_row = [&](int p) { return (blockIdx.x + (p / PASSES) * gridDim.x) * LMQ_ROWS + (p % PASSES) * 32 + warp * 4 + grp; };
 
     // the first pass's weights do not depend on the previous kernel
     release_dependents();
     uint4 wv[LMQ_PIECES], wn[LMQ_PIECES];
-    lmq_load(wv, a.q, row0, a.n, K, j, pieces);
+    if (my_blocks) lmq_load(wv, a.q, pass_row(0), a.n, K, j, pieces);
     wait_for_producer();
 
     // per token: max |x|, sum |x|, any non-finite value
@@ -149,7 +154,7 @@ __global__ void __launch_bounds__(LMQ_THREADS) lm_head_q8_kernel(const LmHeadQ8A
         bnd *= 1.0f + 0x1p-8f;
         if (B || M < 0x1p-100f) bnd = __uint_as_float(0x7f800000u);
         s_bnd[t] = bnd;
-        if (c == 0 && t < tn) a.bound[t0 + t] = bnd;
+        if (blockIdx.x == 0 && t < tn) a.bound[t0 + t] = bnd;
     }
     __syncthreads();
     // the digits
@@ -168,30 +173,30 @@ __global__ void __launch_bounds__(LMQ_THREADS) lm_head_q8_kernel(const LmHeadQ8A
     }
     __syncthreads();
 
-    float low = -__uint_as_float(0x7f800000u);     // lane j: token j's largest lower bound
     const float sx_j = j < tn ? s_sx[j] : 0.0f, bnd_j = j < tn ? s_bnd[j] : 0.0f;
-    for (int pass = 0; pass < LMQ_ROWS / 32; ++pass) {
-        const int row = row0 + pass * 32;
-        if (pass + 1 < LMQ_ROWS / 32) lmq_load(wn, a.q, row + 32, a.n, K, j, pieces);
+    float low = -__uint_as_float(0x7f800000u);      // lane j: token j's largest lower bound in the block
+    for (int p = 0; p < my_blocks * PASSES; ++p) {
+        const int row = pass_row(p);
+        if (p + 1 < my_blocks * PASSES) lmq_load(wn, a.q, pass_row(p + 1), a.n, K, j, pieces);
         int hi[T], lo[T];
 #pragma unroll
         for (int u = 0; u < T; ++u) { hi[u] = 0; lo[u] = 0; }
 #pragma unroll
-        for (int p = 0; p < LMQ_PIECES; ++p) {
-            if (p < pieces) {
-                const int off = (p * 8 + j) * 16;
+        for (int q = 0; q < LMQ_PIECES; ++q) {
+            if (q < pieces) {
+                const int off = (q * 8 + j) * 16;
 #pragma unroll
                 for (int u = 0; u < T; ++u) {
                     const uint4 d0 = *reinterpret_cast<const uint4 *>(&xd[u][0][off]);
                     const uint4 d1 = *reinterpret_cast<const uint4 *>(&xd[u][1][off]);
-                    hi[u] = __dp4a((int)wv[p].x, (int)d0.x, hi[u]);
-                    hi[u] = __dp4a((int)wv[p].y, (int)d0.y, hi[u]);
-                    hi[u] = __dp4a((int)wv[p].z, (int)d0.z, hi[u]);
-                    hi[u] = __dp4a((int)wv[p].w, (int)d0.w, hi[u]);
-                    lo[u] = __dp4a((int)wv[p].x, (int)d1.x, lo[u]);
-                    lo[u] = __dp4a((int)wv[p].y, (int)d1.y, lo[u]);
-                    lo[u] = __dp4a((int)wv[p].z, (int)d1.z, lo[u]);
-                    lo[u] = __dp4a((int)wv[p].w, (int)d1.w, lo[u]);
+                    hi[u] = __dp4a((int)wv[q].x, (int)d0.x, hi[u]);
+                    hi[u] = __dp4a((int)wv[q].y, (int)d0.y, hi[u]);
+                    hi[u] = __dp4a((int)wv[q].z, (int)d0.z, hi[u]);
+                    hi[u] = __dp4a((int)wv[q].w, (int)d0.w, hi[u]);
+                    lo[u] = __dp4a((int)wv[q].x, (int)d1.x, lo[u]);
+                    lo[u] = __dp4a((int)wv[q].y, (int)d1.y, lo[u]);
+                    lo[u] = __dp4a((int)wv[q].z, (int)d1.z, lo[u]);
+                    lo[u] = __dp4a((int)wv[q].w, (int)d1.w, lo[u]);
                 }
             }
         }
@@ -215,33 +220,46 @@ __global__ void __launch_bounds__(LMQ_THREADS) lm_head_q8_kernel(const LmHeadQ8A
             const float e = sn * bnd_j;
             if (e < LMQ_BIG) low = fmaxf(low, ap - fadd(e, LMQ_ABS));
         }
-        if (pass + 1 < LMQ_ROWS / 32) {
+        if (p + 1 < my_blocks * PASSES) {
 #pragma unroll
-            for (int p = 0; p < LMQ_PIECES; ++p) wv[p] = wn[p];
+            for (int q = 0; q < LMQ_PIECES; ++q) wv[q] = wn[q];
         }
-    }
-    // the CTA's largest lower bound per token
-    low = fmaxf(low, __shfl_xor_sync(0xffffffffu, low, 8));
-    low = fmaxf(low, __shfl_xor_sync(0xffffffffu, low, 16));
-    if (lane < T) s_low[warp][lane] = low;
-    __syncthreads();
-    if (t < tn) {
-        float v = s_low[0][t];
-        for (int w = 1; w < LMQ_THREADS / 32; ++w) v = fmaxf(v, s_low[w][t]);
-        a.cta_low[(int64_t)(t0 + t) * ctas + c] = v;
+        if (p % PASSES == PASSES - 1) {
+            // the block's largest lower bound per token
+            low = fmaxf(low, __shfl_xor_sync(0xffffffffu, low, 8));
+            low = fmaxf(low, __shfl_xor_sync(0xffffffffu, low, 16));
+            if (lane < T) s_low[warp][lane] = low;
+            __syncthreads();
+            if (t < tn) {
+                float v = s_low[0][t];
+                for (int w = 1; w < LMQ_THREADS / 32; ++w) v = fmaxf(v, s_low[w][t]);
+                a.cta_low[(int64_t)(t0 + t) * ctas + blockIdx.x + (p / PASSES) * gridDim.x] = v;
+            }
+            __syncthreads();
+            low = -__uint_as_float(0x7f800000u);
+        }
     }
 }
 
-// One pass over the candidates of every token; grid = any number of CTAs.
+// Per token: L, this CTA's share of the rows (strided over the grid) tested against it, the
+// survivors listed in shared memory, then rechecked exactly one per warp. grid = any number of
+// CTAs; shared memory = K floats (x) + 16 x K floats (two staged rows per warp) + the list.
+constexpr int LMQ_LIST = 4096;     // candidate slots per CTA (more than its rows per token at 148 CTAs)
+
+__host__ __device__ inline size_t lmq_pick_smem(int k) { return sizeof(float) * (size_t)(17 * k) + sizeof(int) * LMQ_LIST; }
+
 __global__ void __launch_bounds__(LMQ_PICK_THREADS)
 lm_head_q8_pick_kernel(const LmHeadQ8Args a, int ctas) {
-    extern __shared__ __align__(16) float pxs[];   // [K]
+    extern __shared__ __align__(16) float pxs[];       // [K] x | [8][K] staged rows | list
     __shared__ float rv[LMQ_PICK_THREADS / 32];
     __shared__ int ri[LMQ_PICK_THREADS / 32];
     __shared__ float s_low;
+    __shared__ int s_count;
     __shared__ bool s_last;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int K = a.k, k4 = K / 4;
+    const int K = a.k;
+    float *rowbuf = pxs + K + warp * 2 * K;            // two staged rows per warp
+    int *list = reinterpret_cast<int *>(pxs + 17 * K);
     const int64_t gt = (int64_t)blockIdx.x * LMQ_PICK_THREADS + t, stride = (int64_t)gridDim.x * LMQ_PICK_THREADS;
     release_dependents();
     wait_for_producer();
@@ -252,6 +270,7 @@ lm_head_q8_pick_kernel(const LmHeadQ8Args a, int ctas) {
         for (int c = t; c < ctas; c += LMQ_PICK_THREADS) g = fmaxf(g, a.cta_low[(int64_t)m * ctas + c]);
         for (int o = 16; o > 0; o >>= 1) g = fmaxf(g, __shfl_xor_sync(0xffffffffu, g, o));
         if (lane == 0) rv[warp] = g;
+        if (t == 0) s_count = 0;
         __syncthreads();
         if (t == 0) {
             float b = rv[0];
@@ -260,35 +279,29 @@ lm_head_q8_pick_kernel(const LmHeadQ8Args a, int ctas) {
         }
         __syncthreads();
         const float L = s_low, B = a.bound[m];
-        const float4 *xs4 = reinterpret_cast<const float4 *>(pxs);
-        float bv = -__uint_as_float(0x7f800000u);
-        int bi = 0x7fffffff;
         for (int64_t n = gt; n < a.n; n += stride) {
             const float e = a.s[n] * B;
             if (e < LMQ_BIG && a.approx[(int64_t)m * a.n + n] + fadd(e, LMQ_ABS) < L) continue;   // NaN: a candidate
-            const float4 *wr4 = reinterpret_cast<const float4 *>(a.w + n * K);
-            float4 buf[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) buf[q] = wr4[q];
-            float acc = 0.0f;                           // the reference's in-order dot product
-            for (int c = 0; c < k4; c += 8) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 wv = buf[q];
-                    if (c + 8 + q < k4) buf[q] = wr4[c + 8 + q];
-                    const float4 xv = xs4[c + q];
-                    acc = fadd(acc, fmul(xv.x, wv.x));
-                    acc = fadd(acc, fmul(xv.y, wv.y));
-                    acc = fadd(acc, fmul(xv.z, wv.z));
-                    acc = fadd(acc, fmul(xv.w, wv.w));
-                }
-            }
-            if (argmax_better(acc, (int)n, bv, bi)) { bv = acc; bi = (int)n; }
+            const int at = atomicAdd(&s_count, 1);
+            if (at < LMQ_LIST) list[at] = (int)n;
         }
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (argmax_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        __syncthreads();
+        const int count = min(s_count, LMQ_LIST);
+        float bv = -__uint_as_float(0x7f800000u);
+        int bi = 0x7fffffff;
+        // the list; or, when it overflowed, every row of this CTA's share, a list at a time
+        const bool overflow = s_count > LMQ_LIST;
+        for (int64_t base = (int64_t)blockIdx.x * LMQ_PICK_THREADS;; base += stride) {
+            int cnt = count;
+            if (overflow) {
+                if (base >= a.n) break;
+                __syncthreads();
+                if (base + t < a.n) list[t] = (int)(base + t);
+                __syncthreads();
+                cnt = (int)(a.n - base < LMQ_PICK_THREADS ? a.n - base : LMQ_PICK_THREADS);
+            }
+            best_of_list_warp(a.w, list, warp, LMQ_PICK_THREADS / 32, cnt, pxs, rowbuf, K, bv, bi);
+            if (!overflow) break;
         }
         __syncthreads();
         if (lane == 0) { rv[warp] = bv; ri[warp] = bi; }

@@ -340,7 +340,69 @@ lm_head_tc_kernel(const LmHeadTcArgs a) {
 constexpr int LMP_THREADS = 256;
 constexpr int LMP_LIST = 4096;
 
-__host__ __device__ inline size_t lm_pick_smem(int k) { return sizeof(float) * (size_t)k + sizeof(int) * LMP_LIST; }
+__host__ __device__ inline size_t lm_pick_smem(int k) { return sizeof(float) * (size_t)(17 * k) + sizeof(int) * LMP_LIST; }
+
+// The reference's in-order dot product of x and w (both in shared memory, 16-byte aligned,
+// n a multiple of 16), one thread: the next 16 products' operands are loaded while the current
+// 16 are added.
+__device__ __forceinline__ float chain_dot(const float *x, const float *w, int n) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x), *w4 = reinterpret_cast<const float4 *>(w);
+    float acc = 0.0f;
+    float4 xa[4], wa[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) { xa[u] = x4[u]; wa[u] = w4[u]; }
+    for (int i = 0; i < n / 4; i += 4) {
+        float4 xb[4], wb[4];
+        const bool more = i + 4 < n / 4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (more) { xb[u] = x4[i + 4 + u]; wb[u] = w4[i + 4 + u]; }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            acc = fadd(acc, fmul(xa[u].x, wa[u].x));
+            acc = fadd(acc, fmul(xa[u].y, wa[u].y));
+            acc = fadd(acc, fmul(xa[u].z, wa[u].z));
+            acc = fadd(acc, fmul(xa[u].w, wa[u].w));
+        }
+        if (more) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) { xa[u] = xb[u]; wa[u] = wb[u]; }
+        }
+    }
+    return acc;
+}
+
+// One warp: the best (np.argmax order) exact logit among list[first], list[first + step], ...
+// (count entries): each row comes into shared memory (buf, two k-float halves) by coalesced loads,
+// the next row's loads in flight while lane 0 forms the current row's in-order dot with xs.
+// k <= 1024. Updates (bv, bi) in lane 0.
+__device__ __forceinline__ void best_of_list_warp(const float *w, const int *list, int first, int step, int count,
+                                                  const float *xs, float *buf, int k, float &bv, int &bi) {
+    const int lane = threadIdx.x & 31, k4 = k / 4;
+    float4 r[8];
+    auto fetch = [&](int i) {
+        const float4 *src = reinterpret_cast<const float4 *>(w + (int64_t)list[i] * k);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (lane + 32 * u < k4) r[u] = src[lane + 32 * u];
+    };
+    if (first < count) fetch(first);
+    int slot = 0;
+    for (int i = first; i < count; i += step) {
+        float *b = buf + slot * k;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (lane + 32 * u < k4) reinterpret_cast<float4 *>(b)[lane + 32 * u] = r[u];
+        __syncwarp();
+        if (i + step < count) fetch(i + step);
+        if (lane == 0) {
+            const float v = chain_dot(xs, b, k);
+            if (argmax_better(v, list[i], bv, bi)) { bv = v; bi = list[i]; }
+        }
+        slot ^= 1;
+    }
+    __syncwarp();
+}
 
 __global__ void __launch_bounds__(LMP_THREADS)
 lm_head_pick_kernel(const LmHeadTcArgs a, const float *x, const float *w, int ctas, int64_t *tokens) {
@@ -352,7 +414,8 @@ lm_head_pick_kernel(const LmHeadTcArgs a, const float *x, const float *w, int ct
     const int m = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int K = a.k;
     float *xs = psm;                                   // [K]
-    int *list = reinterpret_cast<int *>(psm + K);
+    float *rowbuf = psm + K;                           // [8 warps][2][K] staged candidate rows
+    int *list = reinterpret_cast<int *>(psm + 17 * K);
     release_dependents();
     wait_for_producer();
     const float delta = a.delta[m];
@@ -396,29 +459,7 @@ lm_head_pick_kernel(const LmHeadTcArgs a, const float *x, const float *w, int ct
     const int count = min(s_count, LMP_LIST);
     float bv = -__uint_as_float(0x7f800000u);
     int bi = 0x7fffffff;
-    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    const int k4 = K / 4;                              // K is a multiple of 32
-    for (int i = t; i < count; i += LMP_THREADS) {
-        const int row = list[i];
-        const float4 *wr4 = reinterpret_cast<const float4 *>(w + (int64_t)row * K);
-        float4 buf[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) buf[j] = wr4[j];
-        float acc = 0.0f;                              // the reference's in-order dot product
-        for (int c = 0; c < k4; c += 8) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 wv = buf[j];
-                if (c + 8 + j < k4) buf[j] = wr4[c + 8 + j];
-                const float4 xv = xs4[c + j];
-                acc = fadd(acc, fmul(xv.x, wv.x));
-                acc = fadd(acc, fmul(xv.y, wv.y));
-                acc = fadd(acc, fmul(xv.z, wv.z));
-                acc = fadd(acc, fmul(xv.w, wv.w));
-            }
-        }
-        if (argmax_better(acc, row, bv, bi)) { bv = acc; bi = row; }
-    }
+    best_of_list_warp(w, list, warp, LMP_THREADS / 32, count, xs, rowbuf + warp * 2 * K, K, bv, bi);
     if (s_count > LMP_LIST && warp == 0) {
         // more candidates than the list holds (non-finite inputs): every row, straight from memory
         for (int row = lane; row < a.n; row += 32) {
