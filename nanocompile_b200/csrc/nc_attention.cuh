@@ -51,6 +51,17 @@ __host__ __device__ inline size_t attention_batched_smem(int d, int cap) {
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// Asks L2 for bytes from p (16-byte aligned start and size), in requests of at most 1 MB.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, int64_t bytes) {
+    const char *c = (const char *)p;
+    while (bytes > 0) {
+        const int n = (int)(bytes < (1 << 20) ? bytes : (1 << 20));
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+        c += n;
+        bytes -= n;
+    }
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
@@ -277,6 +288,9 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         cp_async_wait<ATB_STAGES - 2>();
         return true;
     };
+    // the whole K history into L2 now (its chunks stream through the two stages while the scores
+    // are formed), the V history when the last K chunk is in (it arrives during the softmax)
+    if (t == 0) prefetch_l2_bulk(K, (int64_t)len * D * sizeof(float));
     for (int i = 0; i < ATB_STAGES - 1; ++i) issue(i);
 
     // ---- scores: thread (position of the chunk, half of the 8 head rows), four chains ----
@@ -323,6 +337,7 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         }
     }
     if (failed_at >= 0) goto fault;
+    if (t == 0) prefetch_l2_bulk(V, (int64_t)len * D * sizeof(float));
     {
         // per-head maxima: warps 0..7 hold heads 0..3, warps 8..15 heads 4..7
 #pragma unroll

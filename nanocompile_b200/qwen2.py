@@ -87,6 +87,9 @@ class Qwen2Config:
 # The configurations the benchmark and the tests use.
 TINY = Qwen2Config(256, 64, 128, 2, 4, 2, 1e-6, 1e6, True)
 QWEN2_0_5B = Qwen2Config(151936, 896, 4864, 24, 14, 2, 1e-6, 1e6, True)
+# The smallest shape of the 0.5B model's kind (head dim 64, widths of whole 128-byte chunks): the
+# few-row decode runs through the persistent step and the int8-prefiltered LM head, as 0.5B does.
+SMALL = Qwen2Config(512, 128, 256, 2, 2, 1, 1e-6, 1e6, True)
 
 
 def inverse_frequencies(head_dim: int, theta: float) -> np.ndarray:

@@ -11,7 +11,7 @@ import hashlib
 import numpy as np
 import pytest
 
-from nanocompile_b200.qwen2 import QWEN2_0_5B, TINY, Qwen2, greedy, synthetic_cache, synthetic_weights
+from nanocompile_b200.qwen2 import QWEN2_0_5B, SMALL, TINY, Qwen2, greedy, synthetic_cache, synthetic_weights
 from tests.conftest import bits, golden
 
 pytestmark = pytest.mark.gpu
@@ -72,6 +72,40 @@ def test_bad_token_ids_raise_kernel_error(tiny_models, cuda):
     with pytest.raises(cuda.KernelError, match="index -1"):
         model.forward([-1])
     assert greedy(model, [1, 2], 2) == greedy(model, [1, 2], 2)      # the model still works after
+
+
+def oracle_decode(oracle, first, keys, values, steps):
+    """Greedy tokens of one sequence after its cached history, step by step on the CPU oracle."""
+    out, token = [], first
+    for _ in range(steps):
+        logits, k, v = oracle.step([token], keys, values)
+        keys, values = np.concatenate([keys, k], 2), np.concatenate([values, v], 2)
+        token = int(np.argmax(logits[0]))
+        out.append(token)
+    return out
+
+
+@pytest.mark.parametrize("rows", [1, 2, 4])
+def test_small_persistent_step_is_the_oracles(cuda, rows):
+    """SMALL through the persistent step + int8 LM head (1..4 rows), against the oracle."""
+    from oracle.oracle import OracleModel
+
+    w = synthetic_weights(SMALL, seed=3)
+    backend = cuda.CUDABackend(device=0, capacity=200, slots=4, max_rows=8)
+    model = Qwen2(SMALL, w, run=backend, quantization="int8-vnni")
+    oracle = OracleModel(SMALL, model.weights, "int8")
+    first, keys, values = [], [], []
+    for b in range(rows):
+        k, v, t = synthetic_cache(SMALL, 7 + b, 37 + 29 * b)
+        keys.append(k)
+        values.append(v)
+        first.append(t)
+    tokens = cuda.batched_greedy(model, first, keys, values, 24)     # ragged histories, one replay per step
+    for b in range(rows):
+        assert list(tokens[b]) == oracle_decode(oracle, first[b], keys[b], values[b], 24), b
+    compiled = backend.compiled(model.graph_last, model.weights)
+    kinds = compiled.model.profile(first, list(range(rows)), [k.shape[2] for k in keys], 1)
+    assert "persistent_layers" in kinds and "lm_head_argmax" in kinds, kinds
 
 
 @pytest.fixture(scope="module")
