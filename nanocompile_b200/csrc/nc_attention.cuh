@@ -374,22 +374,23 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             s_rcp[t] = __frcp_rn(sum);
         }
         __syncthreads();
-        for (int h = 0; h < G; ++h) {
-            const float sh = s_sum[h], rh = s_rcp[h];
-            float *eh = e + h * cap4;
-            for (int j = 4 * t; j < len; j += 4 * ATB_THREADS) {
-                float4 v = *reinterpret_cast<float4 *>(eh + j);
-                v.x = fdiv_recip(v.x, sh, rh);
-                v.y = fdiv_recip(v.y, sh, rh);
-                v.z = fdiv_recip(v.z, sh, rh);
-                v.w = fdiv_recip(v.w, sh, rh);
-                *reinterpret_cast<float4 *>(eh + j) = v;
-            }
-        }
     }
     {
         // ---- probabilities @ V: thread (dimension, head pair), positions in order ----
+        // The divisions e / sum of a chunk are made by the threads without P.V work while the P.V
+        // threads consume the chunk before it (chunk 0 before the loop); the barrier that opens
+        // each chunk orders the two.
         const bool pv = t < PV_THREADS;
+        static_assert(ATB_THREADS - PV_THREADS >= 32, "threads left for the divisions");
+        auto divide_chunk = [&](int ci) {
+            if (pv || ci >= nk) return;
+            const int u = t - PV_THREADS, j0 = ci * ATB_CHUNK;
+            for (int i = u; i < G * ATB_CHUNK; i += ATB_THREADS - PV_THREADS) {
+                const int h = i / ATB_CHUNK, j = j0 + i % ATB_CHUNK;
+                if (j < len) e[h * cap4 + j] = fdiv_recip(e[h * cap4 + j], s_sum[h], s_rcp[h]);
+            }
+        };
+        divide_chunk(0);
         const int dim = t % D, hp = 2 * (t / D);
         const float *p0 = e + min(hp, G - 1) * cap4, *p1 = e + min(hp + 1, G - 1) * cap4;   // past G: discarded
         // where row k (mod 8) of a staged V chunk keeps this thread's dimension
@@ -410,6 +411,7 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             const bool ok = ready(idx);
             if (__syncthreads_or(!ok)) { failed_at = idx; break; }
             issue(idx + ATB_STAGES - 1);
+            divide_chunk(ci + 1);
             if (pv) {
                 const float *st = ring + (idx % ATB_STAGES) * STAGE;
                 const int j0 = ci * ATB_CHUNK;
