@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(LMQ_THREADS) lm_head_q8_kernel(const LmHeadQ8A
 // Per token: L, this CTA's share of the rows (strided over the grid) tested against it, the
 // survivors listed in shared memory, then rechecked exactly one per warp. grid = any number of
 // CTAs; shared memory = K floats (x) + 16 x K floats (two staged rows per warp) + the list.
+constexpr int LMQ_SCAN = 8;        // rows a pick thread tests per round (151,936 rows take one round)
 constexpr int LMQ_LIST = 4096;     // candidate slots per CTA (more than its rows per token at 148 CTAs)
 
 __host__ __device__ inline size_t lmq_pick_smem(int k) { return sizeof(float) * (size_t)(17 * k) + sizeof(int) * LMQ_LIST; }
@@ -265,6 +266,17 @@ lm_head_q8_pick_kernel(const LmHeadQ8Args a, int ctas) {
     wait_for_producer();
     for (int m = 0; m < a.m; ++m) {
         __syncthreads();
+        // the first round of this thread's approximations and scales, requested before L is known
+        float ap[LMQ_SCAN], sv[LMQ_SCAN];
+        auto fetch = [&](int64_t n0) {
+#pragma unroll
+            for (int u = 0; u < LMQ_SCAN; ++u) {
+                const int64_t n = n0 + u * stride;
+                ap[u] = n < a.n ? a.approx[(int64_t)m * a.n + n] : 0.0f;
+                sv[u] = n < a.n ? a.s[n] : 0.0f;
+            }
+        };
+        fetch(gt);
         for (int k = t; k < K; k += LMQ_PICK_THREADS) pxs[k] = a.x[(int64_t)m * K + k];
         float g = -__uint_as_float(0x7f800000u);
         for (int c = t; c < ctas; c += LMQ_PICK_THREADS) g = fmaxf(g, a.cta_low[(int64_t)m * ctas + c]);
@@ -279,11 +291,18 @@ lm_head_q8_pick_kernel(const LmHeadQ8Args a, int ctas) {
         }
         __syncthreads();
         const float L = s_low, B = a.bound[m];
-        for (int64_t n = gt; n < a.n; n += stride) {
-            const float e = a.s[n] * B;
-            if (e < LMQ_BIG && a.approx[(int64_t)m * a.n + n] + fadd(e, LMQ_ABS) < L) continue;   // NaN: a candidate
-            const int at = atomicAdd(&s_count, 1);
-            if (at < LMQ_LIST) list[at] = (int)n;
+        // this thread's rows, LMQ_SCAN at a time with all their loads in flight together
+        for (int64_t n0 = gt; n0 < a.n; n0 += LMQ_SCAN * stride) {
+            if (n0 != gt) fetch(n0);
+#pragma unroll
+            for (int u = 0; u < LMQ_SCAN; ++u) {
+                const int64_t n = n0 + u * stride;
+                if (n >= a.n) break;
+                const float e = sv[u] * B;
+                if (e < LMQ_BIG && ap[u] + fadd(e, LMQ_ABS) < L) continue;   // NaN: a candidate
+                const int at = atomicAdd(&s_count, 1);
+                if (at < LMQ_LIST) list[at] = (int)n;
+            }
         }
         __syncthreads();
         const int count = min(s_count, LMQ_LIST);
