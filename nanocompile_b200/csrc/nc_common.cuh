@@ -256,7 +256,14 @@ __device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.
             i += 32;
         }
     }
-    for (; i < n; ++i) acc = fadd(acc, p[i]);
+    if (i < n) {                        // the last n % 32: all loads first, then the adds in order
+        float tv[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) tv[u] = i + u < n ? p[i + u] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 32; ++u)
+            if (i + u < n) acc = fadd(acc, tv[u]);
+    }
     return acc;
 }
 
