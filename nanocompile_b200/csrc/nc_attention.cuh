@@ -14,13 +14,21 @@
 //    Where no tensor map can describe the cache (its extent is not known, or the head dimension is
 //    not a multiple of 32) the same kernel stages by cp.async: per thread eight 16-byte copies per
 //    chunk at offsets computed once, K pieces XOR-swizzled by row.
-//  * 512 threads (16 warps) per CTA: every phase is a chain of dependent float operations, and
-//    warps are what hides their latency.
-//  * Scores: two threads per position of a 256-row chunk (four heads each), the K row in
-//    registers once, the four heads' dot products interleaved (q broadcast from shared memory).
-//  * Probabilities are kept head-major ([8][cap]): the in-order sums read them contiguously and a
-//    P.V thread -- one dimension, two heads, two chains -- reads four positions of a head with one
-//    broadcast load; V is read through offsets precomputed for the eight swizzle phases.
+//  * 512 threads (16 warps) per CTA; each phase takes the threads its shared-memory traffic can
+//    feed. A 16-byte load costs four shared-memory wavefronts even as a broadcast, so the phases
+//    are laid out for few loads per product rather than for many threads.
+//  * Scores: a thread takes two positions of a 256-row chunk and four heads (K pieces of two
+//    rows and q pieces of four heads per step of four dimensions: eight chains).
+//  * The exps of chunk c + 1 are made by fifteen warps while warp 0 adds chunk c to the in-order
+//    sums of its G heads.
+//  * Probabilities are kept head-major ([8][cap]); a P.V warp takes one head, a thread two
+//    adjacent dimensions (two chains): one 8-byte V load and one broadcast probability per
+//    position, no padding head. V is read through offsets precomputed for the eight swizzle
+//    phases.
+//  * The chunk holding the new position gets the new k / v row written into its stage, so the
+//    scores and P.V read one layout.
+//  * Decode streams the K history (cached by earlier steps) from before the wait on the previous
+//    kernel.
 //  * The division by the softmax sum is a reciprocal multiply with a residual check that proves
 //    the correctly rounded quotient (fdiv_recip), the IEEE divide where it cannot.
 #pragma once
@@ -34,7 +42,7 @@ namespace nc {
 __device__ unsigned int g_attention_fault;     // set when a TMA stage never completed (bounded wait)
 
 constexpr int ATB_THREADS = 512;
-constexpr int ATB_CHUNK = 256;     // positions per stage; two scoring threads per position
+constexpr int ATB_CHUNK = 256;     // positions per stage
 constexpr int ATB_STAGES = 2;
 constexpr int ATB_HEADS = 8;       // query heads per CTA at most
 
@@ -158,7 +166,7 @@ __device__ __forceinline__ float pv_chain(float acc, const float *p, int n, V &&
     return acc;
 }
 
-// Logical piece c (16 bytes) of row `row` of a staged K chunk, and element `dim` of a V row.
+// Logical piece c (16 bytes) of row `row` of a staged K chunk.
 template <int D, bool TMA>
 __device__ __forceinline__ float4 staged_piece(const float *stage, int row, int c) {
     if constexpr (TMA) {
@@ -168,14 +176,21 @@ __device__ __forceinline__ float4 staged_piece(const float *stage, int row, int 
         return reinterpret_cast<const float4 *>(stage)[row * (D / 4) + (c ^ (row % (D / 4)))];
     }
 }
+// Where element `dim` of row `row` of a staged V chunk sits (TMA: of a K chunk as well).
 template <int D, bool TMA>
-__device__ __forceinline__ float staged_elem(const float *stage, int row, int dim) {
+__device__ __forceinline__ int staged_index(int row, int dim) {
     if constexpr (TMA) {
         const int b = dim / ATB_BOX, col = dim % ATB_BOX;
-        return stage[b * ATB_CHUNK * ATB_BOX + row * ATB_BOX + ((((col >> 2) ^ (row & 7)) << 2) | (col & 3))];
+        return b * ATB_CHUNK * ATB_BOX + row * ATB_BOX + ((((col >> 2) ^ (row & 7)) << 2) | (col & 3));
     } else {
-        return stage[row * D + dim];
+        return row * D + dim;
     }
+}
+// The same for a staged K chunk: cp.async chunks swizzle K's 16-byte pieces by row (staged_piece).
+template <int D, bool TMA>
+__device__ __forceinline__ int staged_k_index(int row, int dim) {
+    if constexpr (TMA) return staged_index<D, TMA>(row, dim);
+    else return row * D + ((((dim >> 2) ^ (row % (D / 4))) << 2) | (dim & 3));
 }
 
 template <int D, int G, bool TMA>
@@ -188,16 +203,20 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
     constexpr int NP = ATB_CHUNK * PPR / ATB_THREADS; // cp.async: 16-byte pieces a thread copies per chunk
     static_assert(ATB_THREADS % PPR == 0 && NP >= 1, "piece layout");
     constexpr int STAGE = ATB_CHUNK * D;              // floats per stage
-    constexpr int SH = 4;                             // heads per scoring thread (two threads per position)
-    constexpr int PV_THREADS = D * ATB_HEADS / 2;     // P.V: (dimension, head pair)
+    constexpr int SP = 2, SH = 4;                     // scores: positions x heads per thread
+    constexpr int SROWS = ATB_CHUNK / SP;             // position groups of a chunk
+    constexpr int S_THREADS = SROWS * ((G + SH - 1) / SH);
+    constexpr int PV_HEADS = 1;                       // P.V: (dimension pair, PV_HEADS heads)
+    constexpr int DP = D / 2, PV_THREADS = DP * ((G + PV_HEADS - 1) / PV_HEADS);
+    constexpr int QUADS = ATB_CHUNK / 4;              // exps: four positions of one head per item
+    static_assert(S_THREADS % 32 == 0 && S_THREADS <= ATB_THREADS, "scoring warps");
+    static_assert(ATB_THREADS - PV_THREADS >= 32, "threads left for the divisions");
     extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ uint64_t bars[ATB_STAGES];
     __shared__ uint64_t tab[32];
     __shared__ float s_max[ATB_HEADS], s_sum[ATB_HEADS], s_rcp[ATB_HEADS];
     __shared__ float wmax[ATB_THREADS / 32][SH];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    release_dependents();
-    wait_for_producer();
 
     const int r = blockIdx.x / a.kv, g = blockIdx.x % a.kv, h0 = g * G;
     const int pos = a.pos[r], len = pos + 1, slot = a.slot[r], cap4 = atb_cap4(a.cap);
@@ -215,36 +234,6 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
     float *base = a.cache + (int64_t)slot * a.slot_stride;
     float *K = base + (int64_t)g * a.cap * D;
     float *V = base + ((int64_t)a.kv + g) * a.cap * D;
-    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
-    const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
-    // RoPE of the group's q heads (rows past G zero) and of the new k; the new v
-    for (int i = t; i < (ATB_HEADS + 2) * D; i += ATB_THREADS) {
-        const int h = i / D, c = i % D;
-        if (h < ATB_HEADS && h >= G) {
-            q[h * D + c] = 0.0f;
-            continue;
-        }
-        const float *src = h < ATB_HEADS ? qkv + (h0 + h) * D
-                                         : (h == ATB_HEADS ? qkv + (a.heads + g) * D : qkv + (a.heads + a.kv + g) * D);
-        if (h == ATB_HEADS + 1) {
-            vn[c] = src[c];
-            continue;
-        }
-        const float t1 = src[c];
-        const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
-        const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
-        if (h < ATB_HEADS) q[h * D + c] = v;
-        else kn[c] = v;
-    }
-    __syncthreads();
-    if (a.mode != 2) {
-        for (int c = t; c < D; c += ATB_THREADS) {
-            K[(int64_t)pos * D + c] = kn[c];
-            V[(int64_t)pos * D + c] = vn[c];
-        }
-        if (a.mode == 1) return;
-    }
-    const bool own_new = a.mode == 0;    // position pos comes from kn / vn, not the cache
 
     // The ring sequence: K chunks 0..nk-1, then V chunks 0..nk-1.
     const int nk = (len + ATB_CHUNK - 1) / ATB_CHUNK;
@@ -288,13 +277,68 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         cp_async_wait<ATB_STAGES - 2>();
         return true;
     };
-    // the whole K history into L2 now (its chunks stream through the two stages while the scores
-    // are formed), the V history when the last K chunk is in (it arrives during the softmax)
-    if (t == 0) prefetch_l2_bulk(K, (int64_t)len * D * sizeof(float));
-    for (int i = 0; i < ATB_STAGES - 1; ++i) issue(i);
+    // Decode (mode 0): the cached rows come from earlier steps, not from the previous kernel, so
+    // the K history starts towards L2 and the first chunk towards shared memory before the wait.
+    // The whole K history goes into L2 (its chunks stream through the two stages while the scores
+    // are formed), the V history when the last K chunk is in (it arrives during the softmax).
+    const bool early = a.mode == 0;
+    if (early) {
+        if (t == 0) prefetch_l2_bulk(K, (int64_t)len * D * sizeof(float));
+        for (int i = 0; i < ATB_STAGES - 1; ++i) issue(i);
+    }
+    release_dependents();
+    wait_for_producer();
 
-    // ---- scores: thread (position of the chunk, half of the 8 head rows), four chains ----
-    const int srow = t % ATB_CHUNK, hb = (t / ATB_CHUNK) * SH;
+    const float *qkv = a.qkv + (int64_t)r * (a.heads + 2 * a.kv) * D;
+    const float *cs = a.cos_tab + (int64_t)pos * HALF, *sn = a.sin_tab + (int64_t)pos * HALF;
+    // RoPE of the group's q heads (rows past G zero) and of the new k; the new v
+    for (int i = t; i < (ATB_HEADS + 2) * D; i += ATB_THREADS) {
+        const int h = i / D, c = i % D;
+        if (h < ATB_HEADS && h >= G) {
+            q[h * D + c] = 0.0f;
+            continue;
+        }
+        const float *src = h < ATB_HEADS ? qkv + (h0 + h) * D
+                                         : (h == ATB_HEADS ? qkv + (a.heads + g) * D : qkv + (a.heads + a.kv + g) * D);
+        if (h == ATB_HEADS + 1) {
+            vn[c] = src[c];
+            continue;
+        }
+        const float t1 = src[c];
+        const float rot = c < HALF ? -src[c + HALF] : src[c - HALF];
+        const float v = fadd(fmul(t1, cs[c % HALF]), fmul(rot, sn[c % HALF]));
+        if (h < ATB_HEADS) q[h * D + c] = v;
+        else kn[c] = v;
+    }
+    __syncthreads();
+    if (a.mode != 2) {
+        for (int c = t; c < D; c += ATB_THREADS) {
+            K[(int64_t)pos * D + c] = kn[c];
+            V[(int64_t)pos * D + c] = vn[c];
+        }
+        if (a.mode == 1) return;
+    }
+    const bool own_new = a.mode == 0;    // position pos comes from kn / vn, not the cache
+    if (!early) {
+        if (t == 0) prefetch_l2_bulk(K, (int64_t)len * D * sizeof(float));
+        for (int i = 0; i < ATB_STAGES - 1; ++i) issue(i);
+    }
+    // Decode: the staged chunk that holds position pos gets the new row from kn / vn, so every
+    // phase reads one layout. Rows written by the threads go to the async proxy (the ring stage
+    // is loaded by TMA again later) behind a proxy fence.
+    auto own_row = [&](float *st, int row, const float *src, bool is_k) {
+        for (int c = t; c < D; c += ATB_THREADS)
+            st[is_k ? staged_k_index<D, TMA>(row, c) : staged_index<D, TMA>(row, c)] = src[c];
+        if (TMA) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+    };
+
+    // ---- scores: thread (two positions of the chunk, four heads), eight chains ----
+    // Per step of four dimensions a thread loads two K pieces and four q pieces (broadcast) for
+    // 32 products: fewer 16-byte loads per product than one position per thread, and eight warps
+    // (two per scheduler) to hide the chains' latency.
+    const int pq = t % SROWS, hb = (t / SROWS) * SH;
+    const bool scorer = t < S_THREADS;
     float mx[SH];
 #pragma unroll
     for (int h = 0; h < SH; ++h) mx[h] = __uint_as_float(0xff800000u);
@@ -303,50 +347,59 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         const bool ok = ready(ci);
         if (__syncthreads_or(!ok)) { failed_at = ci; break; }
         issue(ci + ATB_STAGES - 1);
-        const int j = ci * ATB_CHUNK + srow;
-        if (j < len) {
-            float4 kr[PPR];
-            if (own_new && j == pos) {
+        const int j0 = ci * ATB_CHUNK;
+        float *st = ring + (ci % ATB_STAGES) * STAGE;
+        if (own_new && ci == nk - 1) own_row(st, pos - j0, kn, true);
+        if (scorer) {
+            float acc[SP][SH];
 #pragma unroll
-                for (int c = 0; c < PPR; ++c) kr[c] = reinterpret_cast<const float4 *>(kn)[c];
-            } else {
-                const float *st = ring + (ci % ATB_STAGES) * STAGE;
+            for (int i = 0; i < SP; ++i)
 #pragma unroll
-                for (int c = 0; c < PPR; ++c) kr[c] = staged_piece<D, TMA>(st, srow, c);
-            }
-            float acc[SH];
-#pragma unroll
-            for (int h = 0; h < SH; ++h) acc[h] = 0.0f;
+                for (int h = 0; h < SH; ++h) acc[i][h] = 0.0f;
 #pragma unroll
             for (int c = 0; c < PPR; ++c) {
+                float4 kr[SP];
+#pragma unroll
+                for (int i = 0; i < SP; ++i) kr[i] = staged_piece<D, TMA>(st, pq + i * SROWS, c);
 #pragma unroll
                 for (int h = 0; h < SH; ++h) {
                     const float4 x = reinterpret_cast<const float4 *>(q + (hb + h) * D)[c];
-                    acc[h] = fadd(acc[h], fmul(x.x, kr[c].x));
-                    acc[h] = fadd(acc[h], fmul(x.y, kr[c].y));
-                    acc[h] = fadd(acc[h], fmul(x.z, kr[c].z));
-                    acc[h] = fadd(acc[h], fmul(x.w, kr[c].w));
+#pragma unroll
+                    for (int i = 0; i < SP; ++i) {
+                        acc[i][h] = fadd(acc[i][h], fmul(x.x, kr[i].x));
+                        acc[i][h] = fadd(acc[i][h], fmul(x.y, kr[i].y));
+                        acc[i][h] = fadd(acc[i][h], fmul(x.z, kr[i].z));
+                        acc[i][h] = fadd(acc[i][h], fmul(x.w, kr[i].w));
+                    }
                 }
             }
 #pragma unroll
-            for (int h = 0; h < SH; ++h) {
-                const float sc = fadd(fmul(acc[h], a.scale), 0.0f);
-                e[(hb + h) * cap4 + j] = sc;
-                mx[h] = nan_max(mx[h], sc);
+            for (int i = 0; i < SP; ++i) {
+                const int j = j0 + pq + i * SROWS;
+                if (j < len) {
+#pragma unroll
+                    for (int h = 0; h < SH; ++h) {
+                        const float sc = fadd(fmul(acc[i][h], a.scale), 0.0f);
+                        e[(hb + h) * cap4 + j] = sc;
+                        mx[h] = nan_max(mx[h], sc);
+                    }
+                }
             }
         }
     }
     if (failed_at >= 0) goto fault;
     if (t == 0) prefetch_l2_bulk(V, (int64_t)len * D * sizeof(float));
     {
-        // per-head maxima: warps 0..7 hold heads 0..3, warps 8..15 heads 4..7
+        // per-head maxima: head quad hq is scored by warps hq * SROWS / 32 ... (hq + 1) * SROWS / 32 - 1
+        if (scorer) {
 #pragma unroll
-        for (int h = 0; h < SH; ++h) {
-            const float m = warp_nan_max(mx[h]);
-            if (lane == 0) wmax[warp][h] = m;
+            for (int h = 0; h < SH; ++h) {
+                const float m = warp_nan_max(mx[h]);
+                if (lane == 0) wmax[warp][h] = m;
+            }
         }
         __syncthreads();
-        constexpr int WPH = ATB_CHUNK / 32;
+        constexpr int WPH = SROWS / 32;
         if (t < G) {
             const int w0 = (t / SH) * WPH, h = t % SH;
             float m = wmax[w0][h];
@@ -354,34 +407,53 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             s_max[t] = m;
         }
         __syncthreads();
-        // exps, four independent positions per thread in flight
-        for (int h = 0; h < G; ++h) {
-            const float mh = s_max[h];
-            float *eh = e + h * cap4;
-            for (int j = 4 * t; j < len; j += 4 * ATB_THREADS) {
-                float4 v = *reinterpret_cast<float4 *>(eh + j);
-                v.x = expf_exact(fsub(v.x, mh), tab);
-                v.y = expf_exact(fsub(v.y, mh), tab);
-                v.z = expf_exact(fsub(v.z, mh), tab);
-                v.w = expf_exact(fsub(v.w, mh), tab);
-                *reinterpret_cast<float4 *>(eh + j) = v;      // positions past len are never read
+        // The exps of chunk ci + 1 (warps 1..15, a quad of one head per item) are made while
+        // lanes 0..G-1 of warp 0 add chunk ci to the in-order sums; chunk 0 by all first.
+        auto exps_chunk = [&](int ci, int u, int n) {
+            if (ci >= nk) return;
+            const int j0 = ci * ATB_CHUNK;
+            for (int i = u; i < G * QUADS; i += n) {
+                const int h = i / QUADS, j = j0 + 4 * (i % QUADS);
+                if (j < len) {
+                    float4 *p = reinterpret_cast<float4 *>(e + h * cap4 + j);   // positions past len are never read
+                    const float mh = s_max[h];
+                    float4 v = *p;
+                    v.x = expf_exact(fsub(v.x, mh), tab);
+                    v.y = expf_exact(fsub(v.y, mh), tab);
+                    v.z = expf_exact(fsub(v.z, mh), tab);
+                    v.w = expf_exact(fsub(v.w, mh), tab);
+                    *p = v;
+                }
             }
-        }
+        };
+        exps_chunk(0, t, ATB_THREADS);
         __syncthreads();
+        float sum = 0.0f;
+        for (int ci = 0; ci < nk; ++ci) {
+            if (warp == 0) {
+                if (lane < G) {
+                    const int j0 = ci * ATB_CHUNK;
+                    sum = chain_sum(e + lane * cap4 + j0, min(ATB_CHUNK, len - j0), sum);
+                }
+            } else {
+                exps_chunk(ci + 1, t - 32, ATB_THREADS - 32);
+            }
+            __syncthreads();
+        }
         if (t < G) {
-            const float sum = chain_sum(e + t * cap4, len);      // the in-order sums
             s_sum[t] = sum;
             s_rcp[t] = __frcp_rn(sum);
         }
         __syncthreads();
     }
     {
-        // ---- probabilities @ V: thread (dimension, head pair), positions in order ----
-        // The divisions e / sum of a chunk are made by the threads without P.V work while the P.V
-        // threads consume the chunk before it (chunk 0 before the loop); the barrier that opens
-        // each chunk orders the two.
+        // ---- probabilities @ V: thread (dimension pair, PV_HEADS heads), positions in order ----
+        // A warp takes 32 dimension pairs of one head: per position one 8-byte V load per thread
+        // and the head's probability as a broadcast, the loads of the next eight positions issued
+        // before the products of the current eight. The divisions e / sum of a chunk are made by
+        // the threads without P.V work while the P.V threads consume the chunk before it (chunk 0
+        // before the loop); the barrier that opens each chunk orders the two.
         const bool pv = t < PV_THREADS;
-        static_assert(ATB_THREADS - PV_THREADS >= 32, "threads left for the divisions");
         auto divide_chunk = [&](int ci) {
             if (pv || ci >= nk) return;
             const int u = t - PV_THREADS, j0 = ci * ATB_CHUNK;
@@ -391,58 +463,74 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             }
         };
         divide_chunk(0);
-        const int dim = t % D, hp = 2 * (t / D);
-        const float *p0 = e + min(hp, G - 1) * cap4, *p1 = e + min(hp + 1, G - 1) * cap4;   // past G: discarded
-        // where row k (mod 8) of a staged V chunk keeps this thread's dimension
+        const int dim = 2 * (t % DP), hq = PV_HEADS * (t / DP);
+        const float *pr[PV_HEADS];
+#pragma unroll
+        for (int i = 0; i < PV_HEADS; ++i) pr[i] = e + min(hq + i, G - 1) * cap4;   // past G: discarded
+        // where row k (mod 8) of a staged V chunk keeps this thread's two dimensions (adjacent)
         int voff[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            if constexpr (TMA) {
-                const int col = dim % ATB_BOX;
-                voff[k] = (dim / ATB_BOX) * ATB_CHUNK * ATB_BOX + k * ATB_BOX + ((((col >> 2) ^ k) << 2) | (col & 3));
-            } else {
-                voff[k] = k * D + dim;
-            }
-        }
+        for (int k = 0; k < 8; ++k) voff[k] = staged_index<D, TMA>(k, dim);
         constexpr int VROW8 = TMA ? 8 * ATB_BOX : 8 * D;  // floats from row j to row j + 8 (same box)
-        float acc0 = 0.0f, acc1 = 0.0f;
+        float acc[PV_HEADS][2];
+#pragma unroll
+        for (int i = 0; i < PV_HEADS; ++i) acc[i][0] = acc[i][1] = 0.0f;
         for (int ci = 0; ci < nk; ++ci) {
             const int idx = nk + ci;
             const bool ok = ready(idx);
             if (__syncthreads_or(!ok)) { failed_at = idx; break; }
             issue(idx + ATB_STAGES - 1);
+            const int j0 = ci * ATB_CHUNK;
+            const float *st = ring + (idx % ATB_STAGES) * STAGE;
+            if (own_new && ci == nk - 1) own_row(ring + (idx % ATB_STAGES) * STAGE, pos - j0, vn, false);
             divide_chunk(ci + 1);
             if (pv) {
-                const float *st = ring + (idx % ATB_STAGES) * STAGE;
-                const int j0 = ci * ATB_CHUNK;
-                const int n = min(ATB_CHUNK, len - j0);
-                const int stop = (own_new && ci == nk - 1) ? n - 1 : n;   // the new row comes from vn
+                const int n = min(ATB_CHUNK, len - j0), n8 = n & ~7;
                 int jj = 0;
-                for (; jj + 8 <= stop; jj += 8) {
-                    const float4 a0 = *reinterpret_cast<const float4 *>(p0 + j0 + jj);
-                    const float4 a1 = *reinterpret_cast<const float4 *>(p0 + j0 + jj + 4);
-                    const float4 b0 = *reinterpret_cast<const float4 *>(p1 + j0 + jj);
-                    const float4 b1 = *reinterpret_cast<const float4 *>(p1 + j0 + jj + 4);
-                    const float *vr = st + (jj / 8) * VROW8;
-                    float v[8];
+                if (n8) {
+                    float4 pc[PV_HEADS][2];
+                    float2 vc[8];
+                    auto load = [&](int j, float4 (&pd)[PV_HEADS][2], float2 (&vd)[8]) {
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) v[k] = vr[voff[k]];
-                    const float pa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    const float pb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                        for (int i = 0; i < PV_HEADS; ++i) {
+                            pd[i][0] = *reinterpret_cast<const float4 *>(pr[i] + j0 + j);
+                            pd[i][1] = *reinterpret_cast<const float4 *>(pr[i] + j0 + j + 4);
+                        }
+                        const float *vr = st + (j / 8) * VROW8;
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        acc0 = fadd(acc0, fmul(pa[k], v[k]));
-                        acc1 = fadd(acc1, fmul(pb[k], v[k]));
+                        for (int k = 0; k < 8; ++k) vd[k] = *reinterpret_cast<const float2 *>(vr + voff[k]);
+                    };
+                    load(0, pc, vc);
+                    for (; jj < n8; jj += 8) {
+                        float4 pn[PV_HEADS][2];
+                        float2 vx[8];
+                        load(min(jj + 8, n8 - 8), pn, vx);      // the last step reloads a step already made
+#pragma unroll
+                        for (int i = 0; i < PV_HEADS; ++i) {
+                            const float pk[8] = {pc[i][0].x, pc[i][0].y, pc[i][0].z, pc[i][0].w,
+                                                 pc[i][1].x, pc[i][1].y, pc[i][1].z, pc[i][1].w};
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                acc[i][0] = fadd(acc[i][0], fmul(pk[k], vc[k].x));
+                                acc[i][1] = fadd(acc[i][1], fmul(pk[k], vc[k].y));
+                            }
+                        }
+#pragma unroll
+                        for (int i = 0; i < PV_HEADS; ++i) {
+                            pc[i][0] = pn[i][0];
+                            pc[i][1] = pn[i][1];
+                        }
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) vc[k] = vx[k];
                     }
                 }
-                for (; jj < stop; ++jj) {
-                    const float v = staged_elem<D, TMA>(st, jj, dim);
-                    acc0 = fadd(acc0, fmul(p0[j0 + jj], v));
-                    acc1 = fadd(acc1, fmul(p1[j0 + jj], v));
-                }
-                if (stop != n) {
-                    acc0 = fadd(acc0, fmul(p0[j0 + n - 1], vn[dim]));
-                    acc1 = fadd(acc1, fmul(p1[j0 + n - 1], vn[dim]));
+                for (; jj < n; ++jj) {
+                    const float2 v = *reinterpret_cast<const float2 *>(st + staged_index<D, TMA>(jj, dim));
+#pragma unroll
+                    for (int i = 0; i < PV_HEADS; ++i) {
+                        acc[i][0] = fadd(acc[i][0], fmul(pr[i][j0 + jj], v.x));
+                        acc[i][1] = fadd(acc[i][1], fmul(pr[i][j0 + jj], v.y));
+                    }
                 }
             }
         }
@@ -452,13 +540,17 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         const int width = a.heads * D;
         __syncthreads();
         if (pv) {
-            if (hp < G) {
-                if (a.ctx) a.ctx[(int64_t)r * width + (h0 + hp) * D + dim] = acc0;
-                q[hp * D + dim] = acc0;
-            }
-            if (hp + 1 < G) {
-                if (a.ctx) a.ctx[(int64_t)r * width + (h0 + hp + 1) * D + dim] = acc1;
-                q[(hp + 1) * D + dim] = acc1;
+#pragma unroll
+            for (int i = 0; i < PV_HEADS; ++i) {
+                const int h = hq + i;
+                if (h < G) {
+                    if (a.ctx) {
+                        a.ctx[(int64_t)r * width + (h0 + h) * D + dim] = acc[i][0];
+                        a.ctx[(int64_t)r * width + (h0 + h) * D + dim + 1] = acc[i][1];
+                    }
+                    q[h * D + dim] = acc[i][0];
+                    q[h * D + dim + 1] = acc[i][1];
+                }
             }
         }
         if (a.q_out) {
