@@ -337,10 +337,13 @@ lm_head_tc_kernel(const LmHeadTcArgs a) {
 // listed first; then every thread takes one candidate and forms the reference's in-order dot
 // product, its row streamed from memory eight 16-byte pieces ahead of the chain, the activations
 // broadcast from shared memory.
-constexpr int LMP_THREADS = 256;
+constexpr int LMP_THREADS = 512;   // 16 warps: 16 candidate rows' in-order chains at a time
 constexpr int LMP_LIST = 4096;
 
-__host__ __device__ inline size_t lm_pick_smem(int k) { return sizeof(float) * (size_t)(17 * k) + sizeof(int) * LMP_LIST; }
+// x, two staged rows per warp, the candidate list
+__host__ __device__ inline size_t lm_pick_smem(int k) {
+    return sizeof(float) * (size_t)((1 + 2 * LMP_THREADS / 32) * k) + sizeof(int) * LMP_LIST;
+}
 
 // The reference's in-order dot product of x and w (both in shared memory, 16-byte aligned,
 // n a multiple of 16), one thread: the next 16 products' operands are loaded while the current
@@ -414,8 +417,8 @@ lm_head_pick_kernel(const LmHeadTcArgs a, const float *x, const float *w, int ct
     const int m = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int K = a.k;
     float *xs = psm;                                   // [K]
-    float *rowbuf = psm + K;                           // [8 warps][2][K] staged candidate rows
-    int *list = reinterpret_cast<int *>(psm + 17 * K);
+    float *rowbuf = psm + K;                           // [warps][2][K] staged candidate rows
+    int *list = reinterpret_cast<int *>(psm + (1 + 2 * LMP_THREADS / 32) * K);
     release_dependents();
     wait_for_producer();
     const float delta = a.delta[m];
