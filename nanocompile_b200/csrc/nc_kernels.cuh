@@ -100,12 +100,22 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
     __shared__ float s_inv;
     __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
+    // a thread requests four values of a row at once (one round trip per 1024 values)
+    auto stage = [&](float *dst, const float *src) {
+        for (int i0 = threadIdx.x; i0 < n; i0 += 4 * NORM_THREADS) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = i0 + u * NORM_THREADS < n ? src[i0 + u * NORM_THREADS] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (i0 + u * NORM_THREADS < n) dst[i0 + u * NORM_THREADS] = v[u];
+        }
+    };
     release_dependents();
-    for (int i = threadIdx.x; i < n; i += NORM_THREADS) ws[i] = w[i];
+    stage(ws, w);
     wait_for_producer();
     const int64_t in_row = row_map ? row_map[b] : b;
-    const float *xr = x + in_row * n;
-    for (int i = threadIdx.x; i < n; i += NORM_THREADS) row[i] = xr[i];
+    stage(row, x + in_row * n);
     __syncthreads();
     rms_norm_smem(row, sq, ws, n, eps, &s_inv);
     if (normed)
