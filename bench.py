@@ -36,7 +36,8 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from nanocompile_b200.shard import RankGroup, rank_sequences  # noqa: E402
+from nanocompile_b200.model import QWEN2_0_5B, synthetic_cache, synthetic_prompt, synthetic_weights  # noqa: E402
+from nanocompile_b200.shard import rank_sequences  # noqa: E402
 
 METRIC = "int8 Qwen2-0.5B decode tok/s (bs1; bs64×1/2/4/8 GPU); % of HBM roofline"
 BATCH = 64            # sequences per GPU (configuration 5)
@@ -46,6 +47,59 @@ FALLBACK_HBM_GBS = 6650.0
 
 
 # -- plumbing ---------------------------------------------------------------------------------
+
+
+class RankGroup:
+    """Rank and world from the torchrun environment, and the host-side collectives the timing
+    needs: a barrier, the max over ranks, a gather of small records. torch.distributed (NCCL on
+    GPUs, gloo on the host) is used here only, never on the data path."""
+
+    def __init__(self, backend: str | None = None, timeout_s: float = 120.0):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dist = None
+        self.device = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
+            kwargs = {}
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                self.device = torch.device("cuda", self.local)
+                kwargs["device_id"] = self.device
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
+            self.dist = dist
+            self.torch = torch
+
+    def barrier(self) -> None:
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max(self, value: float) -> float:
+        """The largest ``value`` over the ranks (every rank gets it)."""
+        if self.dist is None:
+            return value
+        t = self.torch.tensor([value], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj) -> list:
+        """Every rank's ``obj``, in rank order (every rank gets the list)."""
+        if self.dist is None:
+            return [obj]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def close(self) -> None:
+        if self.dist is not None:
+            self.dist.destroy_process_group()
+            self.dist = None
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -125,23 +179,29 @@ class ClockSampler:
 # -- the model ------------------------------------------------------------------------------
 
 
-def build_model(dev: int, slots: int, capacity: int):
+def build_model(dev: int, slots: int, capacity: int, max_rows: int | None = None):
+    """The 0.5B model on GPU ``dev``: float32 weights uploaded and quantized on the device. The
+    host copy of the int8 weights (the CPU baseline's) comes from the host quantizer."""
     from nanocompile_b200 import quantize as q
     from nanocompile_b200 import runtime
-    from nanocompile_b200.qwen2 import QWEN2_0_5B, build_qwen2, quantize, synthetic_weights
 
     cfg = QWEN2_0_5B
     weights = synthetic_weights(cfg, seed=0)
-    graph = quantize(build_qwen2(cfg, last_only=True), "int8", keep=("lm_head.weight",))
-    wq = q.quantized_weights(graph, weights)
-    model = runtime.DeviceModel(cfg, wq, "int8", max_rows=BATCH, slots=slots, capacity=capacity, device=dev)
-    return cfg, wq, model
+    model = runtime.DeviceModel(cfg, weights, "int8", max_rows=max_rows or BATCH, slots=slots, capacity=capacity,
+                                device=dev)
+    return cfg, weights, model
+
+
+def host_int8_weights(weights):
+    from nanocompile_b200 import quantize as q
+
+    return q.int8_projection_weights(weights, QWEN2_0_5B)
 
 
 def layer_bytes(cfg, rows: int, past: int) -> float:
     """One decoder layer's int8 weights, scales, bias and gains, and its KV rows read for `rows` rows."""
-    H, I, d = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
-    heads, kv = cfg.num_attention_heads, cfg.num_key_value_heads
+    H, I, d = cfg.hidden, cfg.inter, cfg.head_dim
+    heads, kv = cfg.heads, cfg.kv_heads
     nqkv, hq = (heads + 2 * kv) * d, heads * d
     weights = nqkv * H + H * hq + 2 * I * H + H * I
     scales = 4 * (nqkv + H + 2 * I + H) + 4 * nqkv + 2 * 4 * H
@@ -150,15 +210,15 @@ def layer_bytes(cfg, rows: int, past: int) -> float:
 
 def algorithmic_bytes(kind: str, cfg, rows: int, past: int) -> float:
     """Bytes a launch of `kind` must move at least (weights / cache / activations, once each)."""
-    H, I, d, V = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim, cfg.vocab_size
-    heads, kv = cfg.num_attention_heads, cfg.num_key_value_heads
+    H, I, d, V = cfg.hidden, cfg.inter, cfg.head_dim, cfg.vocab
+    heads, kv = cfg.heads, cfg.kv_heads
     nqkv = (heads + 2 * kv) * d
     if kind == "lm_head_argmax":
         if rows <= 16:        # int8 prefilter: the int8 copy, its row scales, approximations out and back
             return V * H + V * 4 + rows * (H * 4 + 2 * V * 4)
         return V * H * 4 + rows * H * 4 + rows * V * 4
     if kind == "persistent_layers":
-        return cfg.num_hidden_layers * layer_bytes(cfg, rows, past)
+        return cfg.layers * layer_bytes(cfg, rows, past)
     if kind == "attention":
         return rows * (2 * kv * (past + 1) * d * 4 + nqkv * 4 + heads * d * 1.25)
     if kind == "down_projection":
@@ -195,8 +255,6 @@ def roofline(profile: dict, cfg, rows: int, past: int, workload: str) -> dict:
 def cpu_sample(cfg, wq, steps: int, threads: int, warmup: int = 1) -> dict:
     """Greedy decode of one sequence of the batched workload on the host cores (``warmup``
     untimed steps first)."""
-    from nanocompile_b200.qwen2 import synthetic_cache
-
     ref = ROOT / "oracle" / "_ref"
     keys, values, first = synthetic_cache(cfg, 0, PAST)
     if (ref / "plan.json").exists():
@@ -225,8 +283,7 @@ def cpu_sample(cfg, wq, steps: int, threads: int, warmup: int = 1) -> dict:
 def run_ours(args, dist: RankGroup) -> dict | None:
     dev = dist.local
     capacity = max(PAST, BS1_END) + args.warmup + args.steps + 16
-    cfg, wq, model = build_model(dev, BATCH, capacity)
-    from nanocompile_b200.qwen2 import synthetic_cache
+    cfg, weights, model = build_model(dev, BATCH, capacity)
 
     first, slots, starts = [], list(range(BATCH)), [PAST] * BATCH
     for b, sequence in enumerate(rank_sequences(dist.rank, dist.world, BATCH)):
@@ -261,7 +318,7 @@ def run_ours(args, dist: RankGroup) -> dict | None:
         bs1 = run_bs1(cfg, model)
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-        cpu = cpu_sample(cfg, wq, args.cpu_steps, os.cpu_count() or 1)
+        cpu = cpu_sample(cfg, host_int8_weights(weights), args.cpu_steps, os.cpu_count() or 1)
     model.close()
     if dist.rank != 0:
         return None
@@ -281,9 +338,7 @@ def run_ours(args, dist: RankGroup) -> dict | None:
 
 def run_bs1(cfg, model) -> dict:
     """Configuration 3 on slot 0: 32-token prompt, then greedy decode up to 1024 positions."""
-    from nanocompile_b200.qwen2 import synthetic_prompt
-
-    prompt = synthetic_prompt(cfg.vocab_size, BS1_PROMPT)
+    prompt = synthetic_prompt(cfg.vocab, BS1_PROMPT)
     _, tok = model.step(prompt, [0] * BS1_PROMPT, list(range(BS1_PROMPT)), [BS1_PROMPT - 1], want_logits=False)
     first = int(tok[0])
     steps = BS1_END - BS1_PROMPT
@@ -295,9 +350,9 @@ def run_bs1(cfg, model) -> dict:
     # the workload's mean position, the LM head as read) over the measured time per token
     peak, source = measured_peaks()
     mean_past = (BS1_PROMPT + BS1_END - 1) // 2
-    layers = cfg.num_hidden_layers * layer_bytes(cfg, 1, mean_past)
+    layers = cfg.layers * layer_bytes(cfg, 1, mean_past)
     head_read = algorithmic_bytes("lm_head_argmax", cfg, 1, mean_past)
-    head_fp32 = cfg.vocab_size * cfg.hidden_size * 4
+    head_fp32 = cfg.vocab * cfg.hidden * 4
     s_per_token = ms / steps / 1000.0
     step = {"bytes_per_token": layers + head_read, "achieved": round((layers + head_read) / s_per_token / 1e9, 1),
             "peak": peak, "unit": "GB/s", "frac": round((layers + head_read) / s_per_token / 1e9 / peak, 4),
@@ -318,12 +373,8 @@ def run_reference(args) -> dict | None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if int(os.environ.get("RANK", "0")) != 0:
         return None
-    from nanocompile_b200 import quantize as q
-    from nanocompile_b200.qwen2 import QWEN2_0_5B, build_qwen2, quantize, synthetic_weights
-
     cfg = QWEN2_0_5B
-    graph = quantize(build_qwen2(cfg, last_only=True), "int8", keep=("lm_head.weight",))
-    wq = q.quantized_weights(graph, synthetic_weights(cfg, seed=0))
+    wq = host_int8_weights(synthetic_weights(cfg, seed=0))
     threads = os.cpu_count() or 1
     base = cpu_sample(cfg, wq, max(args.steps, 1), threads, warmup=args.warmup)
     return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": world,

@@ -109,7 +109,10 @@ int64_t nc_lm_head_scratch_bytes(int64_t rows, int64_t vocab);
  *  - Limit: rows * ceil(vocab / 128) <= 32768 (e.g. 27 rows of a 151,936-token vocabulary);
  *    larger calls fail with NC_ERR_ARGUMENT and a message.
  *  - The first call on each device looks the array's address up (cudaGetSymbolAddress, with
- *    that device current); make that first call before any stream capture.
+ *    that device current); make that first call before any stream capture.  The address is
+ *    kept for the life of the process: it does not survive a cudaDeviceReset of that device
+ *    (the library's module is reloaded at a new address), so do not call this entry point on
+ *    a device after resetting it.
  *  - Every call shares the array: calls that overlap on the GPU (other streams, other host
  *    threads) race.  Each call clears the finish counter on its stream before the kernel. */
 int32_t nc_lm_head_argmax_noalloc(void **p, const int64_t *s, void *stream);
@@ -157,6 +160,14 @@ int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t b
  * p: [0] out f32[n]  [1] x f32[n];  s: n */
 int32_t nc_expf_exact(void **p, const int64_t *s, void *stream);
 
+/* quantize_int8 (nanocompile/quantize.py:55-70) on the device: per-row symmetric int8 weights,
+ * scale = max|row| / 127 (0 -> 1), values sign(v) * floor(|v| + 0.5) of v = w / scale clipped to
+ * +-127 -- the same bytes and scales as the host scheme.
+ * p: [0] values i8[rows, cols] (packed: u8 value + 128, the layout the projections read)
+ *    [1] scales f32[rows]  [2] weights f32[rows, cols]
+ * s: rows, cols, packed (0 / 1) */
+int32_t nc_quantize_int8_rows(void **p, const int64_t *s, void *stream);
+
 /* The block scale mag / 127 is computed by a branch-free correctly rounded division; this runs
  * it against the IEEE divide on every non-negative float and reports the differences (0). */
 int32_t nc_selfcheck_div127(int64_t *mismatches);
@@ -187,6 +198,9 @@ int64_t nc_qwen2_arena_bytes(const nc_model *model);
  * nanocompile/quantize.py:47-52).  Returns NC_ERR_ARGUMENT for an unknown name or size. */
 int32_t nc_qwen2_upload(nc_model *model, const char *name, const void *host, int64_t bytes);
 int32_t nc_qwen2_missing_weights(const nc_model *model, int32_t *count);
+/* A float32 projection "<name>" of an int8 model, quantized on the device (nc_quantize_int8_rows)
+ * into its "<name>@int8" / "<name>@scales" weights: the host need not run quantize_int8. */
+int32_t nc_qwen2_upload_quantize(nc_model *model, const char *name, const float *host, int64_t bytes);
 
 /* KV cache of one slot: positions [start, start+count) of every layer, host arrays
  * [layers, kv_heads, count, head_dim]. */
@@ -226,8 +240,13 @@ int32_t nc_qwen2_decode_timed(nc_model *model, int32_t batch, const int32_t *slo
  * every launch, and sums the milliseconds and launches per fused-group kind into the
  * [NC_KINDS] arrays (kinds: 0 gather, 1 q/k/v projection, 2 attention, 3 o projection,
  * 4 gate/up projection, 5 down projection, 6 rms_norm row kernel, 7 block quantization,
- * 8 LM head + argmax). */
-#define NC_KINDS 9
+ * 8 LM head + argmax, 9 the persistent decode kernel's layers). */
+#define NC_KINDS 10
+/* Kernel-time probe around nc_qwen2_step calls: on != 0 starts bracketing every launch of the
+ * following steps with CUDA events; on == 0 stops, synchronizes and sums milliseconds and
+ * launches per fused-group kind (as nc_qwen2_profile) into the arrays (nullable). */
+int32_t nc_qwen2_probe(nc_model *model, int32_t on, float *ms_per_kind, int32_t *launches_per_kind);
+
 int32_t nc_qwen2_profile(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
                          const int32_t *start, int32_t steps, float *ms_per_kind, int32_t *launches_per_kind);
 

@@ -14,6 +14,7 @@
 #include "nc_decode_mk.cuh"
 #include "nc_gemm_i8.cuh"
 
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -743,6 +744,16 @@ extern "C" int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host
     return NC_OK;
 }
 
+extern "C" int32_t nc_quantize_int8_rows(void **p, const int64_t *s, void *stream) {
+    const int64_t rows = s[0], cols = s[1], packed = s[2];
+    if (rows < 0 || cols <= 0 || rows > INT32_MAX) return fail(NC_ERR_ARGUMENT, "bad sizes %lld x %lld", (long long)rows,
+                                                              (long long)cols);
+    if (rows == 0) return NC_OK;
+    quantize_int8_rows_kernel<<<(unsigned)rows, QI8_THREADS, 0, (cudaStream_t)stream>>>(
+        p[0], (float *)p[1], (const float *)p[2], cols, packed ? 1 : 0);
+    return check_launch("quantize_int8_rows_kernel");
+}
+
 extern "C" int32_t nc_selfcheck_div127(int64_t *mismatches) {
     unsigned long long *d = nullptr;
     CUDA_TRY(cudaMalloc(&d, sizeof *d));
@@ -1146,6 +1157,8 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
         return fail(NC_ERR_ARGUMENT, "unsupported model shape");
     if (c.hidden % 32 || c.inter % 32 || (c.heads * c.head_dim) % 32)
         return fail(NC_ERR_ARGUMENT, "widths must be whole 32-blocks");
+    if (c.quant < 0 || c.quant > 1)
+        return fail(NC_ERR_ARGUMENT, "projection mode %d: the library implements 0 (float32) and 1 (int8-vnni)", c.quant);
     if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024 &&
         attention_smem(1, (int)c.head_dim, c.capacity) > 220 * 1024)
         return fail(NC_ERR_ARGUMENT, "capacity %d exceeds the attention kernel's shared memory", c.capacity);
@@ -1502,6 +1515,7 @@ static int32_t decode_graph(nc_model *m, int batch, bool tokens_only, cudaGraphE
         return NC_OK;
     }
     cudaGraph_t graph;
+    if (m->probing) return fail(NC_ERR_STATE, "a decode graph cannot be captured while the kernel-time probe is on");
     CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     m->logit_identity = true;                 // decode_setup makes the logit rows 0..batch-1
     int32_t s = enqueue_step(m, batch, batch, true, tokens_only);
@@ -1635,6 +1649,61 @@ extern "C" int32_t nc_qwen2_decode_timed(nc_model *m, int32_t batch, const int32
     return model_faults(m);
 }
 
+extern "C" int32_t nc_qwen2_probe(nc_model *m, int32_t on, float *ms_per_kind, int32_t *launches_per_kind) {
+    if (!m) return fail(NC_ERR_ARGUMENT, "null model");
+    if (on) {
+        m->probing = true;
+        m->event_next = 0;
+        m->probe_marks.clear();
+        return NC_OK;
+    }
+    m->probing = false;
+    for (int k = 0; k < K_KINDS; ++k) {
+        if (ms_per_kind) ms_per_kind[k] = 0.0f;
+        if (launches_per_kind) launches_per_kind[k] = 0;
+    }
+    CUDA_TRY(cudaSetDevice(m->dev));
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    for (auto &pm : m->probe_marks) {
+        float ms = 0.0f;
+        CUDA_TRY(cudaEventElapsedTime(&ms, pm.second.first, pm.second.second));
+        if (ms_per_kind) ms_per_kind[pm.first] += ms;
+        if (launches_per_kind) launches_per_kind[pm.first] += 1;
+    }
+    m->probe_marks.clear();
+    return NC_OK;
+}
+
+// A float32 projection quantized on the device into its "<name>@int8" / "<name>@scales" slots
+// (nanocompile/quantize.py:55-70, the same bytes as the host scheme), staged through a
+// temporary device buffer.
+extern "C" int32_t nc_qwen2_upload_quantize(nc_model *m, const char *name, const float *host, int64_t bytes) {
+    if (!m || !name || !host) return fail(NC_ERR_ARGUMENT, "null argument");
+    const std::string base(name);
+    auto qi = m->weights.find(base + "@int8"), si = m->weights.find(base + "@scales");
+    if (qi == m->weights.end() || si == m->weights.end())
+        return fail(NC_ERR_ARGUMENT, "no int8 projection named %s", name);
+    const int64_t rows = si->second.bytes / 4, cols = rows ? qi->second.bytes / rows : 0;
+    if (bytes != rows * cols * 4)
+        return fail(NC_ERR_ARGUMENT, "weight %s has %lld bytes, expected %lld float32", name, (long long)bytes,
+                    (long long)(rows * cols * 4));
+    CUDA_TRY(cudaSetDevice(m->dev));
+    float *staged = nullptr;
+    CUDA_TRY(cudaMalloc(&staged, (size_t)bytes));
+    cudaError_t e = cudaMemcpyAsync(staged, host, (size_t)bytes, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) {
+        quantize_int8_rows_kernel<<<(unsigned)rows, QI8_THREADS, 0, m->stream>>>(
+            qi->second.dst, (float *)si->second.dst, staged, cols, 1);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    cudaFree(staged);
+    if (e != cudaSuccess) return fail(NC_ERR_CUDA, "quantizing %s: %s", name, cudaGetErrorString(e));
+    m->uploaded.insert(base + "@int8");
+    m->uploaded.insert(base + "@scales");
+    return NC_OK;
+}
+
 // ---- the LM head + argmax without any allocation ---------------------------------------------
 // Some callers cannot call cudaMalloc: a host that gives this library a fixed device-memory
 // budget and forbids allocations it did not make, code that runs while another thread captures
@@ -1674,6 +1743,13 @@ int32_t noalloc_scratch(void **out) {
 extern "C" int32_t nc_lm_head_argmax_noalloc(void **p, const int64_t *s, void *stream) {
     const int64_t rows = s[0], vocab = s[1], hidden = s[2];
     if (rows <= 0 || vocab <= 0) return NC_OK;
+    // refuse sizes whose product could overflow before forming it (rows alone above the limit
+    // can never fit; vocab and hidden must also fit the kernel's 32-bit sizes)
+    if (rows > NOALLOC_PARTIALS || vocab > INT32_MAX || hidden <= 0 || hidden > INT32_MAX)
+        return fail(NC_ERR_ARGUMENT,
+                    "nc_lm_head_argmax_noalloc: rows %lld, vocab %lld, hidden %lld are outside what the static "
+                    "scratch holds (rows * ceil(vocab / 128) <= %lld, vocab and hidden < 2^31)",
+                    (long long)rows, (long long)vocab, (long long)hidden, (long long)NOALLOC_PARTIALS);
     const int64_t partials = rows * ((vocab + F32_ROWS - 1) / F32_ROWS);
     if (partials > NOALLOC_PARTIALS)
         return fail(NC_ERR_ARGUMENT,

@@ -1025,6 +1025,42 @@ __global__ void xor80_kernel(uint8_t *p, int64_t n) {
         p[i] ^= 0x80;
 }
 
+// Per-row int8 weights on the device (nanocompile/quantize.py:55-70), one CTA per row:
+// scale = max|w| / 127 (a NaN-propagating maximum: |w| bit patterns order as unsigned
+// integers, NaN above inf; a zero scale becomes 1), then for each value v = w / scale the
+// rounding sign(v) * floor(|v| + 0.5) and the clip to +-127 -- every step the single float32
+// rounding NumPy takes.  packed != 0 stores value + 128 as a byte, the layout the projection
+// kernels read; otherwise the int8 value.  A NaN or infinite weight gives a NaN or infinite
+// scale and zero values where the quotient is NaN (NumPy's cast of NaN to int8 is
+// platform-defined; on x86-64 it is 0 as well).
+constexpr int QI8_THREADS = 256;
+__global__ void __launch_bounds__(QI8_THREADS) quantize_int8_rows_kernel(void *out, float *scales, const float *w,
+                                                                         int64_t cols, int packed) {
+    __shared__ unsigned s_max[QI8_THREADS / 32];
+    const int64_t row = blockIdx.x;
+    const float *src = w + row * cols;
+    unsigned mx = 0;
+    for (int64_t i = threadIdx.x; i < cols; i += QI8_THREADS) mx = max(mx, __float_as_uint(src[i]) & 0x7fffffffu);
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    unsigned top = 0;
+#pragma unroll
+    for (int i = 0; i < QI8_THREADS / 32; ++i) top = max(top, s_max[i]);
+    float scale = __fdiv_rn(__uint_as_float(top), 127.0f);
+    if (scale == 0.0f) scale = 1.0f;
+    if (threadIdx.x == 0) scales[row] = scale;
+    for (int64_t i = threadIdx.x; i < cols; i += QI8_THREADS) {
+        const float v = __fdiv_rn(src[i], scale);
+        const float mag = floorf(__fadd_rn(fabsf(v), 0.5f));
+        float r = v > 0.0f ? mag : (v < 0.0f ? -mag : 0.0f);
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        const int q = (int)r;
+        if (packed) static_cast<uint8_t *>(out)[row * cols + i] = (uint8_t)(q + 128);
+        else static_cast<int8_t *>(out)[row * cols + i] = (int8_t)q;
+    }
+}
+
 // Every non-negative float through div127 and through the IEEE divide; counts differences.
 __global__ void selfcheck_div127_kernel(unsigned long long *mismatches) {
     unsigned long long bad = 0;

@@ -1,42 +1,43 @@
 """Per-row int8 weights and the activation scheme of nanocompile's ``int8-vnni`` mode.
 
-Host side, once per model: the projection weights are quantized here in NumPy,
-exactly as nanocompile's ``quantize.quantize_int8`` does it
-(``nanocompile/quantize.py:55-70``): one float32 scale per output row,
-``max(|row|) / 127`` with an all-zero row getting scale 1, and the row divided
-by it and rounded half away from zero as ``sign(x) * floor(|x| + 0.5)`` in
-float32. The device never sees float32 projection weights in this mode.
+One float32 scale per output row, ``max(|row|) / 127`` with an all-zero row getting scale 1,
+and the row divided by it and rounded half away from zero as ``sign(x) * floor(|x| + 0.5)``
+in float32, clipped to +-127 (``nanocompile/quantize.py:55-70``). The projections are quantized
+once per model: on the host here (:func:`quantize_int8`), or on the device from the float32
+weights by ``nc_quantize_int8_rows`` with the same bytes. The device never reads float32
+projection weights in this mode.
 
-The activations are quantized on the device, per 32-value block, by the fused
-kernels (``nanocompile/quantize.py:102-124``); ``BLOCK`` is that block.
+The activations are quantized on the device, per 32-value block, by the fused kernels
+(``nanocompile/quantize.py:102-124``); ``BLOCK`` is that block.
 """
 
 from __future__ import annotations
 
-from collections.abc import Iterable, Mapping
+from collections.abc import Mapping
 
 import numpy as np
 
+from nanocompile_b200.model import ModelShape, projection_shapes
+
 INT8_MAX = 127
 BLOCK = 32                     # nanocompile/quantize.py:43 DEFAULT_BLOCK
-ACTIVATIONS = ("f32", "int8")  # nanocompile/quantize.py:42
 
 
 def int8_name(name: str) -> str:
-    """``nanocompile/quantize.py:47``: the int8 values of weight ``name``."""
+    """The int8 values of projection ``name`` (``nanocompile/quantize.py:47``)."""
     return f"{name}@int8"
 
 
 def scales_name(name: str) -> str:
-    """``nanocompile/quantize.py:51``: the per-row float32 scales of weight ``name``."""
+    """The per-row float32 scales of projection ``name`` (``nanocompile/quantize.py:51``)."""
     return f"{name}@scales"
 
 
 def quantize_int8(weights: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """``[out, in]`` float32 to per-row int8 values and float32 scales.
 
-    The same NumPy operations in the same order as ``nanocompile/quantize.py:55-70``,
-    so the bytes and scales are identical.
+    The NumPy operations of ``nanocompile/quantize.py:55-70`` in the same order -- the scheme's
+    bytes are only the reference's if every rounding is the same one.
     """
     if weights.ndim != 2:
         raise ValueError(f"expected a 2-D weight matrix, got shape {weights.shape}")
@@ -49,40 +50,21 @@ def quantize_int8(weights: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return values, scales.astype(np.float32)
 
 
-def quantized_weights(graph, weights: Mapping[str, np.ndarray]) -> dict[str, np.ndarray]:
-    """The arrays ``graph`` reads, quantizing the int8 ones it names from ``weights``.
+def int8_projection_weights(weights: Mapping[str, np.ndarray], shape: ModelShape) -> dict[str, np.ndarray]:
+    """``weights`` with every layer's seven projections replaced by their ``@int8`` / ``@scales`` pair.
 
-    ``nanocompile/quantize.py:167-180``: a name already in ``weights`` is passed
-    through; ``W@int8`` / ``W@scales`` are made from ``weights[W]``; anything
-    else is a ``KeyError``.
+    Arrays already given in quantized form are kept as they are; the tied embedding (also the LM
+    head and a gather table) and the norms and biases stay float32.
     """
     out: dict[str, np.ndarray] = {}
-    for name in graph.weights:
-        if name in weights:
-            out[name] = weights[name]
+    projections = {name for layer in range(shape.layers) for name in projection_shapes(shape, layer)}
+    for name, array in weights.items():
+        if name not in projections:
+            out[name] = array
+    for name in sorted(projections):
+        if int8_name(name) in weights and scales_name(name) in weights:
             continue
-        if name.endswith("@int8") or name.endswith("@scales"):
-            source = name.rsplit("@", 1)[0]
-            if int8_name(source) not in out:
-                out[int8_name(source)], out[scales_name(source)] = quantize_int8(weights[source])
-            continue
-        raise KeyError(f"no weight {name!r}")
+        if name not in weights:
+            raise KeyError(f"no weight {name!r} to quantize")
+        out[int8_name(name)], out[scales_name(name)] = quantize_int8(np.asarray(weights[name]))
     return out
-
-
-def projection_names(layers: int, keep: Iterable[str] = ()) -> list[str]:
-    """The weights a Qwen2 step reads only as ``x @ W.T`` (``nanocompile/quantize.py:86-99``).
-
-    The tied embedding is also the LM head, and a gather table, so it is never
-    among them; ``keep`` removes more.
-    """
-    kept = set(keep)
-    names = []
-    for i in range(layers):
-        p = f"model.layers.{i}"
-        for n in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
-                  "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
-            name = f"{p}.{n}.weight"
-            if name not in kept:
-                names.append(name)
-    return names

@@ -15,9 +15,14 @@ the GPU box with the snapshot):
   lies;
 * ``plan.json`` / ``consts.npz`` -- the compiled program's buffers, calls and constants, so
   ``oracle/ref_runner.py`` can replay the call loop of ``CompiledGraph.__call__`` without the
-  reference's Python.
+  reference's Python;
+* ``py/nanocompile/`` -- the reference's Python package as it is, so the tests that drive the CUDA
+  backend through the reference's own ``Qwen2`` and ``CBackend``-style ``Runner`` API can import it
+  on a machine without the checkout (the GPU box).
 
-Nothing from the reference's source tree is copied into the repository.
+Nothing from the reference's source tree is committed: ``oracle/_ref/`` is git-ignored. The
+checkout is found through ``NANOCOMPILE_REFERENCE`` or, without it, the ``reference_path`` that
+``BASELINE.json`` records.
 """
 
 from __future__ import annotations
@@ -35,6 +40,36 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
+PACKAGE = OUT / "py"
+
+
+def reference_checkout() -> Path | None:
+    """The nanocompile checkout: ``NANOCOMPILE_REFERENCE``, else BASELINE.json's ``reference_path``."""
+    configured = os.environ.get("NANOCOMPILE_REFERENCE")
+    if not configured:
+        baseline = HERE.parent / "BASELINE.json"
+        try:
+            configured = json.loads(baseline.read_text()).get("reference_path")
+        except (OSError, ValueError):
+            configured = None
+    if not configured:
+        return None
+    path = Path(configured)
+    return path if (path / "nanocompile" / "__init__.py").exists() else None
+
+
+def copy_package(reference: Path, out: Path = PACKAGE) -> Path:
+    """The reference's ``nanocompile`` package (its .py files and pool.c) under ``out``."""
+    source = Path(reference) / "nanocompile"
+    target = out / "nanocompile"
+    if target.exists():
+        shutil.rmtree(target)
+    for path in source.rglob("*"):
+        if path.suffix in (".py", ".c") and "__pycache__" not in path.parts:
+            dest = target / path.relative_to(source)
+            dest.parent.mkdir(parents=True, exist_ok=True)
+            shutil.copyfile(path, dest)
+    return target
 
 
 def _poly(d) -> list:
@@ -44,7 +79,7 @@ def _poly(d) -> list:
     return [[list(m), int(c)] for m, c in d._terms.items()]
 
 
-def build(reference: Path = Path("/root/reference"), out: Path = OUT) -> Path:
+def build(reference: Path, out: Path = OUT) -> Path:
     reference = Path(reference)
     if not (reference / "nanocompile").exists():
         raise FileNotFoundError(f"no nanocompile checkout at {reference}")
@@ -87,6 +122,7 @@ def build(reference: Path = Path("/root/reference"), out: Path = OUT) -> Path:
     subprocess.run(["gcc", *codegen_c.CFLAGS, "-pthread", "-fPIC", "-shared", "-o", str(out / "libnc_pool.so"),
                     str(reference / "nanocompile" / "pool.c")], check=True)
     (out / "cpu.txt").write_text(_cpu_identity())
+    copy_package(reference, out / "py")
     return out
 
 
@@ -102,9 +138,13 @@ def _cpu_identity() -> str:
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default=os.environ.get("NANOCOMPILE_REFERENCE", "/root/reference"))
+    parser.add_argument("--reference", default=None, help="the nanocompile checkout (default: "
+                        "NANOCOMPILE_REFERENCE, else BASELINE.json's reference_path)")
     args = parser.parse_args()
-    print(build(Path(args.reference)))
+    reference = Path(args.reference) if args.reference else reference_checkout()
+    if reference is None:
+        parser.error("no nanocompile checkout: pass --reference or set NANOCOMPILE_REFERENCE")
+    print(build(reference))
     return 0
 
 

@@ -191,19 +191,16 @@ class OracleModel:
     (``activations="int8"``) or float32 (``activations=None``).
     """
 
-    def __init__(self, config, weights: Mapping[str, np.ndarray], activations: str | None, threads: int = 0,
+    def __init__(self, shape, weights: Mapping[str, np.ndarray], activations: str | None, threads: int = 0,
                  inv_freq: np.ndarray | None = None):
-        from nanocompile_b200.qwen2 import attention_scale, inverse_frequencies
-
         if activations not in (None, "int8"):
             raise ValueError("the oracle implements float32 and int8-vnni projections")
-        c = config
-        self.config = c
+        c = shape
+        self.shape = c
         self.quant = activations == "int8"
         self._keep: list[np.ndarray] = []
-        self.cfg = OrcConfig(c.vocab_size, c.hidden_size, c.intermediate_size, c.num_hidden_layers,
-                             c.num_attention_heads, c.num_key_value_heads, c.head_dim, np.float32(c.rms_norm_eps),
-                             attention_scale(c.head_dim), 1 if self.quant else 0, threads)
+        self.cfg = OrcConfig(c.vocab, c.hidden, c.inter, c.layers, c.heads, c.kv_heads, c.head_dim,
+                             np.float32(c.eps), c.attention_scale, 1 if self.quant else 0, threads)
 
         def arr(name: str, dtype=np.float32) -> np.ndarray:
             a = np.ascontiguousarray(weights[name], dtype)
@@ -212,14 +209,11 @@ class OracleModel:
 
         self.embed = arr("model.embed_tokens.weight")
         self.final_norm = arr("model.norm.weight")
-        if not c.tie_word_embeddings:
-            raise ValueError("the oracle implements tied embeddings (the configs under test)")
-        self.inv_freq = np.ascontiguousarray(
-            inverse_frequencies(c.head_dim, c.rope_theta) if inv_freq is None else inv_freq, np.float32)
-        layers = (OrcLayer * c.num_hidden_layers)()
+        self.inv_freq = np.ascontiguousarray(c.rope_rates() if inv_freq is None else inv_freq, np.float32)
+        layers = (OrcLayer * c.layers)()
         short = {"q_proj": "q", "k_proj": "k", "v_proj": "v", "o_proj": "o", "gate_proj": "g", "up_proj": "u",
                  "down_proj": "d"}
-        for i in range(c.num_hidden_layers):
+        for i in range(c.layers):
             p = f"model.layers.{i}"
             L = layers[i]
             L.in_norm = _ptr(arr(f"{p}.input_layernorm.weight"))
@@ -237,15 +231,15 @@ class OracleModel:
 
     def step(self, ids: Sequence[int], past_keys: np.ndarray, past_values: np.ndarray, last_only: bool = True):
         """``(logits, keys, values)`` for ``ids`` after the cached ``past_*`` ``[L, kv, cap, d]``."""
-        c = self.config
+        c = self.shape
         ids = np.ascontiguousarray(np.asarray(ids, np.int64))
         seq = ids.size
         past = past_keys.shape[2] if past_keys is not None else 0
         pk = np.ascontiguousarray(past_keys, np.float32)
         pv = np.ascontiguousarray(past_values, np.float32)
         rows = 1 if last_only else seq
-        logits = np.empty((rows, c.vocab_size), np.float32)
-        shape = (c.num_hidden_layers, c.num_key_value_heads, seq, c.head_dim)
+        logits = np.empty((rows, c.vocab), np.float32)
+        shape = (c.layers, c.kv_heads, seq, c.head_dim)
         keys = np.empty(shape, np.float32)
         values = np.empty(shape, np.float32)
         bad = ctypes.c_int64(0)
@@ -254,14 +248,14 @@ class OracleModel:
                                       1 if last_only else 0, _ptr(logits), _ptr(keys), _ptr(values),
                                       ctypes.byref(bad))
         if status != 0:
-            raise IndexError(f"gather index {bad.value} is outside 0..{c.vocab_size - 1}")
+            raise IndexError(f"gather index {bad.value} is outside 0..{c.vocab - 1}")
         return logits, keys, values
 
     def greedy(self, prompt: Sequence[int], steps: int, past_keys=None, past_values=None,
                return_logits: bool = False):
         """Greedy decode: the reference's driver loop with a growing host cache."""
-        c = self.config
-        shape = (c.num_hidden_layers, c.num_key_value_heads, 0, c.head_dim)
+        c = self.shape
+        shape = (c.layers, c.kv_heads, 0, c.head_dim)
         pk = np.zeros(shape, np.float32) if past_keys is None else past_keys
         pv = np.zeros(shape, np.float32) if past_values is None else past_values
         pending = list(prompt)

@@ -35,7 +35,7 @@ def golden(name: str) -> dict[str, np.ndarray]:
 
 @pytest.fixture(scope="session")
 def qwen05b_weights():
-    from nanocompile_b200.qwen2 import QWEN2_0_5B, synthetic_weights
+    from nanocompile_b200.model import QWEN2_0_5B, synthetic_weights
 
     return synthetic_weights(QWEN2_0_5B, seed=0)
 
@@ -43,10 +43,19 @@ def qwen05b_weights():
 @pytest.fixture(scope="session")
 def qwen05b_vnni_weights(qwen05b_weights):
     from nanocompile_b200 import quantize as q
-    from nanocompile_b200.qwen2 import QWEN2_0_5B, build_qwen2, quantize
+    from nanocompile_b200.model import QWEN2_0_5B
 
-    graph = quantize(build_qwen2(QWEN2_0_5B, last_only=True), "int8", keep=("lm_head.weight",))
-    return q.quantized_weights(graph, qwen05b_weights)
+    return q.int8_projection_weights(qwen05b_weights, QWEN2_0_5B)
+
+
+@pytest.fixture(scope="session")
+def reference():
+    """The reference's own nanocompile package (the copy oracle/build_ref.py ships in oracle/_ref/py)."""
+    from oracle import reference as ref
+
+    if not ref.available():
+        pytest.skip("the reference's package was not copied to oracle/_ref/py (run oracle/build_ref.py)")
+    return ref.import_reference()
 
 
 @pytest.fixture(scope="session")

@@ -4,7 +4,7 @@
 
 Every fixture here is an output of nanocompile's own ``CBackend`` (its generated C,
 compiled by gcc) -- never of this repository's code -- on seeded synthetic inputs:
-weights from ``nanocompile_b200.qwen2.synthetic_weights`` (``N(0, 0.02)`` in
+weights from ``nanocompile_b200.model.synthetic_weights`` (``N(0, 0.02)`` in
 checkpoint order, norm gains 1), prompts from ``np.random.default_rng``. The GPU
 parity tests and the CPU oracle are both held to these files; nothing at test
 time reads the reference.
@@ -28,7 +28,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
 
-from nanocompile_b200.qwen2 import (QWEN2_0_5B, TINY, Qwen2Config, synthetic_cache,  # noqa: E402
+from nanocompile_b200.model import (QWEN2_0_5B, TINY, ModelShape, synthetic_cache,  # noqa: E402
                                     synthetic_prompt, synthetic_weights)
 
 SAMPLE_STRIDE = 1009
@@ -40,9 +40,9 @@ def sha1(a: np.ndarray) -> np.ndarray:
     return np.frombuffer(hashlib.sha1(np.ascontiguousarray(a).tobytes()).digest(), np.uint8)
 
 
-def ref_config(config: Qwen2Config):
+def ref_config(shape: ModelShape):
     from nanocompile.models.qwen2 import Qwen2Config as RefConfig
-    return RefConfig(*[getattr(config, f) for f in config.__dataclass_fields__])
+    return RefConfig(**shape.config_fields())
 
 
 def run_greedy(model, prompt, steps, cache):
@@ -76,9 +76,9 @@ def make_tiny() -> None:
     from nanocompile.runtime import CBackend
 
     w = synthetic_weights(TINY, seed=0)
-    prompt = synthetic_prompt(TINY.vocab_size, 8)
+    prompt = synthetic_prompt(TINY.vocab, 8)
     out: dict[str, np.ndarray] = {"prompt": np.array(prompt, np.int64),
-                                  "inv_freq": inverse_frequencies(TINY.head_dim, TINY.rope_theta)}
+                                  "inv_freq": TINY.rope_rates()}
     for tag, quant in (("fp32", None), ("vnni", "int8-vnni")):
         model = Qwen2(ref_config(TINY), w, run=CBackend(), quantization=quant)
         tokens, logits = run_greedy(model, prompt, 16, model.new_cache(4))   # capacity 4: forces growth
@@ -143,7 +143,7 @@ def make_05b(quant: str | None, steps: int, name: str) -> None:
     from nanocompile.runtime import CBackend
 
     w = synthetic_weights(QWEN2_0_5B, seed=0)
-    prompt = synthetic_prompt(QWEN2_0_5B.vocab_size, 32)
+    prompt = synthetic_prompt(QWEN2_0_5B.vocab, 32)
     model = Qwen2(ref_config(QWEN2_0_5B), w, run=CBackend(), quantization=quant)
     cache = model.new_cache(32 + steps)
     started = time.perf_counter()
@@ -151,7 +151,7 @@ def make_05b(quant: str | None, steps: int, name: str) -> None:
     print(f"{name}: {steps} steps in {time.perf_counter() - started:.1f} s")
     keys, values = cache.past()
     out = {"prompt": np.array(prompt, np.int64), "tokens": np.array(tokens, np.int64),
-           "inv_freq": inverse_frequencies(QWEN2_0_5B.head_dim, QWEN2_0_5B.rope_theta),
+           "inv_freq": QWEN2_0_5B.rope_rates(),
            "first_logits": logits[:2].copy(),
            "keys_sha1": np.stack([sha1(np.ascontiguousarray(keys[l])) for l in range(keys.shape[0])]),
            "values_sha1": np.stack([sha1(np.ascontiguousarray(values[l])) for l in range(values.shape[0])]),
@@ -191,7 +191,7 @@ def make_prefill(seq: int = 512) -> None:
 
     cfg = QWEN2_0_5B
     w = synthetic_weights(cfg, seed=0)
-    ids = synthetic_prompt(cfg.vocab_size, seq, seed=4)
+    ids = synthetic_prompt(cfg.vocab, seq, seed=4)
     model = Qwen2(ref_config(cfg), w, run=CBackend(), quantization="int8-vnni")
     cache = model.new_cache(seq)
     started = time.perf_counter()
@@ -199,17 +199,23 @@ def make_prefill(seq: int = 512) -> None:
     print(f"prefill {seq}: {time.perf_counter() - started:.1f} s")
     keys, values = cache.past()
     np.savez_compressed(HERE / "prefill.npz", ids=np.array(ids, np.int64), logits=last[0],
-                        keys_sha1=np.stack([sha1(np.ascontiguousarray(keys[l])) for l in range(cfg.num_hidden_layers)]),
-                        values_sha1=np.stack([sha1(np.ascontiguousarray(values[l])) for l in range(cfg.num_hidden_layers)]),
+                        keys_sha1=np.stack([sha1(np.ascontiguousarray(keys[l])) for l in range(cfg.layers)]),
+                        values_sha1=np.stack([sha1(np.ascontiguousarray(values[l])) for l in range(cfg.layers)]),
                         keys_layer23_head1=np.ascontiguousarray(keys[23, 1, ::37]))
 
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default=os.environ.get("NANOCOMPILE_REFERENCE", "/root/reference"))
+    parser.add_argument("--reference", default=None,
+                        help="the nanocompile checkout (default: NANOCOMPILE_REFERENCE, else BASELINE.json's)")
     parser.add_argument("parts", nargs="*", default=["tiny", "proj", "quant", "fp32", "prefill", "batch"])
     args = parser.parse_args()
-    sys.path.insert(1, args.reference)
+    from oracle.build_ref import reference_checkout
+
+    reference = args.reference or reference_checkout()
+    if reference is None:
+        parser.error("no nanocompile checkout: pass --reference or set NANOCOMPILE_REFERENCE")
+    sys.path.insert(1, str(reference))
     os.environ.setdefault("NANOCOMPILE_CACHE", "/tmp/nanocompile-cache")
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
     for part in args.parts:

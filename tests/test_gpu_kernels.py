@@ -319,3 +319,27 @@ def test_gather_reports_the_first_bad_row(cuda):
     assert int(err.numpy()[0]) == 1
     out = dout.numpy()
     assert np.array_equal(out[0], table[1]) and np.array_equal(out[2], table[2])
+
+
+@pytest.mark.parametrize("packed", [0, 1])
+def test_quantize_int8_rows_is_the_references(cuda, packed):
+    """Device quantize_int8 (nanocompile/quantize.py:55-70): the reference's own bytes on its edge
+    cases (tests/golden/proj.npz), and the host scheme's on rows built to hit each rounding step."""
+    g = golden("proj")
+    rng = np.random.default_rng(11)
+    w = (rng.standard_normal((300, 896)) * 0.02).astype(np.float32)
+    w[7] = 0.0                                            # all zero: scale 1
+    w[8] = np.float32(1e-44)                              # max / 127 underflows to 0: scale 1
+    w[9, 0], w[9, 1:40] = 127.0, np.arange(39, dtype=np.float32) - 19.5       # exact half-integers at scale 1
+    w[10, 0], w[10, 1] = 127.0, np.float32(0.5) - np.float32(2.0 ** -25)      # |v| + 0.5 rounds up to 1.0
+    w[11] = np.float32(3e38) * np.sign(w[11])             # near the top of the float range
+    cases = [(g["qi8_w"], g["qi8_values"], g["qi8_scales"]), (w, *q.quantize_int8(w))]
+    for weights, values, scales in cases:
+        rows, cols = weights.shape
+        dw = DeviceArray(cuda, weights)
+        dv = DeviceArray(cuda, shape=(rows, cols), dtype=np.uint8 if packed else np.int8)
+        ds = DeviceArray(cuda, shape=(rows,), dtype=np.float32)
+        call(cuda, "nc_quantize_int8_rows", [dv, ds, dw], [rows, cols, packed])
+        expected = (values.astype(np.int16) + 128).astype(np.uint8) if packed else values
+        assert np.array_equal(dv.numpy(), expected)
+        assert np.array_equal(bits(ds.numpy()), bits(scales))

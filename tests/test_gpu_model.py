@@ -1,7 +1,9 @@
-"""The whole step on the B200 through the public API, against the reference's own outputs.
+"""The whole step on the B200, driven through the reference's own ``Qwen2`` and ``Runner`` API.
 
-Golden vectors come from nanocompile's CBackend on the same seeded weights (tests/golden);
-the GPU must give the same tokens and the same logits to the bit.
+``nanocompile.models.qwen2.Qwen2(config, weights, run=CUDABackend(), quantization=...)`` is the
+reference's driver, unchanged (the copy ``oracle/build_ref.py`` ships); the CUDA backend is the
+only thing swapped in. Golden vectors come from the reference's CBackend on the same seeded
+weights (tests/golden): the GPU must give the same tokens, and the same logits to the bit.
 """
 
 from __future__ import annotations
@@ -11,7 +13,7 @@ import hashlib
 import numpy as np
 import pytest
 
-from nanocompile_b200.qwen2 import QWEN2_0_5B, SMALL, TINY, Qwen2, greedy, synthetic_cache, synthetic_weights
+from nanocompile_b200.model import QWEN2_0_5B, SMALL, TINY, synthetic_cache, synthetic_weights
 from tests.conftest import bits, golden
 
 pytestmark = pytest.mark.gpu
@@ -21,16 +23,25 @@ def sha1(a) -> np.ndarray:
     return np.frombuffer(hashlib.sha1(np.ascontiguousarray(a, np.float32).tobytes()).digest(), np.uint8)
 
 
+def ref_model(reference, cuda, shape, weights, quantization, **backend):
+    from nanocompile.models.qwen2 import Qwen2, Qwen2Config
+
+    return Qwen2(Qwen2Config(**shape.config_fields()), weights, run=cuda.CUDABackend(device=0, **backend),
+                 quantization=quantization)
+
+
 @pytest.fixture(scope="module")
-def tiny_models(cuda):
+def tiny_models(reference, cuda):
     w = synthetic_weights(TINY, seed=0)
-    backend = cuda.CUDABackend(device=0, capacity=64, slots=4, max_rows=16)
-    return {"fp32": Qwen2(TINY, w, run=backend, quantization=None),
-            "vnni": Qwen2(TINY, w, run=backend, quantization="int8-vnni")}
+    return {"fp32": ref_model(reference, cuda, TINY, w, None, capacity=64, slots=4, max_rows=16),
+            "vnni": ref_model(reference, cuda, TINY, w, "int8-vnni", capacity=64, slots=4, max_rows=16)}
 
 
 @pytest.mark.parametrize("tag", ["fp32", "vnni"])
-def test_tiny_greedy_tokens_and_logits_are_the_references(tiny_models, tag):
+def test_tiny_reference_greedy_tokens_and_logits(tiny_models, tag):
+    """The reference's own greedy loop and host KVCache over the CUDA runner."""
+    from nanocompile.models.qwen2 import greedy
+
     g = golden("tiny")
     model = tiny_models[tag]
     prompt = list(g["prompt"])
@@ -45,78 +56,99 @@ def test_tiny_greedy_tokens_and_logits_are_the_references(tiny_models, tag):
 
 
 @pytest.mark.parametrize("tag", ["fp32", "vnni"])
-def test_tiny_full_chunked_and_stateless_steps(tiny_models, tag):
+def test_tiny_full_chunked_and_device_cache_steps(tiny_models, cuda, tag):
     g = golden("tiny")
     model = tiny_models[tag]
     prompt = list(g["prompt"])
     assert np.array_equal(bits(model.forward(prompt)), bits(g[f"{tag}_full_logits"]))
-    cache = model.new_cache(32)
-    rows = [model.forward(prompt[:5], cache=cache)] + [model.forward([t], cache=cache) for t in prompt[5:]]
-    assert np.array_equal(bits(np.concatenate(rows)), bits(g[f"{tag}_chunked_logits"]))
-    keys, values = cache.past()
-    assert np.array_equal(bits(keys), bits(g[f"{tag}_keys"])) and np.array_equal(bits(values), bits(g[f"{tag}_values"]))
-    # the reference's stateless Runner contract: host KV in, new KV out
-    from nanocompile_b200.qwen2 import KVCache
-
-    host = KVCache(TINY, 4)
+    host = model.new_cache(4)                                    # the reference's KVCache, grown by doubling
     rows = [model.forward(prompt[:5], cache=host)] + [model.forward([t], cache=host) for t in prompt[5:]]
     assert np.array_equal(bits(np.concatenate(rows)), bits(g[f"{tag}_chunked_logits"]))
     hk, hv = host.past()
     assert np.array_equal(bits(hk), bits(g[f"{tag}_keys"])) and np.array_equal(bits(hv), bits(g[f"{tag}_values"]))
+    device = cuda.new_device_cache(model, 32)                    # the history stays in HBM
+    rows = [device.forward(prompt[:5])] + [device.forward([t]) for t in prompt[5:]]
+    assert np.array_equal(bits(np.concatenate(rows)), bits(g[f"{tag}_chunked_logits"]))
+    dk, dv = device.past()
+    assert np.array_equal(bits(dk), bits(g[f"{tag}_keys"])) and np.array_equal(bits(dv), bits(g[f"{tag}_values"]))
+    assert cuda.device_greedy(model, prompt, 16) == list(g[f"{tag}_tokens"])
 
 
-def test_bad_token_ids_raise_kernel_error(tiny_models, cuda):
+def test_bad_token_ids_raise_the_references_kernel_error(tiny_models, cuda):
+    from nanocompile.runtime import KernelError
+    from nanocompile.models.qwen2 import greedy
+
     model = tiny_models["vnni"]
-    with pytest.raises(cuda.KernelError, match="index 256"):
+    with pytest.raises(KernelError, match="gather index 256 is outside 0..255"):
         model.forward([1, 256])
-    with pytest.raises(cuda.KernelError, match="index -1"):
+    with pytest.raises(cuda.KernelError, match="gather index -1 is outside 0..255"):
         model.forward([-1])
-    assert greedy(model, [1, 2], 2) == greedy(model, [1, 2], 2)      # the model still works after
+    assert greedy(model, [1, 2], 2) == cuda.device_greedy(model, [1, 2], 2)      # the model still works after
 
 
-def oracle_decode(oracle, first, keys, values, steps):
-    """Greedy tokens of one sequence after its cached history, step by step on the CPU oracle."""
-    out, token = [], first
-    for _ in range(steps):
-        logits, k, v = oracle.step([token], keys, values)
-        keys, values = np.concatenate([keys, k], 2), np.concatenate([values, v], 2)
-        token = int(np.argmax(logits[0]))
-        out.append(token)
-    return out
+def test_argument_errors_are_the_interpreters(tiny_models):
+    from nanocompile.interpreter import InterpreterError
+
+    model = tiny_models["vnni"]
+    zeros = np.zeros((2, 2, 3, 16), np.float32)
+    step = model.run.compiled(model.graph_last)
+    with pytest.raises(InterpreterError, match="already bound"):
+        step({"token_ids": np.array([1], np.int64), "past_keys": zeros, "past_values": zeros[:, :, :2]}, model.weights)
+    with pytest.raises(InterpreterError, match="missing"):
+        step({"token_ids": np.array([1], np.int64)}, model.weights)
+    big = np.zeros((2, 2, 64, 16), np.float32)                   # past + seq beyond the backend's capacity
+    with pytest.raises(InterpreterError, match="capacity"):
+        step({"token_ids": np.array([1], np.int64), "past_keys": big, "past_values": big}, model.weights)
+
+
+def test_profile_and_plan_of_a_stateless_call(tiny_models):
+    model = tiny_models["vnni"]
+    step = model.run.compiled(model.graph)
+    zeros = np.zeros((2, 2, 0, 16), np.float32)
+    profile: dict[str, float] = {}
+    out = step({"token_ids": np.array([3, 1, 4], np.int64), "past_keys": zeros, "past_values": zeros}, model.weights,
+               profile=profile)
+    assert out["logits"].shape == (3, 256) and out["keys"].shape == (2, 2, 3, 16)
+    assert {"gather", "attention", "lm_head_argmax"} <= set(profile) and all(v > 0 for v in profile.values())
+    plan = step.last_plan
+    assert plan.rows == 3 and plan.past == 0 and plan.kv_bytes_out == 3 * 2 * 2 * 16 * 4 * 2 and plan.arena_bytes > 0
 
 
 @pytest.mark.parametrize("rows", [1, 2, 4])
 def test_small_persistent_step_is_the_oracles(cuda, rows):
     """SMALL through the persistent step + int8 LM head (1..4 rows), against the oracle."""
+    from nanocompile_b200 import quantize as q
     from oracle.oracle import OracleModel
 
-    w = synthetic_weights(SMALL, seed=3)
-    backend = cuda.CUDABackend(device=0, capacity=200, slots=4, max_rows=8)
-    model = Qwen2(SMALL, w, run=backend, quantization="int8-vnni")
-    oracle = OracleModel(SMALL, model.weights, "int8")
+    w = q.int8_projection_weights(synthetic_weights(SMALL, seed=3), SMALL)
+    model = cuda.DeviceModel(SMALL, w, "int8", max_rows=8, slots=4, capacity=200)
+    oracle = OracleModel(SMALL, w, "int8")
     first, keys, values = [], [], []
     for b in range(rows):
         k, v, t = synthetic_cache(SMALL, 7 + b, 37 + 29 * b)
+        model.kv_write(b, 0, k, v)
         keys.append(k)
         values.append(v)
         first.append(t)
-    tokens = cuda.batched_greedy(model, first, keys, values, 24)     # ragged histories, one replay per step
+    tokens, _ = model.decode(first, list(range(rows)), [k.shape[2] for k in keys], 24)   # ragged histories
     for b in range(rows):
-        assert list(tokens[b]) == oracle_decode(oracle, first[b], keys[b], values[b], 24), b
-    compiled = backend.compiled(model.graph_last, model.weights)
-    kinds = compiled.model.profile(first, list(range(rows)), [k.shape[2] for k in keys], 1)
+        assert list(tokens[:, b]) == oracle.greedy([first[b]], 24, keys[b], values[b]), b
+    kinds = model.profile(first, list(range(rows)), [k.shape[2] for k in keys], 1)
     assert "persistent_layers" in kinds and "lm_head_argmax" in kinds, kinds
 
 
 @pytest.fixture(scope="module")
-def vnni_05b(cuda, qwen05b_weights):
-    backend = cuda.CUDABackend(device=0, capacity=1100, slots=2, max_rows=64)
-    return Qwen2(QWEN2_0_5B, qwen05b_weights, run=backend, quantization="int8-vnni")
+def vnni_05b(reference, cuda, qwen05b_weights):
+    return ref_model(reference, cuda, QWEN2_0_5B, qwen05b_weights, "int8-vnni", capacity=1100, slots=2, max_rows=512)
 
 
-def test_05b_int8_vnni_greedy_993_tokens_are_the_references(vnni_05b):
-    """Config 3: 32-token prompt, greedy decode up to past = 1024, CUDA-graph replays."""
+def test_05b_int8_vnni_greedy_993_tokens_are_the_references(vnni_05b, cuda):
+    """Configuration 3: 32-token prompt, greedy to past 1024 -- the reference's greedy over the
+    stateless runner (its host KVCache each step), and the device-resident decode."""
+    from nanocompile.models.qwen2 import greedy
+
     g = golden("qwen05b_vnni")
+    assert cuda.device_greedy(vnni_05b, list(g["prompt"]), 993) == list(g["tokens"])
     assert greedy(vnni_05b, list(g["prompt"]), 993) == list(g["tokens"])
 
 
@@ -131,24 +163,27 @@ def test_05b_int8_vnni_step_logits_are_the_references(vnni_05b):
     assert np.array_equal(bits(g["samples"][47]), bits(lg[::1009]))
 
 
-def test_05b_prefill_512_is_the_references(vnni_05b):
-    """Config 4: one step over 512 prompt tokens at past 0."""
+def test_05b_prefill_512_is_the_references(vnni_05b, cuda):
+    """Configuration 4: one step over 512 prompt tokens at past 0, host and device caches."""
     g = golden("prefill")
-    cache = vnni_05b.new_cache(600)
-    lg = vnni_05b.forward(list(g["ids"]), cache=cache, last_only=True)[0]
-    assert np.array_equal(bits(lg), bits(g["logits"]))
-    keys, values = cache.past()
-    for layer in range(QWEN2_0_5B.num_hidden_layers):
-        assert np.array_equal(sha1(keys[layer]), g["keys_sha1"][layer])
-        assert np.array_equal(sha1(values[layer]), g["values_sha1"][layer])
+    for cache in (vnni_05b.new_cache(600), cuda.new_device_cache(vnni_05b, 600)):
+        if hasattr(cache, "forward"):
+            lg = cache.forward(list(g["ids"]), last_only=True)[0]
+        else:
+            lg = vnni_05b.forward(list(g["ids"]), cache=cache, last_only=True)[0]
+        assert np.array_equal(bits(lg), bits(g["logits"]))
+        keys, values = cache.past()
+        for layer in range(QWEN2_0_5B.layers):
+            assert np.array_equal(sha1(keys[layer]), g["keys_sha1"][layer])
+            assert np.array_equal(sha1(values[layer]), g["values_sha1"][layer])
 
 
-def test_05b_batched_decode_is_the_references(cuda, qwen05b_weights):
-    """Config 5: 64 sequences from N(0,1) caches of 2048 positions, 64 greedy steps each."""
+def test_05b_batched_decode_is_the_references(reference, cuda, qwen05b_weights):
+    """Configuration 5: 64 sequences from N(0,1) caches of 2048 positions, 64 greedy steps each."""
     g = golden("batch")
     past = int(g["past"])
-    backend = cuda.CUDABackend(device=0, capacity=past + 64, slots=64, max_rows=64)
-    model = Qwen2(QWEN2_0_5B, qwen05b_weights, run=backend, quantization="int8-vnni")
+    model = ref_model(reference, cuda, QWEN2_0_5B, qwen05b_weights, "int8-vnni", capacity=past + 64, slots=64,
+                      max_rows=64)
     first, keys, values = [], [], []
     for b in range(64):
         k, v, t = synthetic_cache(QWEN2_0_5B, b, past)
@@ -162,29 +197,41 @@ def test_05b_batched_decode_is_the_references(cuda, qwen05b_weights):
 
 
 @pytest.mark.parametrize("rows", [1, 3, 4])
-def test_05b_small_batched_decode_is_the_references(cuda, qwen05b_weights, rows):
-    """A few of config 5's sequences at once: the persistent decode step (up to four rows)."""
+def test_05b_small_batched_decode_is_the_references(cuda, qwen05b_vnni_weights, rows):
+    """A few of configuration 5's sequences at once: the persistent decode step (up to four rows)."""
     g = golden("batch")
     past = int(g["past"])
-    backend = cuda.CUDABackend(device=0, capacity=past + 64, slots=8, max_rows=8)
-    model = Qwen2(QWEN2_0_5B, qwen05b_weights, run=backend, quantization="int8-vnni")
+    model = cuda.DeviceModel(QWEN2_0_5B, qwen05b_vnni_weights, "int8", max_rows=8, slots=8, capacity=past + 64)
     pick = [5, 17, 40, 63][:rows]
-    first, keys, values = [], [], []
-    for b in pick:
-        k, v, t = synthetic_cache(QWEN2_0_5B, b, past)
-        keys.append(k)
-        values.append(v)
+    first = []
+    for b, sequence in enumerate(pick):
+        k, v, t = synthetic_cache(QWEN2_0_5B, sequence, past)
+        model.kv_write(b, 0, k, v)
         first.append(t)
-    tokens = cuda.batched_greedy(model, first, keys, values, 64)
-    assert np.array_equal(tokens, g["tokens"][pick, 1:])
+    tokens, _ = model.decode(first, list(range(rows)), [past] * rows, 64)
+    assert np.array_equal(tokens.T, g["tokens"][pick, 1:])
+    model.close()
 
 
-def test_05b_fp32_greedy_is_the_references(cuda, qwen05b_weights):
-    """Config 2: float32 projections, 32-token prompt, 128 greedy steps."""
+def test_05b_device_quantized_weights_decode_the_same(cuda, qwen05b_weights, qwen05b_vnni_weights):
+    """float32 projections uploaded and quantized on the device give the host quantizer's bytes:
+    the same 24 greedy tokens as the golden run."""
+    g = golden("qwen05b_vnni")
+    model = cuda.DeviceModel(QWEN2_0_5B, qwen05b_weights, "int8", max_rows=64, slots=1, capacity=128)
+    _, tok = model.run(np.asarray(g["prompt"], np.int64), 0, 0, last_only=True, want_logits=False)
+    more, _ = model.decode([int(tok[0])], [0], [len(g["prompt"])], 23)
+    assert [int(tok[0])] + [int(t) for t in more[:, 0]] == list(g["tokens"][:24])
+    model.close()
+
+
+def test_05b_fp32_greedy_is_the_references(reference, cuda, qwen05b_weights):
+    """Configuration 2: float32 projections, 32-token prompt, 128 greedy steps."""
+    from nanocompile.models.qwen2 import greedy
+
     g = golden("qwen05b_fp32")
-    backend = cuda.CUDABackend(device=0, capacity=200, slots=2, max_rows=64)
-    model = Qwen2(QWEN2_0_5B, qwen05b_weights, run=backend, quantization=None)
-    assert greedy(model, list(g["prompt"]), 128) == list(g["tokens"])
+    model = ref_model(reference, cuda, QWEN2_0_5B, qwen05b_weights, None, capacity=200, slots=2, max_rows=64)
+    assert cuda.device_greedy(model, list(g["prompt"]), 128) == list(g["tokens"])
     cache = model.new_cache(200)
     lg = model.forward(list(g["prompt"]), cache=cache, last_only=True)[0]
     assert np.array_equal(bits(lg), bits(g["first_logits"][0]))
+    assert greedy(model, list(g["prompt"]), 8) == list(g["tokens"][:8])

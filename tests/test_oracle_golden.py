@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from nanocompile_b200 import quantize as q
-from nanocompile_b200.qwen2 import QWEN2_0_5B, TINY, build_qwen2, inverse_frequencies, quantize, synthetic_weights
+from nanocompile_b200.model import QWEN2_0_5B, TINY, ModelShape, synthetic_weights
 from oracle import oracle
 from tests.conftest import bits, golden
 
@@ -21,8 +21,7 @@ def tiny_weights(activations):
     w = synthetic_weights(TINY, seed=0)
     if activations is None:
         return w
-    graph = quantize(build_qwen2(TINY), activations, keep=("lm_head.weight",))
-    return q.quantized_weights(graph, w)
+    return q.int8_projection_weights(w, TINY)
 
 
 @pytest.mark.parametrize("tag,activations", [("fp32", None), ("vnni", "int8")])
@@ -39,7 +38,7 @@ def test_oracle_tiny_full_and_chunked_passes(tag, activations):
     g = golden("tiny")
     model = oracle.OracleModel(TINY, tiny_weights(activations), activations)
     prompt = list(g["prompt"])
-    zeros = np.zeros((TINY.num_hidden_layers, TINY.num_key_value_heads, 0, TINY.head_dim), np.float32)
+    zeros = np.zeros((TINY.layers, TINY.kv_heads, 0, TINY.head_dim), np.float32)
     full, keys, values = model.step(prompt, zeros, zeros, last_only=False)
     assert np.array_equal(bits(full), bits(g[f"{tag}_full_logits"]))
     assert np.array_equal(bits(keys), bits(g[f"{tag}_keys"]))
@@ -55,8 +54,8 @@ def test_oracle_tiny_full_and_chunked_passes(tag, activations):
 
 
 def test_inverse_frequencies_are_the_references():
-    assert np.array_equal(bits(inverse_frequencies(TINY.head_dim, TINY.rope_theta)), bits(golden("tiny")["inv_freq"]))
-    assert np.array_equal(bits(inverse_frequencies(64, 1e6)), bits(golden("qwen05b_vnni")["inv_freq"]))
+    assert np.array_equal(bits(TINY.rope_rates()), bits(golden("tiny")["inv_freq"]))
+    assert np.array_equal(bits(QWEN2_0_5B.rope_rates()), bits(golden("qwen05b_vnni")["inv_freq"]))
 
 
 def test_quantize_int8_is_the_references_byte_for_byte():

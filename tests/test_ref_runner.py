@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 from tests.conftest import bits, golden
-from nanocompile_b200.qwen2 import QWEN2_0_5B, synthetic_cache
+from nanocompile_b200.model import QWEN2_0_5B, synthetic_cache
 from oracle import oracle
 
 ref_runner = pytest.importorskip("oracle.ref_runner")

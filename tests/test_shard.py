@@ -11,7 +11,8 @@ import socket
 import numpy as np
 import pytest
 
-from nanocompile_b200.shard import RankGroup, decode_shard, rank_sequences
+from bench import RankGroup
+from nanocompile_b200.shard import decode_shard, rank_sequences
 
 PER_RANK, STEPS, PAST = 3, 4, 16
 
@@ -33,11 +34,10 @@ def test_single_process_group_is_the_identity():
 
 def _tiny_decoder():
     from nanocompile_b200 import quantize as q
-    from nanocompile_b200.qwen2 import TINY, build_qwen2, quantize, synthetic_cache, synthetic_weights
+    from nanocompile_b200.model import TINY, synthetic_cache, synthetic_weights
     from oracle.oracle import OracleModel
 
-    graph = quantize(build_qwen2(TINY, last_only=True), "int8", keep=("lm_head.weight",))
-    model = OracleModel(TINY, q.quantized_weights(graph, synthetic_weights(TINY, seed=5)), "int8", threads=1)
+    model = OracleModel(TINY, q.int8_projection_weights(synthetic_weights(TINY, seed=5), TINY), "int8", threads=1)
 
     def decode(sequences):
         out = []
