@@ -85,6 +85,19 @@ int32_t nc_quantize_blocks(void **p, const int64_t *s, void *stream);
  * s: rows, n, k, epilogue (0 none, 1 bias, 2 residual, 3 silu(y0) * y1) */
 int32_t nc_matmul_i8_vnni(void **p, const int64_t *s, void *stream);
 
+/* The same projection on the tensor cores (tcgen05.mma kind::i8, block-diagonal activations so
+ * every 4-byte Dp4 lane stays its own int32), bit for bit the reference's matmul_i8_vnni
+ * (nanocompile/lower.py:363-397 with _combine, lower.py:298-317, and the fused epilogues of
+ * nanocompile/fusion.py:699-711).  The model runtime takes it for steps of more than four rows.
+ * p: [0] out f32[m, n] (unused by epilogue 4)  [1] xq i8[m, k]  [2] xs f32[m, k/32]
+ *    [3] offset f32[m] (prologue 0)  [4] w u8[n, k] (int8 + 128)  [5] scales f32[n]
+ *    [6] bias / residual / second weight (SwiGLU)  [7] second scales (SwiGLU)
+ *    [8] block sums i32[m, k/32] (prologue 2: the offset is 128 * in-order sum of sum_b * xs_b)
+ *    [9] xq out i8[m, n]  [10] xs out f32[m, n/32]  [11] block sums out i32[m, n/32] (epilogue 4)
+ * s: m, n, k, epilogue (0 none, 1 bias, 2 residual, 3 silu(gate)*up, 4 the same block-quantized),
+ *    prologue (0 given offsets, 2 from block sums), tokens per work item (0 by shape, 4, 8) */
+int32_t nc_matmul_i8_tc(void **p, const int64_t *s, void *stream);
+
 /* float32 matmul with epilogue (nanocompile/lower.py:255-274, fusion.py:652-675):
  * acc = acc + x[k] * w[n, k] in index order, no FMA.
  * p: [0] out f32[rows, n]  [1] x f32[rows, k]  [2] w f32[n, k]  [3] epilogue operand
@@ -152,6 +165,19 @@ int32_t nc_attention_cache(void **p, const int64_t *s, void *stream);
 /* NC_ERR_KERNEL if a kernel recorded a device-side fault since the last call (a TMA stage of
  * the grouped attention kernel that did not arrive within its bounded wait); clears it. */
 int32_t nc_device_faults(void);
+
+/* Bounds the library's abandonable device-side waits (pipeline stages of the tensor-core
+ * projection, the self-test below) to `cycles` SM clock cycles on the current device; <= 0
+ * restores the default 2^31 (about a second).  A wait that runs out makes its kernel stop, drain
+ * the copies and MMAs it has in flight, free its TMEM and record a fault that the next
+ * nc_device_faults / model call reports as NC_ERR_KERNEL.  For tests of that path. */
+int32_t nc_set_wait_limit(int64_t cycles);
+
+/* Runs one of the bounded waits against a condition that never comes true, with nothing in
+ * flight: kind 0 polls hand-over words that never carry their tag (the persistent decode
+ * step's wait), kind 1 waits on an mbarrier whose bytes never arrive (a pipeline stage wait).
+ * Returns NC_ERR_KERNEL once the wait has given up (and clears the fault), NC_OK never. */
+int32_t nc_selftest_wait(int32_t kind);
 
 /* int8 weights as the kernels read them: u8 = int8 + 128 (one XOR per byte). */
 int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t bytes);

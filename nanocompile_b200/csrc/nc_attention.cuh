@@ -91,7 +91,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity) {
     const long long start = clock64();
     while (!mbar_try_wait(bar, parity))
-        if (clock64() - start > (1ll << 31)) return false;
+        if (clock64() - start > NC_DRAIN_CYCLES) return false;
+    return true;
+}
+// Bounded by `limit` cycles (g_wait_cycles for the waits a kernel can abandon and drain after).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, unsigned parity, long long limit) {
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - start > limit) return false;
     return true;
 }
 // One 2-D tile of the tensor map (x = column, y = row) into shared memory, counted on bar.

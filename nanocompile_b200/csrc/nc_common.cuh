@@ -267,6 +267,15 @@ __device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.
     return acc;
 }
 
+// ---- bounded waits ------------------------------------------------------------------------------
+// Every spin on a flag or an mbarrier gives up after a number of SM cycles.  Waits after which a
+// kernel can stop, drain what it has in flight and return use g_wait_cycles (default 2^31, about a
+// second; nc_set_wait_limit changes it per device, for tests that make a wait run out); the waits
+// that drain work already in flight, and the waits of kernels that cannot stop early, use the
+// fixed NC_DRAIN_CYCLES.
+__device__ long long g_wait_cycles = 1ll << 31;
+constexpr long long NC_DRAIN_CYCLES = 1ll << 31;
+
 // ---- programmatic dependent launch -----------------------------------------------------------
 // Every kernel of a step is launched with programmatic stream serialization: it may start while
 // the previous kernel still runs, loads what does not depend on it (weights, scales, the KV

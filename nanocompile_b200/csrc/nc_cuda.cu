@@ -13,6 +13,7 @@
 #include "nc_lm_head_q8.cuh"
 #include "nc_decode_mk.cuh"
 #include "nc_gemm_i8.cuh"
+#include "nc_gemm_i8_tc.cuh"
 
 #include <climits>
 #include <cmath>
@@ -142,6 +143,21 @@ bool tc_head_enabled() {
         return !(v && v[0] == '0');
     }();
     return on;
+}
+
+bool tc_i8_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("NC_TC_I8");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+int sm_count() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148;
+    return sms > 0 ? sms : 148;
 }
 
 template <typename... KArgs, typename... Args>
@@ -431,6 +447,77 @@ int32_t make_kv_map(CUtensorMap *map, float *base, int64_t rows, int d) {
     return NC_OK;
 }
 
+// A 2-D tensor map over int8 weights [n, k] (u8, k bytes per row): 128-byte x box_rows boxes,
+// 128-byte swizzle, the K-major operand layout of tcgen05.mma; rows past n read as zeros.
+int32_t make_i8_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t k, int box_rows) {
+    static EncodeTiledFn encode = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(fn);
+    }();
+    if (!encode) return fail(NC_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    if (n <= 0 || n >= (int64_t(1) << 31) || k <= 0 || k % QBLOCK || ((uintptr_t)w & 15))
+        return fail(NC_ERR_ARGUMENT, "no tensor map for int8 weights %lld x %lld", (long long)n, (long long)k);
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)k};
+    const cuuint32_t box[2] = {(cuuint32_t)CHUNK, (cuuint32_t)box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)w, dims, strides, box, elem,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NC_ERR_CUDA, "cuTensorMapEncodeTiled (int8 weights) failed (%d)", (int)r);
+    return NC_OK;
+}
+
+// The tensor-core int8 projection (more than four rows): persistent CTAs over items of 128 weight
+// rows x T tokens; T = 8 when that still gives every SM two items, else 4.
+template <int T, int PRO, int EPI>
+int32_t launch_i8_tc_t(cudaStream_t st, const FusedI8Args &f, const CUtensorMap &m1, const CUtensorMap &m2) {
+    constexpr bool TWO = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT;
+    auto kernel = gemm_i8_tc_kernel<T, PRO, EPI>;
+    const I8TcLayout L = i8tc_layout(T, f.g.k);
+    if (L.bytes > 227 * 1024) return fail(NC_ERR_ARGUMENT, "int8 width %d too wide for the tensor-core projection", f.g.k);
+    CUDA_TRY(allow_smem(kernel, L.bytes));
+    const int row_tiles = TWO ? (f.g.n + 63) / 64 : (f.g.n + I8TC_ROWS - 1) / I8TC_ROWS;
+    const int items = row_tiles * ((f.g.m + T - 1) / T);
+    CUDA_TRY(launch_k(kernel, std::min(items, sm_count()), I8TC_THREADS, L.bytes, st, f, m1, m2));
+    return check_launch("gemm_i8_tc_kernel");
+}
+
+template <int T, int PRO>
+int32_t launch_i8_tc_epi(cudaStream_t st, const FusedI8Args &f, int epi, const CUtensorMap &m1, const CUtensorMap &m2) {
+    switch (epi) {
+        case EPI_NONE: return launch_i8_tc_t<T, PRO, EPI_NONE>(st, f, m1, m2);
+        case EPI_BIAS: return launch_i8_tc_t<T, PRO, EPI_BIAS>(st, f, m1, m2);
+        case EPI_RESIDUAL: return launch_i8_tc_t<T, PRO, EPI_RESIDUAL>(st, f, m1, m2);
+        case EPI_SWIGLU: return launch_i8_tc_t<T, PRO, EPI_SWIGLU>(st, f, m1, m2);
+        case EPI_SWIGLU_QUANT: return launch_i8_tc_t<T, PRO, EPI_SWIGLU_QUANT>(st, f, m1, m2);
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+}
+
+// tokens: 0 chooses by shape, else 4 or 8.
+int32_t launch_i8_tc(cudaStream_t st, const FusedI8Args &f, int pro, int epi, const CUtensorMap &m1,
+                     const CUtensorMap &m2, int tokens = 0) {
+    const GemvI8Args &a = f.g;
+    if (a.m <= 0 || a.n <= 0) return NC_OK;
+    if (a.k % QBLOCK) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a whole number of 32-blocks", a.k);
+    if (epi == EPI_SWIGLU_QUANT && a.n % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized output width %d", a.n);
+    const bool two = epi == EPI_SWIGLU || epi == EPI_SWIGLU_QUANT;
+    const int row_tiles = two ? (a.n + 63) / 64 : (a.n + I8TC_ROWS - 1) / I8TC_ROWS;
+    if (tokens == 0) tokens = row_tiles * ((a.m + 7) / 8) >= 2 * sm_count() ? 8 : 4;
+    if (tokens != 4 && tokens != 8) return fail(NC_ERR_ARGUMENT, "tokens per item %d: 4 or 8", tokens);
+    if (pro != PRO_NONE && pro != PRO_OFFSET) return fail(NC_ERR_ARGUMENT, "prologue %d is not a batched one", pro);
+    if (tokens == 8)
+        return pro == PRO_NONE ? launch_i8_tc_epi<8, PRO_NONE>(st, f, epi, m1, m2)
+                               : launch_i8_tc_epi<8, PRO_OFFSET>(st, f, epi, m1, m2);
+    return pro == PRO_NONE ? launch_i8_tc_epi<4, PRO_NONE>(st, f, epi, m1, m2)
+                           : launch_i8_tc_epi<4, PRO_OFFSET>(st, f, epi, m1, m2);
+}
+
 template <int D, int G, bool TMA>
 int32_t launch_attention_batched(cudaStream_t st, const AttnArgs &a, int rows, const CUtensorMap &map) {
     auto kernel = attention_batched_kernel<D, G, TMA>;
@@ -534,13 +621,14 @@ int32_t check_device_faults() {
     if (fault) {
         const unsigned int zero = 0;
         CUDA_TRY(cudaMemcpyToSymbol(g_attention_fault, &zero, sizeof(zero)));
-        return fail(NC_ERR_KERNEL, "attention: a K/V stage did not arrive within its wait limit");
+        return fail(NC_ERR_KERNEL, "a pipeline stage (K/V, weight tile or tensor-core result) did not arrive within "
+                                   "its wait limit");
     }
     CUDA_TRY(cudaMemcpyFromSymbol(&fault, g_mk_fault, sizeof(fault)));
     if (fault) {
         const unsigned int zero = 0;
         CUDA_TRY(cudaMemcpyToSymbol(g_mk_fault, &zero, sizeof(zero)));
-        return fail(NC_ERR_KERNEL, "persistent decode step: a grid barrier was not reached within its wait limit");
+        return fail(NC_ERR_KERNEL, "persistent decode step: a hand-over word did not arrive within its wait limit");
     }
     return NC_OK;
 }
@@ -594,6 +682,40 @@ extern "C" int32_t nc_matmul_i8_vnni(void **p, const int64_t *s, void *stream) {
         a.scales2 = (const float *)p[7];
     }
     return launch_i8((cudaStream_t)stream, a, epi);
+}
+
+extern "C" int32_t nc_matmul_i8_tc(void **p, const int64_t *s, void *stream) {
+    FusedI8Args f{};
+    GemvI8Args &a = f.g;
+    a.out = (float *)p[0];
+    a.xq = (const int8_t *)p[1];
+    a.xs = (const float *)p[2];
+    a.offset = (const float *)p[3];
+    a.w = (const uint8_t *)p[4];
+    a.scales = (const float *)p[5];
+    a.m = (int)s[0];
+    a.n = (int)s[1];
+    a.k = (int)s[2];
+    const int epi = (int)s[3], pro = (int)s[4], tokens = (int)s[5];
+    if (epi == EPI_BIAS) a.bias = (const float *)p[6];
+    if (epi == EPI_RESIDUAL) a.residual = (const float *)p[6];
+    if (epi == EPI_SWIGLU || epi == EPI_SWIGLU_QUANT) {
+        a.w2 = (const uint8_t *)p[6];
+        a.scales2 = (const float *)p[7];
+    }
+    if (pro == PRO_OFFSET) f.bsums_in = (const int32_t *)p[8];
+    if (epi == EPI_SWIGLU_QUANT) {
+        f.q_out = (int8_t *)p[9];
+        f.xs_out = (float *)p[10];
+        f.bsums_out = (int32_t *)p[11];
+    }
+    if (a.m <= 0 || a.n <= 0) return NC_OK;
+    const bool two = epi == EPI_SWIGLU || epi == EPI_SWIGLU_QUANT;
+    CUtensorMap m1, m2;
+    NC_TRY(make_i8_map(&m1, a.w, a.n, a.k, two ? 64 : I8TC_ROWS));
+    m2 = m1;
+    if (two) NC_TRY(make_i8_map(&m2, a.w2, a.n, a.k, 64));
+    return launch_i8_tc((cudaStream_t)stream, f, pro, epi, m1, m2, tokens);
 }
 
 extern "C" int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream) {
@@ -736,6 +858,27 @@ extern "C" int32_t nc_attention_cache(void **p, const int64_t *s, void *stream) 
 
 extern "C" int32_t nc_device_faults(void) { return check_device_faults(); }
 
+extern "C" int32_t nc_set_wait_limit(int64_t cycles) {
+    const long long v = cycles > 0 ? (long long)cycles : (1ll << 31);
+    CUDA_TRY(cudaMemcpyToSymbol(g_wait_cycles, &v, sizeof(v)));
+    return NC_OK;
+}
+
+extern "C" int32_t nc_selftest_wait(int32_t kind) {
+    if (kind != 0 && kind != 1) return fail(NC_ERR_ARGUMENT, "wait kind %d: 0 hand-over word, 1 pipeline stage", kind);
+    unsigned long long *words = nullptr;
+    CUDA_TRY(cudaMalloc(&words, 64 * sizeof(unsigned long long)));
+    cudaError_t e = cudaMemset(words, 0, 64 * sizeof(unsigned long long));
+    if (e == cudaSuccess) {
+        wait_selftest_kernel<<<1, MK_THREADS>>>(words, 64, kind);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(words);
+    if (e != cudaSuccess) return fail(NC_ERR_CUDA, "wait self-test: %s", cudaGetErrorString(e));
+    return check_device_faults();
+}
+
 extern "C" int32_t nc_pack_int8_weights(void *dst_device, const int8_t *src_host, int64_t bytes) {
     CUDA_TRY(cudaMemcpy(dst_device, src_host, (size_t)bytes, cudaMemcpyHostToDevice));
     xor80_kernel<<<1024, 256>>>((uint8_t *)dst_device, bytes);
@@ -797,7 +940,9 @@ struct nc_model {
         uint8_t *wqkv, *wo, *wg, *wu, *wd;    // int8 mode
         float *sqkv, *so, *sg, *su, *sd;
         float *fqkv, *fo, *fg, *fu, *fd;      // float32 mode
+        CUtensorMap mqkv, mo, mg, mu, md;     // int8 mode: the weights as tensor-core operand tiles
     };
+    bool tc_i8 = false;                       // the tensor maps above are valid
     std::vector<Layer> layers;
     float *kv = nullptr;            // [slot][layer][2][kv][cap][d]
     int64_t slot_stride = 0, layer_stride = 0;
@@ -977,6 +1122,14 @@ int32_t launch_lm_head_q8(nc_model *m, int rows) {
     return launch_lm_head_q8(m->stream, a);
 }
 
+// An int8 projection of the step: more than four rows take the tensor cores when the model has
+// its weights' tensor maps (NC_TC_I8=0 keeps them on the dp4a kernels).
+int32_t model_i8(nc_model *m, const FusedI8Args &f, int pro, int epi, const CUtensorMap &m1, const CUtensorMap &m2) {
+    if (m->tc_i8 && tc_i8_enabled() && f.g.m > PRO_NORM_ROWS && pro != PRO_NORM)
+        return launch_i8_tc(m->stream, f, pro, epi, m1, m2);
+    return launch_i8_fused(m->stream, f, pro, epi);
+}
+
 // Gather, the layers as separate fused-group kernels, and the final norm of the logit rows.
 int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
     const nc_qwen2_config &c = m->c;
@@ -1010,12 +1163,16 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
                     NC_TRY(launch_norm(st, nullptr, m->x, L.in_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
                 }
                 Probe pr(m, K_QKV);
-                NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_BIAS));
+                NC_TRY(model_i8(m, f, PRO_NONE, EPI_BIAS, L.mqkv, L.mqkv));
             }
         } else {
-            NC_TRY(launch_norm(st, m->normed, m->x, L.in_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
+            {
+                Probe pr(m, K_NORM);
+                NC_TRY(launch_norm(st, m->normed, m->x, L.in_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
+            }
             GemvF32Args a{};
             a.out = m->qkv; a.x = m->normed; a.w = L.fqkv; a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
+            Probe pr(m, K_QKV);
             NC_TRY(launch_f32(st, a, EPI_BIAS, false));
         }
         // RoPE, cache append, attention (and the quantization of its output)
@@ -1031,6 +1188,7 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
             Probe pr(m, K_ATTENTION);
             NC_TRY(launch_attention(st, at, rows, m->has_kv_map ? &m->kv_map : nullptr));
         } else {
+            Probe pr(m, K_ATTENTION);
             at.mode = 1;
             NC_TRY(launch_attention(st, at, rows, m->has_kv_map ? &m->kv_map : nullptr));
             at.mode = 2;
@@ -1044,14 +1202,19 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
             if (attn_quant) {
                 f.bsums_in = m->bsums;
                 Probe pr(m, K_O);
-                NC_TRY(launch_i8_fused(st, f, PRO_OFFSET, EPI_RESIDUAL));
+                NC_TRY(model_i8(m, f, PRO_OFFSET, EPI_RESIDUAL, L.mo, L.mo));
             } else {
-                NC_TRY(launch_quant(st, m->xq, m->ctx, m->xs, m->off, nullptr, rows, Hq));
-                NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_RESIDUAL));
+                {
+                    Probe pr(m, K_QUANT);
+                    NC_TRY(launch_quant(st, m->xq, m->ctx, m->xs, m->off, nullptr, rows, Hq));
+                }
+                Probe pr(m, K_O);
+                NC_TRY(model_i8(m, f, PRO_NONE, EPI_RESIDUAL, L.mo, L.mo));
             }
         } else {
             GemvF32Args a{};
             a.out = m->x; a.x = m->ctx; a.w = L.fo; a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
+            Probe pr(m, K_O);
             NC_TRY(launch_f32(st, a, EPI_RESIDUAL, false));
         }
         // post-attention norm -> gate/up with silu * up (quantized) -> down with the residual add
@@ -1070,20 +1233,27 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
                     NC_TRY(launch_norm(st, nullptr, m->x, L.post_norm, m->xq, m->xs, m->off, nullptr, nullptr, rows, H, c.eps));
                 }
                 Probe pr(m, K_GATE_UP);
-                NC_TRY(launch_i8_fused(st, f, PRO_NONE, EPI_SWIGLU_QUANT));
+                NC_TRY(model_i8(m, f, PRO_NONE, EPI_SWIGLU_QUANT, L.mg, L.mu));
             }
             FusedI8Args b{};
             b.g.out = m->x; b.g.xq = m->hq; b.g.xs = m->hxs; b.g.w = L.wd; b.g.scales = L.sd;
             b.g.residual = m->x; b.g.m = rows; b.g.n = H; b.g.k = I; b.bsums_in = m->bsums;
             Probe pr(m, K_DOWN);
-            NC_TRY(launch_i8_fused(st, b, PRO_OFFSET, EPI_RESIDUAL));
+            NC_TRY(model_i8(m, b, PRO_OFFSET, EPI_RESIDUAL, L.md, L.md));
         } else {
-            NC_TRY(launch_norm(st, m->normed, m->x, L.post_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
+            {
+                Probe pr(m, K_NORM);
+                NC_TRY(launch_norm(st, m->normed, m->x, L.post_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
+            }
             GemvF32Args a{};
             a.out = m->hbuf; a.x = m->normed; a.w = L.fg; a.w2 = L.fu; a.m = rows; a.n = I; a.k = H;
-            NC_TRY(launch_f32(st, a, EPI_SWIGLU, false));
+            {
+                Probe pr(m, K_GATE_UP);
+                NC_TRY(launch_f32(st, a, EPI_SWIGLU, false));
+            }
             GemvF32Args b{};
             b.out = m->x; b.x = m->hbuf; b.w = L.fd; b.residual = m->x; b.m = rows; b.n = H; b.k = I;
+            Probe pr(m, K_DOWN);
             NC_TRY(launch_f32(st, b, EPI_RESIDUAL, false));
         }
     }
@@ -1275,6 +1445,18 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
         m->has_kv_map = make_kv_map(&m->kv_map, m->kv, kv_rows, (int)d) == NC_OK;
     m->tc_head = tc_head;
     m->q8_head = q8_head;
+    // int8 weights as tcgen05 operand tiles for the batched projections (more than four rows)
+    if (c.quant) {
+        bool ok = true;
+        for (auto &L : m->layers) {
+            ok = ok && make_i8_map(&L.mqkv, L.wqkv, Nqkv, H, I8TC_ROWS) == NC_OK;
+            ok = ok && make_i8_map(&L.mo, L.wo, H, Hq, I8TC_ROWS) == NC_OK;
+            ok = ok && make_i8_map(&L.mg, L.wg, I, H, 64) == NC_OK;
+            ok = ok && make_i8_map(&L.mu, L.wu, I, H, 64) == NC_OK;
+            ok = ok && make_i8_map(&L.md, L.wd, H, I, I8TC_ROWS) == NC_OK;
+        }
+        m->tc_i8 = ok;
+    }
 
     // RoPE tables: angle = float(position) * inv_freq[i] (nanocompile/nn.py:78-94), evaluated with
     // the C library's cosf/sinf -- the functions the reference's generated C calls for them.

@@ -132,7 +132,7 @@ __device__ __forceinline__ void mk_prefetch_l2(const void *p, int64_t bytes) {
 // Reads words addr(0) .. addr(n-1) until each carries tag, handing (index, value) to store; up to
 // four words per thread are in flight together. False (and g_mk_fault set) when the wait gave up.
 template <typename A, typename F>
-__device__ __forceinline__ bool mk_poll(int n, uint32_t tag, A &&addr, F &&store) {
+__device__ __forceinline__ bool mk_poll(int n, uint32_t tag, A &&addr, F &&store, long long limit = NC_DRAIN_CYCLES) {
     const long long t0 = clock64();
     for (int base = threadIdx.x; base < n; base += 4 * MK_THREADS) {
         bool pend[4];
@@ -155,7 +155,7 @@ __device__ __forceinline__ bool mk_poll(int n, uint32_t tag, A &&addr, F &&store
                     }
                 }
             if (!any) break;
-            if (*(volatile unsigned *)&g_mk_fault || clock64() - t0 > (1LL << 31)) {
+            if (*(volatile unsigned *)&g_mk_fault || clock64() - t0 > limit) {
                 atomicExch(&g_mk_fault, 1u);
                 return false;
             }
@@ -618,6 +618,26 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             a.sync[1] = a.sync[1] + 1u;
             __threadfence();
         }
+    }
+}
+
+// The library's two bounded waits run out on purpose, with nothing in flight: kind 0 polls
+// tagged hand-over words (mk_poll) that carry no tag, kind 1 waits on an mbarrier expecting bytes
+// that no copy will bring.  Both give up after g_wait_cycles and set their fault word, which the
+// host reports as NC_ERR_KERNEL (nc_selftest_wait).
+__global__ void __launch_bounds__(MK_THREADS) wait_selftest_kernel(const unsigned long long *words, int n, int kind) {
+    __shared__ uint64_t bar;
+    const long long limit = g_wait_cycles;
+    if (kind == 0) {
+        const bool ok = mk_poll(n, 0x5eedu, [&](int i) { return words + i; }, [&](int, uint32_t) {}, limit);
+        if (!ok && threadIdx.x == 0) atomicExch(&g_mk_fault, 1u);
+        return;
+    }
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(&bar, 1024);                  // the arrival comes, the bytes never do
+        if (!mbar_wait_for(&bar, 0, limit)) atomicOr(&g_attention_fault, 1u);
     }
 }
 

@@ -65,7 +65,7 @@ _P64, _P32, _PF = ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32)
 
 # Fused-group entry points: int32_t f(void **p, const int64_t *s, void *stream).
 GROUP_ENTRY_POINTS = ("nc_gather_rows", "nc_rms_norm_quantize", "nc_quantize_blocks", "nc_matmul_i8_vnni",
-                      "nc_matmul_f32", "nc_lm_head_argmax",
+                      "nc_matmul_i8_tc", "nc_matmul_f32", "nc_lm_head_argmax",
                       "nc_lm_head_argmax_noalloc", "nc_attention", "nc_attention_cache", "nc_expf_exact",
                       "nc_lm_head_q8_prepare", "nc_lm_head_q8_argmax", "nc_quantize_int8_rows")
 
@@ -86,6 +86,8 @@ def library() -> ctypes.CDLL:
             fn.restype = _i32
         signatures = {
             "nc_device_faults": ([], _i32),
+            "nc_set_wait_limit": ([_i64], _i32),
+            "nc_selftest_wait": ([_i32], _i32),
             "nc_selfcheck_div127": ([_P64], _i32),
             "nc_lm_head_scratch_bytes": ([_i64, _i64], _i64),
             "nc_lm_head_q8_scratch_bytes": ([_i64, _i64], _i64),
@@ -141,6 +143,24 @@ def device_count() -> int:
     n = ctypes.c_int32(0)
     check(library().nc_device_count(ctypes.byref(n)))
     return n.value
+
+
+def set_wait_limit(cycles: int) -> None:
+    """Bound the abandonable device-side waits on the current device to ``cycles`` SM cycles
+    (``<= 0``: the default 2^31). A wait that runs out stops its kernel cleanly and is reported
+    by the next :func:`device_faults` or model call as a :class:`KernelError`."""
+    check(library().nc_set_wait_limit(int(cycles)))
+
+
+def device_faults() -> None:
+    """Raise :class:`KernelError` if a device-side wait gave up since the last check (and clear it)."""
+    check(library().nc_device_faults())
+
+
+def selftest_wait(kind: int) -> None:
+    """Make one of the bounded waits run out against a condition that never comes true (0: a
+    hand-over word, 1: a pipeline stage); raises the :class:`KernelError` it reports."""
+    check(library().nc_selftest_wait(int(kind)))
 
 
 def _p(a: np.ndarray | None, kind):

@@ -343,3 +343,73 @@ def test_quantize_int8_rows_is_the_references(cuda, packed):
         expected = (values.astype(np.int16) + 128).astype(np.uint8) if packed else values
         assert np.array_equal(dv.numpy(), expected)
         assert np.array_equal(bits(ds.numpy()), bits(scales))
+
+
+# -- the tensor-core int8 projection (tcgen05 kind::i8, block-diagonal activations) ---------------
+
+
+def call_tc(cuda, out, xq, xs, off, w, s, extra=None, extra2=None, bsums=None, q_out=None, xs_out=None,
+            bsums_out=None, sizes=()):
+    call(cuda, "nc_matmul_i8_tc", [out, xq, xs, off, w, s, extra, extra2, bsums, q_out, xs_out, bsums_out],
+         list(sizes))
+
+
+@pytest.mark.parametrize("k,n", [(896, 72), (4864, 24), (160, 40), (96, 24)])
+@pytest.mark.parametrize("tokens", [1, 3, 7])
+@pytest.mark.parametrize("per_item", [4, 8])
+def test_matmul_i8_tc_is_the_references_bitwise(cuda, k, n, tokens, per_item):
+    """The reference's own projection outputs (tests/golden/proj.npz) through the tensor cores,
+    including widths with 32-byte groups past the last whole 128-byte chunk (160, 96)."""
+    g = golden("proj")
+    tag = f"k{k}_n{n}_t{tokens}"
+    xq, xs, off = g[f"{tag}_xq"].reshape(tokens, k), g[f"{tag}_xs"].reshape(tokens, -1), g[f"{tag}_offset"].reshape(-1)
+    dq, dxs, doff = DeviceArray(cuda, xq), DeviceArray(cuda, xs), DeviceArray(cuda, off)
+    dw, ds = packed_int8(cuda, g[f"{tag}_q"]), DeviceArray(cuda, g[f"{tag}_scales"])
+    dout = DeviceArray(cuda, shape=(tokens, n), dtype=np.float32)
+    call_tc(cuda, dout, dq, dxs, doff, dw, ds, sizes=[tokens, n, k, 0, 0, per_item])
+    assert same_bits(dout.numpy(), g[f"{tag}_y"])
+
+
+@pytest.mark.parametrize("rows,n,k", [(64, 1152, 896), (64, 896, 4864), (5, 200, 96), (67, 4864, 896),
+                                      (16, 96, 160), (130, 256, 896)])
+@pytest.mark.parametrize("epi,pro", [(0, 0), (1, 0), (2, 0), (2, 2), (3, 0), (4, 0), (0, 2)])
+def test_matmul_i8_tc_epilogues_are_the_oracles(cuda, rows, n, k, epi, pro):
+    """Every prologue / epilogue the model runtime uses, against the oracle, bit for bit: offsets
+    given or formed from block sums; bias, residual, SiLU(gate) * up and its block quantization."""
+    rng = np.random.default_rng(rows * 7 + n + k + epi * 3 + pro)
+    x = activations(rng, rows, k)
+    xq, xs, off, sums = oracle.quantize_blocks(x)
+    w1, s1 = q.quantize_int8((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    w2, s2 = q.quantize_int8((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    w1[3] = 127                                         # extreme lanes: |Dp4| up to 4 * 255 * 127
+    y1 = oracle.matmul_i8_vnni(xq, xs, off, w1, s1)
+    y2 = oracle.matmul_i8_vnni(xq, xs, off, w2, s2)
+    bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    res = rng.standard_normal((rows, n)).astype(np.float32)
+    extra = extra2 = None
+    if epi == 0:
+        expect = y1
+    elif epi == 1:
+        expect, extra = y1 + bias, DeviceArray(cuda, bias)
+    elif epi == 2:
+        expect, extra = res + y1, DeviceArray(cuda, res)
+    else:
+        expect, extra, extra2 = oracle.swiglu(y1, y2), packed_int8(cuda, w2), DeviceArray(cuda, s2)
+    dq, dxs, doff, dsum = DeviceArray(cuda, xq), DeviceArray(cuda, xs), DeviceArray(cuda, off[:, 0]), DeviceArray(cuda, sums)
+    dw, ds = packed_int8(cuda, w1), DeviceArray(cuda, s1)
+    dout = DeviceArray(cuda, shape=(rows, n), dtype=np.float32, fill=0)
+    outs = [None, None, None]
+    if epi == 4:
+        outs = [DeviceArray(cuda, shape=(rows, n), dtype=np.int8), DeviceArray(cuda, shape=(rows, n // 32), dtype=np.float32),
+                DeviceArray(cuda, shape=(rows, n // 32), dtype=np.int32)]
+    for per_item in (4, 8):
+        call_tc(cuda, dout, dq, dxs, None if pro else doff, dw, ds, extra, extra2, dsum if pro else None, *outs,
+                sizes=[rows, n, k, epi, pro, per_item])
+        if epi == 4:
+            hq, hxs, _, hsums = oracle.quantize_blocks(expect)
+            assert np.array_equal(outs[0].numpy(), hq) and np.array_equal(outs[2].numpy(), hsums)
+            assert same_bits(outs[1].numpy(), hxs)
+        else:
+            assert same_bits(dout.numpy(), expect)
+        if epi == 2:
+            extra.upload(res)                           # the residual is read in place: restore it

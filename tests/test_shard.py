@@ -94,3 +94,40 @@ def test_two_gloo_ranks_decode_disjoint_shards_equal_to_one_process():
         assert tokens == expected                       # every rank gathers the whole batch, in order
         assert slowest == 3.0                           # the max over ranks, seen by every rank
     assert len({tuple(t) for t in expected}) > 1        # the sequences really differ
+
+
+def _killed_rank_main(rank: int, world: int, port: int, queue) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    import time
+
+    group = RankGroup("gloo", timeout_s=10)
+    if rank == 1:
+        os._exit(3)                                    # this worker dies between steps, holding nothing
+    started = time.monotonic()
+    try:
+        group.barrier()                                # the next host-side step of the survivors
+        queue.put((rank, None, time.monotonic() - started))
+    except Exception as e:                             # the failure is seen on the host, as an error
+        queue.put((rank, repr(e), time.monotonic() - started))
+
+
+def test_a_killed_worker_is_detected_by_the_survivors():
+    """A rank that exits between steps: the surviving rank's next host collective ends with an
+    error within the process group's timeout instead of waiting for ever."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_killed_rank_main, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        rank, err, seconds = queue.get(timeout=120)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert rank == 0 and err is not None and seconds < 60, (rank, err, seconds)
+    assert procs[1].exitcode == 3
