@@ -105,6 +105,13 @@ int32_t nc_matmul_i8_tc(void **p, const int64_t *s, void *stream);
  * s: rows, n, k, epilogue (as above) */
 int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream);
 
+/* matmul_i8 (+epilogue): int8 weights, float32 activations (nanocompile/lower.py:320-356
+ * int8_dots, times scales[n]: lower.py:398-412, fusion.py:677-711).  Widths multiples of 16.
+ * p: [0] out f32[rows, n]  [1] x f32[rows, k]  [2] w u8[n, k] (int8 + 128)  [3] scales f32[n]
+ *    [4] bias / residual / up weights (SwiGLU)  [5] up scales (SwiGLU)
+ * s: rows, n, k, epilogue (0 none, 1 bias, 2 residual, 3 silu(gate)*up) */
+int32_t nc_matmul_i8_f32(void **p, const int64_t *s, void *stream);
+
 /* The tied LM head (call 41) fused with greedy argmax (nanocompile/models/qwen2.py:364,
  * first maximum wins): logits = x @ embed.T in index order per row, then the argmax of
  * each row.  Scratch holds one (value, index) pair per (row, CTA): nc_lm_head_scratch_bytes.
@@ -206,7 +213,7 @@ typedef struct {
     int64_t vocab, hidden, inter, layers, heads, kv_heads, head_dim;
     float eps;            /* float32(rms_norm_eps) */
     float attn_scale;     /* float32(head_dim ** -0.5) */
-    int32_t quant;        /* 0 = float32 projections, 1 = int8-vnni */
+    int32_t quant;        /* 0 = float32 projections, 1 = int8-vnni, 2 = int8 weights + float32 activations */
     int32_t max_rows;     /* token rows per step (prompt length, or sequences in a batch) */
     int32_t slots;        /* KV-cache sequence slots */
     int32_t capacity;     /* KV positions per slot */

@@ -14,6 +14,7 @@
 #include "nc_decode_mk.cuh"
 #include "nc_gemm_i8.cuh"
 #include "nc_gemm_i8_tc.cuh"
+#include "nc_gemm_i8f.cuh"
 
 #include <climits>
 #include <cmath>
@@ -400,6 +401,26 @@ int32_t launch_f32(cudaStream_t st, const GemvF32Args &a, int epi, bool argmax) 
     return a.m == 1 ? launch_f32_tok<1>(st, a, epi, argmax) : launch_f32_tok<16>(st, a, epi, argmax);
 }
 
+// int8 weights with float32 activations (matmul_i8): 64 output rows per CTA, tokens in passes
+// of four (two with the SwiGLU pair of weights).
+template <int T, int EPI>
+int32_t launch_i8f_t(cudaStream_t st, const GemvI8fArgs &a) {
+    CUDA_TRY(launch_k(gemv_i8f_kernel<T, EPI>, (a.n + I8F_ROWS - 1) / I8F_ROWS, I8F_WARPS * 32, 0, st, a));
+    return check_launch("gemv_i8f_kernel");
+}
+
+int32_t launch_i8f(cudaStream_t st, const GemvI8fArgs &a, int epi) {
+    if (a.m <= 0 || a.n <= 0) return NC_OK;
+    if (a.k % 16 || a.k <= 0) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a multiple of 16", a.k);
+    switch (epi) {
+        case EPI_NONE: return a.m == 1 ? launch_i8f_t<1, EPI_NONE>(st, a) : launch_i8f_t<4, EPI_NONE>(st, a);
+        case EPI_BIAS: return a.m == 1 ? launch_i8f_t<1, EPI_BIAS>(st, a) : launch_i8f_t<4, EPI_BIAS>(st, a);
+        case EPI_RESIDUAL: return a.m == 1 ? launch_i8f_t<1, EPI_RESIDUAL>(st, a) : launch_i8f_t<4, EPI_RESIDUAL>(st, a);
+        case EPI_SWIGLU: return a.m == 1 ? launch_i8f_t<1, EPI_SWIGLU>(st, a) : launch_i8f_t<2, EPI_SWIGLU>(st, a);
+        default: return fail(NC_ERR_ARGUMENT, "unknown epilogue %d", epi);
+    }
+}
+
 size_t attention_smem(int heads_per_cta, int d, int cap) {
     switch (d) {
         case 16: return sizeof(float) * attention_smem_floats<16>(heads_per_cta, cap);
@@ -716,6 +737,25 @@ extern "C" int32_t nc_matmul_i8_tc(void **p, const int64_t *s, void *stream) {
     m2 = m1;
     if (two) NC_TRY(make_i8_map(&m2, a.w2, a.n, a.k, 64));
     return launch_i8_tc((cudaStream_t)stream, f, pro, epi, m1, m2, tokens);
+}
+
+extern "C" int32_t nc_matmul_i8_f32(void **p, const int64_t *s, void *stream) {
+    GemvI8fArgs a{};
+    a.out = (float *)p[0];
+    a.x = (const float *)p[1];
+    a.w = (const uint8_t *)p[2];
+    a.scales = (const float *)p[3];
+    a.m = (int)s[0];
+    a.n = (int)s[1];
+    a.k = (int)s[2];
+    const int epi = (int)s[3];
+    if (epi == EPI_BIAS) a.bias = (const float *)p[4];
+    if (epi == EPI_RESIDUAL) a.residual = (const float *)p[4];
+    if (epi == EPI_SWIGLU) {
+        a.w2 = (const uint8_t *)p[4];
+        a.scales2 = (const float *)p[5];
+    }
+    return launch_i8f((cudaStream_t)stream, a, epi);
 }
 
 extern "C" int32_t nc_matmul_f32(void **p, const int64_t *s, void *stream) {
@@ -1136,7 +1176,8 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
     cudaStream_t st = m->stream;
     const int H = (int)c.hidden, I = (int)c.inter, d = (int)c.head_dim;
     const int Hq = (int)(c.heads * d), Nqkv = (int)((c.heads + 2 * c.kv_heads) * d);
-    const bool q8 = c.quant != 0;
+    const bool q8 = c.quant == 1;             // int8-vnni: block-32 int8 activations
+    const bool i8f = c.quant == 2;            // int8 weights, float32 activations
     const bool norm_fused = rows <= PRO_NORM_ROWS && H <= 8 * CHUNK;
     const bool attn_quant = q8 && d % QBLOCK == 0;
 
@@ -1170,10 +1211,17 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
                 Probe pr(m, K_NORM);
                 NC_TRY(launch_norm(st, m->normed, m->x, L.in_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
             }
-            GemvF32Args a{};
-            a.out = m->qkv; a.x = m->normed; a.w = L.fqkv; a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
             Probe pr(m, K_QKV);
-            NC_TRY(launch_f32(st, a, EPI_BIAS, false));
+            if (i8f) {
+                GemvI8fArgs a{};
+                a.out = m->qkv; a.x = m->normed; a.w = L.wqkv; a.scales = L.sqkv; a.bias = L.bqkv;
+                a.m = rows; a.n = Nqkv; a.k = H;
+                NC_TRY(launch_i8f(st, a, EPI_BIAS));
+            } else {
+                GemvF32Args a{};
+                a.out = m->qkv; a.x = m->normed; a.w = L.fqkv; a.bias = L.bqkv; a.m = rows; a.n = Nqkv; a.k = H;
+                NC_TRY(launch_f32(st, a, EPI_BIAS, false));
+            }
         }
         // RoPE, cache append, attention (and the quantization of its output)
         AttnArgs at{};
@@ -1212,10 +1260,16 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
                 NC_TRY(model_i8(m, f, PRO_NONE, EPI_RESIDUAL, L.mo, L.mo));
             }
         } else {
-            GemvF32Args a{};
-            a.out = m->x; a.x = m->ctx; a.w = L.fo; a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
             Probe pr(m, K_O);
-            NC_TRY(launch_f32(st, a, EPI_RESIDUAL, false));
+            if (i8f) {
+                GemvI8fArgs a{};
+                a.out = m->x; a.x = m->ctx; a.w = L.wo; a.scales = L.so; a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
+                NC_TRY(launch_i8f(st, a, EPI_RESIDUAL));
+            } else {
+                GemvF32Args a{};
+                a.out = m->x; a.x = m->ctx; a.w = L.fo; a.residual = m->x; a.m = rows; a.n = H; a.k = Hq;
+                NC_TRY(launch_f32(st, a, EPI_RESIDUAL, false));
+            }
         }
         // post-attention norm -> gate/up with silu * up (quantized) -> down with the residual add
         if (q8) {
@@ -1245,16 +1299,30 @@ int32_t enqueue_layers(nc_model *m, int rows, int logit_rows, bool fused) {
                 Probe pr(m, K_NORM);
                 NC_TRY(launch_norm(st, m->normed, m->x, L.post_norm, nullptr, nullptr, nullptr, nullptr, nullptr, rows, H, c.eps));
             }
-            GemvF32Args a{};
-            a.out = m->hbuf; a.x = m->normed; a.w = L.fg; a.w2 = L.fu; a.m = rows; a.n = I; a.k = H;
-            {
-                Probe pr(m, K_GATE_UP);
-                NC_TRY(launch_f32(st, a, EPI_SWIGLU, false));
+            if (i8f) {
+                GemvI8fArgs a{};
+                a.out = m->hbuf; a.x = m->normed; a.w = L.wg; a.scales = L.sg; a.w2 = L.wu; a.scales2 = L.su;
+                a.m = rows; a.n = I; a.k = H;
+                {
+                    Probe pr(m, K_GATE_UP);
+                    NC_TRY(launch_i8f(st, a, EPI_SWIGLU));
+                }
+                GemvI8fArgs b{};
+                b.out = m->x; b.x = m->hbuf; b.w = L.wd; b.scales = L.sd; b.residual = m->x; b.m = rows; b.n = H; b.k = I;
+                Probe pr(m, K_DOWN);
+                NC_TRY(launch_i8f(st, b, EPI_RESIDUAL));
+            } else {
+                GemvF32Args a{};
+                a.out = m->hbuf; a.x = m->normed; a.w = L.fg; a.w2 = L.fu; a.m = rows; a.n = I; a.k = H;
+                {
+                    Probe pr(m, K_GATE_UP);
+                    NC_TRY(launch_f32(st, a, EPI_SWIGLU, false));
+                }
+                GemvF32Args b{};
+                b.out = m->x; b.x = m->hbuf; b.w = L.fd; b.residual = m->x; b.m = rows; b.n = H; b.k = I;
+                Probe pr(m, K_DOWN);
+                NC_TRY(launch_f32(st, b, EPI_RESIDUAL, false));
             }
-            GemvF32Args b{};
-            b.out = m->x; b.x = m->hbuf; b.w = L.fd; b.residual = m->x; b.m = rows; b.n = H; b.k = I;
-            Probe pr(m, K_DOWN);
-            NC_TRY(launch_f32(st, b, EPI_RESIDUAL, false));
         }
     }
     // final norm of the rows that need logits, then the tied LM head with the argmax
@@ -1270,7 +1338,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tok
     const nc_qwen2_config &c = m->c;
     cudaStream_t st = m->stream;
     const int H = (int)c.hidden;
-    if (c.quant && m->mk_ctas && rows <= MK_ROWS && fused && m->logit_identity && logit_rows == rows) {
+    if (c.quant == 1 && m->mk_ctas && rows <= MK_ROWS && fused && m->logit_identity && logit_rows == rows) {
         Probe pr(m, K_LAYERS);
         NC_TRY(launch_decode_mk(m, rows));
     } else {
@@ -1327,8 +1395,11 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
         return fail(NC_ERR_ARGUMENT, "unsupported model shape");
     if (c.hidden % 32 || c.inter % 32 || (c.heads * c.head_dim) % 32)
         return fail(NC_ERR_ARGUMENT, "widths must be whole 32-blocks");
-    if (c.quant < 0 || c.quant > 1)
-        return fail(NC_ERR_ARGUMENT, "projection mode %d: the library implements 0 (float32) and 1 (int8-vnni)", c.quant);
+    if (c.quant < 0 || c.quant > 2)
+        return fail(NC_ERR_ARGUMENT, "projection mode %d: the library implements 0 (float32), 1 (int8-vnni) and 2 "
+                                     "(int8 weights, float32 activations)", c.quant);
+    if (c.quant == 2 && (c.hidden % 16 || c.inter % 16 || (c.heads * c.head_dim) % 16))
+        return fail(NC_ERR_ARGUMENT, "int8 weights with float32 activations take widths that are multiples of 16");
     if (attention_smem((int)(c.heads / c.kv_heads), (int)c.head_dim, c.capacity) > 220 * 1024 &&
         attention_smem(1, (int)c.head_dim, c.capacity) > 220 * 1024)
         return fail(NC_ERR_ARGUMENT, "capacity %d exceeds the attention kernel's shared memory", c.capacity);
@@ -1446,7 +1517,7 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
     m->tc_head = tc_head;
     m->q8_head = q8_head;
     // int8 weights as tcgen05 operand tiles for the batched projections (more than four rows)
-    if (c.quant) {
+    if (c.quant == 1) {
         bool ok = true;
         for (auto &L : m->layers) {
             ok = ok && make_i8_map(&L.mqkv, L.wqkv, Nqkv, H, I8TC_ROWS) == NC_OK;
@@ -1511,7 +1582,7 @@ extern "C" int32_t nc_qwen2_create(const nc_qwen2_config *cfg, const float *inv_
             }
         }
     }
-    if (c.quant) {
+    if (c.quant == 1) {
         std::vector<MkLayer> ml((size_t)c.layers);
         for (int64_t l = 0; l < c.layers; ++l) {
             const auto &L = m->layers[l];

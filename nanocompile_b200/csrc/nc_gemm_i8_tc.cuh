@@ -131,7 +131,8 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(I8TC_EPI_WARPS * 32) : "memory"); }
 
 template <int T, int PRO, int EPI>
-__global__ void __maxnreg__(112)
+// 18 warps: the busiest sub-partition holds five, so 16384 / (5 * 32) caps a thread at 96 registers.
+__global__ void __launch_bounds__(I8TC_THREADS, 1)
 gemm_i8_tc_kernel(const FusedI8Args f, const __grid_constant__ CUtensorMap wmap,
                   const __grid_constant__ CUtensorMap wmap2) {
     using S = I8Tc<T>;

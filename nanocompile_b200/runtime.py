@@ -36,7 +36,7 @@ from nanocompile_b200.quantize import int8_name, scales_name
 LIBRARY_PATH = Path(__file__).resolve().parent / "libnc_cuda.so"
 
 NC_OK, NC_ERR_KERNEL, NC_ERR_ARGUMENT, NC_ERR_CUDA, NC_ERR_STATE = 0, 1, 2, 3, 4
-QUANT_CODES = {None: 0, "int8": 1}
+QUANT_CODES = {None: 0, "int8": 1, "f32": 2}
 
 
 class KernelError(RuntimeError):
@@ -65,7 +65,7 @@ _P64, _P32, _PF = ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32)
 
 # Fused-group entry points: int32_t f(void **p, const int64_t *s, void *stream).
 GROUP_ENTRY_POINTS = ("nc_gather_rows", "nc_rms_norm_quantize", "nc_quantize_blocks", "nc_matmul_i8_vnni",
-                      "nc_matmul_i8_tc", "nc_matmul_f32", "nc_lm_head_argmax",
+                      "nc_matmul_i8_tc", "nc_matmul_i8_f32", "nc_matmul_f32", "nc_lm_head_argmax",
                       "nc_lm_head_argmax_noalloc", "nc_attention", "nc_attention_cache", "nc_expf_exact",
                       "nc_lm_head_q8_prepare", "nc_lm_head_q8_argmax", "nc_quantize_int8_rows")
 
@@ -173,8 +173,8 @@ def _p(a: np.ndarray | None, kind):
 class DeviceModel:
     """One model resident on one GPU: weights, the KV cache of ``slots`` sequences, activations.
 
-    ``activations`` is ``None`` (float32 projections) or ``"int8"`` (int8-vnni: block-32 int8
-    activations). ``weights`` are by
+    ``activations`` is ``None`` (float32 projections), ``"int8"`` (int8-vnni: block-32 int8
+    activations) or ``"f32"`` (int8 weights with float32 activations). ``weights`` are by
     checkpoint name; int8 modes take ``W@int8`` / ``W@scales`` pairs, or a float32 ``W`` that is
     then quantized on the device (``nc_qwen2_upload_quantize``, the same bytes as the host
     scheme). ``rope_rates`` default to the shape's ``theta``.

@@ -164,6 +164,23 @@ static float vnni_dot(const int8_t *w, const int8_t *x, const float *xs, int64_t
     return combine32(acc);
 }
 
+/* lower.py:320-356 int8_dots for one (token, output row), int8 weights widened to float times
+ * float activations: accumulator j (0..31) takes element j of every 32-element block in order,
+ * acc = fmaf(float(w), x, acc); the 8-element groups past the last whole block go into
+ * accumulators 0..7, group after group; _combine; then each element past the last group is added
+ * as sum = sum + float(w) * x (a multiply and an add, two roundings). */
+static float i8f_dot(const int8_t *w, const float *x, int64_t k) {
+    float acc[32] = {0};
+    const int64_t wide = k / 32 * 32, groups = (k % 32) / 8, tail = wide + groups * 8;
+    for (int64_t k0 = 0; k0 < k / 32; ++k0)
+        for (int j = 0; j < 32; ++j) acc[j] = fmaf((float)w[k0 * 32 + j], x[k0 * 32 + j], acc[j]);
+    for (int64_t k1 = 0; k1 < groups; ++k1)
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf((float)w[wide + k1 * 8 + j], x[wide + k1 * 8 + j], acc[j]);
+    float sum = combine32(acc);
+    for (int64_t r = tail; r < k; ++r) sum = sum + (float)w[r] * x[r];
+    return sum;
+}
+
 /* lower.py:255-274 _matmul_kernel: acc = acc + a*b in index order, no FMA. */
 static inline float f32_dot(const float *x, const float *w, int64_t k) {
     float acc = 0.0f;
@@ -231,6 +248,29 @@ void orc_matmul_i8_vnni(const int8_t *xq, const float *xs, const float *offset, 
     for (int64_t m = 0; m < rows; ++m) {
         vnni_job job = {xq, q, xs, offset, scales, m, n, k, out, lanes};
         parallel_rows(n, vnni_rows, &job);
+    }
+}
+
+typedef struct {
+    const float *x;
+    const int8_t *q;
+    const float *scales;
+    int64_t m, n, k;
+    float *out;
+} i8f_job;
+
+static void i8f_rows(void *p, int64_t begin, int64_t end) {
+    const i8f_job *a = (const i8f_job *)p;
+    const float *x = a->x + a->m * a->k;
+    for (int64_t j = begin; j < end; ++j) a->out[a->m * a->n + j] = i8f_dot(a->q + j * a->k, x, a->k) * a->scales[j];
+}
+
+/* lower.py:398-412 / fusion.py:677-711 matmul_i8: out[m, n] = int8_dots(q[n], x[m]) * scales[n]. */
+void orc_matmul_i8(const float *x, const int8_t *q, const float *scales, int64_t rows, int64_t n, int64_t k,
+                   float *out) {
+    for (int64_t m = 0; m < rows; ++m) {
+        i8f_job job = {x, q, scales, m, n, k, out};
+        parallel_rows(n, i8f_rows, &job);
     }
 }
 
@@ -332,8 +372,12 @@ typedef struct {
 
 static void project(const orc_config *c, const acts *a, const float *w32, const int8_t *w8,
                     const float *scales, int64_t rows, int64_t n, int64_t k, float *out) {
-    if (c->quant) {
+    if (c->quant == 1) {
         orc_matmul_i8_vnni(a->xq, a->xs, a->offset, w8, scales, rows, n, k, out, NULL);
+        return;
+    }
+    if (c->quant == 2) {
+        orc_matmul_i8(a->x, w8, scales, rows, n, k, out);
         return;
     }
     for (int64_t m = 0; m < rows; ++m) {
@@ -349,7 +393,7 @@ typedef struct {
 
 static acts make_acts(const orc_config *c, const float *x, int64_t rows, int64_t k, qbuf *q) {
     acts a = {x, NULL, NULL, NULL};
-    if (c->quant) {
+    if (c->quant == 1) {
         orc_quantize_blocks(x, rows, k, q->xq, q->xs, q->offset, NULL);
         a.xq = q->xq;
         a.xs = q->xs;

@@ -21,7 +21,7 @@ typedef struct {
     int64_t vocab, hidden, inter, layers, heads, kv_heads, head_dim;
     float eps;          /* float32(rms_norm_eps) */
     float attn_scale;   /* float32(head_dim ** -0.5) */
-    int32_t quant;      /* 0 = float32 projections, 1 = int8-vnni (block 32) */
+    int32_t quant;      /* 0 = float32 projections, 1 = int8-vnni (block 32), 2 = int8 weights, float32 activations */
     int32_t threads;    /* worker threads for row-parallel loops; <= 0 keeps the last setting */
 } orc_config;
 
@@ -30,8 +30,8 @@ typedef struct {
     const float *in_norm, *post_norm;                 /* [H] */
     const float *bq, *bk, *bv;                        /* [heads*d], [kv*d], [kv*d] */
     const float *wq, *wk, *wv, *wo, *wg, *wu, *wd;    /* float32 weights (quant == 0) */
-    const int8_t *qq, *qk, *qv, *qo, *qg, *qu, *qd;   /* int8 weights (quant == 1) */
-    const float *sq, *sk, *sv, *so, *sg, *su, *sd;    /* per-row scales (quant == 1) */
+    const int8_t *qq, *qk, *qv, *qo, *qg, *qu, *qd;   /* int8 weights (quant == 1, 2) */
+    const float *sq, *sk, *sv, *so, *sg, *su, *sd;    /* per-row scales (quant == 1, 2) */
 } orc_layer;
 
 /* One step of the model: the reference graph `build_qwen2(config, last_only)`
@@ -50,6 +50,11 @@ int32_t orc_qwen2_step(const orc_config *c, const float *embed, const float *fin
  * block_sums may be NULL. */
 void orc_quantize_blocks(const float *x, int64_t rows, int64_t k, int8_t *xq, float *xs,
                          float *offset, int32_t *block_sums);
+
+/* matmul_i8: out[m, n] = int8_dots(q[n], x[m]) * scales[n], float32 activations
+ * (lower.py:320-356, lower.py:398-412). */
+void orc_matmul_i8(const float *x, const int8_t *q, const float *scales, int64_t rows, int64_t n, int64_t k,
+                   float *out);
 
 /* matmul_i8_vnni: out[m, n] for m < rows (lower.py:363-397 + fusion.py:677-711).
  * lanes (nullable): the int32 Dp4 value of every (row m, output n, 4-byte lane),

@@ -63,6 +63,7 @@ def lib() -> ctypes.CDLL:
         L.orc_quantize_blocks.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, _i8p, _f32p, _f32p, _i32p]
         L.orc_matmul_i8_vnni.argtypes = [_i8p, _f32p, _f32p, _i8p, _f32p, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int64, _f32p, _i32p]
+        L.orc_matmul_i8.argtypes = [_f32p, _i8p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _f32p]
         L.orc_rms_norm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _f32p]
         L.orc_lm_head.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int64, _f32p]
         L.orc_argmax.restype = ctypes.c_int64
@@ -111,6 +112,17 @@ def matmul_i8_vnni(xq, xs, offset, q, scales, lanes: bool = False):
                              _ptr(np.ascontiguousarray(scales, np.float32)), rows, n, k, _ptr(out),
                              _ptr(lane_arr, _i32p))
     return (out, lane_arr) if lanes else out
+
+
+def matmul_i8(x, q, scales):
+    """``out [rows, n]`` of int8 weights and float32 activations (``lower.py:320-356``)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, k = x.shape
+    n = q.shape[0]
+    out = np.empty((rows, n), np.float32)
+    lib().orc_matmul_i8(_ptr(x), _ptr(np.ascontiguousarray(q, np.int8), _i8p), _ptr(np.ascontiguousarray(scales, np.float32)),
+                        rows, n, k, _ptr(out))
+    return out
 
 
 def rms_norm(x, w, eps: float, residual=None):
@@ -193,14 +205,14 @@ class OracleModel:
 
     def __init__(self, shape, weights: Mapping[str, np.ndarray], activations: str | None, threads: int = 0,
                  inv_freq: np.ndarray | None = None):
-        if activations not in (None, "int8"):
-            raise ValueError("the oracle implements float32 and int8-vnni projections")
+        if activations not in (None, "int8", "f32"):
+            raise ValueError("the oracle implements float32, int8-vnni and int8 (float activations) projections")
         c = shape
         self.shape = c
-        self.quant = activations == "int8"
+        self.quant = {None: 0, "int8": 1, "f32": 2}[activations]
         self._keep: list[np.ndarray] = []
         self.cfg = OrcConfig(c.vocab, c.hidden, c.inter, c.layers, c.heads, c.kv_heads, c.head_dim,
-                             np.float32(c.eps), c.attention_scale, 1 if self.quant else 0, threads)
+                             np.float32(c.eps), c.attention_scale, self.quant, threads)
 
         def arr(name: str, dtype=np.float32) -> np.ndarray:
             a = np.ascontiguousarray(weights[name], dtype)

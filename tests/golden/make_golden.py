@@ -1,6 +1,6 @@
 """Golden vectors from the reference itself (run in a container that has nanocompile).
 
-    python tests/golden/make_golden.py [--reference PATH] [tiny proj quant 05b fp32 batch prefill]
+    python tests/golden/make_golden.py [--reference PATH] [tiny proj quant fp32 batch prefill int8 int8_05b]
 
 Every fixture here is an output of nanocompile's own ``CBackend`` (its generated C,
 compiled by gcc) -- never of this repository's code -- on seeded synthetic inputs:
@@ -136,6 +136,46 @@ def make_proj() -> None:
     np.savez_compressed(HERE / "proj.npz", **out)
 
 
+WIDTHS_I8 = [(896, 72), (4864, 24), (160, 40), (96, 24), (136, 16), (100, 8)]   # + 8-groups and a short tail
+
+
+def make_int8_f32() -> None:
+    """The int8 mode with float32 activations (matmul_i8, nanocompile/lower.py:320-356): one
+    projection per width (widths with 8-element groups and a tail past them included), tokens
+    1/3/7; and configuration 1's greedy run with quantization="int8"."""
+    from nanocompile import dtypes, quantize
+    from nanocompile.frontend import GraphBuilder
+    from nanocompile.models.qwen2 import Qwen2
+    from nanocompile.nn import linear
+    from nanocompile.runtime import CBackend, CompiledGraph
+
+    out: dict[str, np.ndarray] = {}
+    for k, n in WIDTHS_I8:
+        b = GraphBuilder("projection_i8")
+        x = b.input("x", dtypes.f32, (b.symbol("seq"), k))
+        graph = quantize.quantize(b.build({"y": linear(x, b.weight("w", (n, k)))}), "f32")
+        compiled = CompiledGraph(graph)
+        for tokens in TOKENS:
+            rng = np.random.default_rng(3 * k + tokens)
+            w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+            xin = (rng.standard_normal((tokens, k)) * 2).astype(np.float32)
+            weights = quantize.quantized_weights(graph, {"w": w})
+            tag = f"k{k}_n{n}_t{tokens}"
+            out[f"{tag}_x"] = xin
+            out[f"{tag}_q"] = weights["w@int8"]
+            out[f"{tag}_scales"] = weights["w@scales"]
+            out[f"{tag}_y"] = compiled({"x": xin}, weights)["y"]
+    w = synthetic_weights(TINY, seed=0)
+    prompt = synthetic_prompt(TINY.vocab, 8)
+    model = Qwen2(ref_config(TINY), w, run=CBackend(), quantization="int8")
+    tokens, logits = run_greedy(model, prompt, 16, model.new_cache(4))
+    out["tiny_prompt"] = np.array(prompt, np.int64)
+    out["tiny_tokens"] = np.array(tokens, np.int64)
+    out["tiny_logits"] = logits
+    out["tiny_full_logits"] = model.forward(prompt)
+    np.savez_compressed(HERE / "int8_f32.npz", **out)
+
+
 def make_05b(quant: str | None, steps: int, name: str) -> None:
     """Configs 2/3: the 0.5B model, 32-token prompt, greedy decode."""
     from nanocompile.models.qwen2 import Qwen2
@@ -222,6 +262,7 @@ def main() -> int:
         started = time.perf_counter()
         {"tiny": make_tiny, "proj": make_proj,
          "quant": lambda: make_05b("int8-vnni", 993, "qwen05b_vnni"),
+         "int8": make_int8_f32, "int8_05b": lambda: make_05b("int8", 48, "qwen05b_int8"),
          "fp32": lambda: make_05b(None, 128, "qwen05b_fp32"),
          "prefill": make_prefill,
          "batch": lambda: make_batch(64, 64)}[part]()

@@ -400,8 +400,12 @@ def test_matmul_i8_tc_epilogues_are_the_oracles(cuda, rows, n, k, epi, pro):
     dout = DeviceArray(cuda, shape=(rows, n), dtype=np.float32, fill=0)
     outs = [None, None, None]
     if epi == 4:
-        outs = [DeviceArray(cuda, shape=(rows, n), dtype=np.int8), DeviceArray(cuda, shape=(rows, n // 32), dtype=np.float32),
-                DeviceArray(cuda, shape=(rows, n // 32), dtype=np.int32)]
+        outs = [DeviceArray(cuda, shape=(rows, n), dtype=np.int8), DeviceArray(cuda, shape=(rows, max(n // 32, 1)), dtype=np.float32),
+                DeviceArray(cuda, shape=(rows, max(n // 32, 1)), dtype=np.int32)]
+    if epi == 4 and n % 32:                             # quantized outputs are whole 32-blocks
+        with pytest.raises(cuda.InterpreterError, match="quantized output width"):
+            call_tc(cuda, dout, dq, dxs, doff, dw, ds, extra, extra2, None, *outs, sizes=[rows, n, k, epi, pro, 4])
+        return
     for per_item in (4, 8):
         call_tc(cuda, dout, dq, dxs, None if pro else doff, dw, ds, extra, extra2, dsum if pro else None, *outs,
                 sizes=[rows, n, k, epi, pro, per_item])
@@ -413,3 +417,41 @@ def test_matmul_i8_tc_epilogues_are_the_oracles(cuda, rows, n, k, epi, pro):
             assert same_bits(dout.numpy(), expect)
         if epi == 2:
             extra.upload(res)                           # the residual is read in place: restore it
+
+
+# -- int8 weights with float32 activations (matmul_i8) ---------------------------------------------
+
+
+@pytest.mark.parametrize("k,n", [(896, 72), (4864, 24), (160, 40), (96, 24)])
+@pytest.mark.parametrize("tokens", [1, 3, 7])
+def test_matmul_i8_f32_is_the_references_bitwise(cuda, k, n, tokens):
+    """The reference's own matmul_i8 outputs (tests/golden/int8_f32.npz, its generated C)."""
+    g = golden("int8_f32")
+    tag = f"k{k}_n{n}_t{tokens}"
+    dout = DeviceArray(cuda, shape=(tokens, n), dtype=np.float32)
+    call(cuda, "nc_matmul_i8_f32", [dout, DeviceArray(cuda, g[f"{tag}_x"]), packed_int8(cuda, g[f"{tag}_q"]),
+                                    DeviceArray(cuda, g[f"{tag}_scales"]), None, None], [tokens, n, k, 0])
+    assert same_bits(dout.numpy(), g[f"{tag}_y"])
+
+
+@pytest.mark.parametrize("rows,n,k", [(1, 1152, 896), (3, 896, 4864), (5, 200, 144), (2, 4864, 896), (9, 64, 48)])
+@pytest.mark.parametrize("epi", [1, 2, 3])
+def test_matmul_i8_f32_epilogues_are_the_oracles(cuda, rows, n, k, epi):
+    """Bias, residual and SiLU(gate) * up, and widths with 8-element groups past the last block."""
+    rng = np.random.default_rng(rows + n + k + epi)
+    x = activations(rng, rows, k)
+    w1, s1 = q.quantize_int8((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    w2, s2 = q.quantize_int8((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    y1, y2 = oracle.matmul_i8(x, w1, s1), oracle.matmul_i8(x, w2, s2)
+    bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    res = rng.standard_normal((rows, n)).astype(np.float32)
+    if epi == 1:
+        expect, extra, extra2 = y1 + bias, DeviceArray(cuda, bias), None
+    elif epi == 2:
+        expect, extra, extra2 = res + y1, DeviceArray(cuda, res), None
+    else:
+        expect, extra, extra2 = oracle.swiglu(y1, y2), packed_int8(cuda, w2), DeviceArray(cuda, s2)
+    dout = DeviceArray(cuda, shape=(rows, n), dtype=np.float32)
+    call(cuda, "nc_matmul_i8_f32", [dout, DeviceArray(cuda, x), packed_int8(cuda, w1), DeviceArray(cuda, s1), extra,
+                                    extra2], [rows, n, k, epi])
+    assert same_bits(dout.numpy(), expect)

@@ -235,3 +235,29 @@ def test_05b_fp32_greedy_is_the_references(reference, cuda, qwen05b_weights):
     lg = model.forward(list(g["prompt"]), cache=cache, last_only=True)[0]
     assert np.array_equal(bits(lg), bits(g["first_logits"][0]))
     assert greedy(model, list(g["prompt"]), 8) == list(g["tokens"][:8])
+
+
+def test_tiny_int8_f32_through_the_reference_api(reference, cuda):
+    """quantization="int8" (int8 weights, float32 activations): the reference's greedy and full
+    logits over the CUDA runner, against its CBackend's."""
+    from nanocompile.models.qwen2 import greedy
+
+    g = golden("int8_f32")
+    model = ref_model(reference, cuda, TINY, synthetic_weights(TINY, seed=0), "int8", capacity=64, slots=2, max_rows=16)
+    prompt = list(g["tiny_prompt"])
+    assert greedy(model, prompt, 16) == list(g["tiny_tokens"])
+    assert cuda.device_greedy(model, prompt, 16) == list(g["tiny_tokens"])
+    assert np.array_equal(bits(model.forward(prompt)), bits(g["tiny_full_logits"]))
+
+
+def test_05b_int8_f32_greedy_is_the_references(reference, cuda, qwen05b_weights):
+    """The 0.5B model with quantization="int8": 48 greedy tokens and every step's logits (SHA-1)."""
+    g = golden("qwen05b_int8")
+    model = ref_model(reference, cuda, QWEN2_0_5B, qwen05b_weights, "int8", capacity=128, slots=2, max_rows=64)
+    assert cuda.device_greedy(model, list(g["prompt"]), 48) == list(g["tokens"])
+    cache = model.new_cache(128)
+    pending = list(g["prompt"])
+    for step in range(8):
+        lg = model.forward(pending, cache=cache, last_only=True)[0]
+        assert np.array_equal(sha1(lg), g["sha1"][step]), step
+        pending = [int(g["tokens"][step])]

@@ -116,3 +116,40 @@ def test_oracle_05b_int8_vnni_first_steps_are_the_references(qwen05b_vnni_weight
     assert tokens == list(g["tokens"][:2])
     assert np.array_equal(bits(logits), bits(g["first_logits"]))
     assert all(np.array_equal(sha1(logits[i]), g["sha1"][i]) for i in range(2))
+
+
+# -- int8 weights with float32 activations (matmul_i8, nanocompile/lower.py:320-356) ----------------
+
+WIDTHS_I8 = [(896, 72), (4864, 24), (160, 40), (96, 24), (136, 16), (100, 8)]
+
+
+@pytest.mark.parametrize("k,n", WIDTHS_I8)
+@pytest.mark.parametrize("tokens", [1, 3, 7])
+def test_oracle_int8_f32_projection_is_the_references_bitwise(k, n, tokens):
+    g = golden("int8_f32")
+    tag = f"k{k}_n{n}_t{tokens}"
+    rng = np.random.default_rng(3 * k + tokens)          # the fixture's weight, regenerated
+    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+    values, scales = q.quantize_int8(w)
+    assert np.array_equal(values, g[f"{tag}_q"]) and np.array_equal(bits(scales), bits(g[f"{tag}_scales"]))
+    assert np.array_equal(bits(oracle.matmul_i8(g[f"{tag}_x"], values, scales)), bits(g[f"{tag}_y"]))
+
+
+def test_oracle_tiny_int8_f32_greedy_is_the_references_bitwise():
+    g = golden("int8_f32")
+    model = oracle.OracleModel(TINY, q.int8_projection_weights(synthetic_weights(TINY, seed=0), TINY), "f32")
+    tokens, logits = model.greedy(list(g["tiny_prompt"]), 16, return_logits=True)
+    assert tokens == list(g["tiny_tokens"]) and np.array_equal(bits(logits), bits(g["tiny_logits"]))
+    zeros = np.zeros((TINY.layers, TINY.kv_heads, 0, TINY.head_dim), np.float32)
+    full, _, _ = model.step(list(g["tiny_prompt"]), zeros, zeros, last_only=False)
+    assert np.array_equal(bits(full), bits(g["tiny_full_logits"]))
+
+
+@pytest.mark.slow
+def test_oracle_05b_int8_f32_first_steps_are_the_references(qwen05b_vnni_weights):
+    g = golden("qwen05b_int8")
+    model = oracle.OracleModel(QWEN2_0_5B, qwen05b_vnni_weights, "f32", threads=8)
+    tokens, logits = model.greedy(list(g["prompt"]), 3, return_logits=True)
+    assert tokens == list(g["tokens"][:3])
+    assert np.array_equal(bits(logits[:2]), bits(g["first_logits"]))
+    assert all(np.array_equal(sha1(logits[i]), g["sha1"][i]) for i in range(3))
