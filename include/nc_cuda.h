@@ -95,7 +95,7 @@ int32_t nc_matmul_i8_vnni(void **p, const int64_t *s, void *stream);
  *    [8] block sums i32[m, k/32] (prologue 2: the offset is 128 * in-order sum of sum_b * xs_b)
  *    [9] xq out i8[m, n]  [10] xs out f32[m, n/32]  [11] block sums out i32[m, n/32] (epilogue 4)
  * s: m, n, k, epilogue (0 none, 1 bias, 2 residual, 3 silu(gate)*up, 4 the same block-quantized),
- *    prologue (0 given offsets, 2 from block sums), tokens per work item (0 by shape, 4, 8) */
+ *    prologue (0 given offsets, 2 from block sums), tokens per work item (0 or 4) */
 int32_t nc_matmul_i8_tc(void **p, const int64_t *s, void *stream);
 
 /* float32 matmul with epilogue (nanocompile/lower.py:255-274, fusion.py:652-675):
@@ -275,6 +275,13 @@ int32_t nc_qwen2_decode_timed(nc_model *model, int32_t batch, const int32_t *slo
  * 4 gate/up projection, 5 down projection, 6 rms_norm row kernel, 7 block quantization,
  * 8 LM head + argmax, 9 the persistent decode kernel's layers). */
 #define NC_KINDS 10
+
+/* Timing hook for benchmarks: `iters` eager steps of the same `rows` rows (ids / slot / pos as
+ * nc_qwen2_step; the rows' KV positions are rewritten with the same values each time), each
+ * producing only the last row's argmax; *ms gets the average milliseconds per step, CUDA events
+ * on the model's stream.  Configuration 4 (a 512-token prefill) is timed with it. */
+int32_t nc_qwen2_step_timed(nc_model *model, int32_t rows, const int64_t *ids, const int32_t *slot,
+                            const int32_t *pos, int32_t iters, float *ms);
 /* Kernel-time probe around nc_qwen2_step calls: on != 0 starts bracketing every launch of the
  * following steps with CUDA events; on == 0 stops, synchronizes and sums milliseconds and
  * launches per fused-group kind (as nc_qwen2_profile) into the arrays (nullable). */

@@ -146,12 +146,14 @@ bool tc_head_enabled() {
     return on;
 }
 
+// The tensor-core (tcgen05 kind::i8) batched projection is opt-in (NC_TC_I8=1): measured on a
+// B200 it is slower than the dp4a kernel at 64 and 512 rows (gate/up 63 vs 41 us at 64 rows; 432
+// vs 288 us at 512): one MMA per 32-byte group of N = 32 (token, lane) columns costs ~240 cycles
+// to issue and complete, and only 1/8 of each block-diagonal operand is useful.
+// Read at every launch decision (a captured decode graph keeps the choice it was captured with).
 bool tc_i8_enabled() {
-    static const bool on = [] {
-        const char *v = std::getenv("NC_TC_I8");
-        return !(v && v[0] == '0');
-    }();
-    return on;
+    const char *v = std::getenv("NC_TC_I8");
+    return v && v[0] == '1';
 }
 
 int sm_count() {
@@ -494,7 +496,7 @@ int32_t make_i8_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t k, in
 }
 
 // The tensor-core int8 projection (more than four rows): persistent CTAs over items of 128 weight
-// rows x T tokens; T = 8 when that still gives every SM two items, else 4.
+// rows x 4 tokens.
 template <int T, int PRO, int EPI>
 int32_t launch_i8_tc_t(cudaStream_t st, const FusedI8Args &f, const CUtensorMap &m1, const CUtensorMap &m2) {
     constexpr bool TWO = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_QUANT;
@@ -520,21 +522,17 @@ int32_t launch_i8_tc_epi(cudaStream_t st, const FusedI8Args &f, int epi, const C
     }
 }
 
-// tokens: 0 chooses by shape, else 4 or 8.
+// tokens: 0 or 4 (items of four tokens, one per epilogue warp of a TMEM sub-partition).
 int32_t launch_i8_tc(cudaStream_t st, const FusedI8Args &f, int pro, int epi, const CUtensorMap &m1,
                      const CUtensorMap &m2, int tokens = 0) {
     const GemvI8Args &a = f.g;
     if (a.m <= 0 || a.n <= 0) return NC_OK;
     if (a.k % QBLOCK) return fail(NC_ERR_ARGUMENT, "int8 width %d is not a whole number of 32-blocks", a.k);
     if (epi == EPI_SWIGLU_QUANT && a.n % QBLOCK) return fail(NC_ERR_ARGUMENT, "quantized output width %d", a.n);
-    const bool two = epi == EPI_SWIGLU || epi == EPI_SWIGLU_QUANT;
-    const int row_tiles = two ? (a.n + 63) / 64 : (a.n + I8TC_ROWS - 1) / I8TC_ROWS;
-    if (tokens == 0) tokens = row_tiles * ((a.m + 7) / 8) >= 2 * sm_count() ? 8 : 4;
-    if (tokens != 4 && tokens != 8) return fail(NC_ERR_ARGUMENT, "tokens per item %d: 4 or 8", tokens);
+    if (tokens != 0 && tokens != 4) return fail(NC_ERR_ARGUMENT, "tokens per item %d: 4", tokens);
+    if (4 * (a.k / QBLOCK) > 2 * I8TC_EPI_WARPS * 32)
+        return fail(NC_ERR_ARGUMENT, "int8 width %d too wide for the tensor-core projection", a.k);
     if (pro != PRO_NONE && pro != PRO_OFFSET) return fail(NC_ERR_ARGUMENT, "prologue %d is not a batched one", pro);
-    if (tokens == 8)
-        return pro == PRO_NONE ? launch_i8_tc_epi<8, PRO_NONE>(st, f, epi, m1, m2)
-                               : launch_i8_tc_epi<8, PRO_OFFSET>(st, f, epi, m1, m2);
     return pro == PRO_NONE ? launch_i8_tc_epi<4, PRO_NONE>(st, f, epi, m1, m2)
                            : launch_i8_tc_epi<4, PRO_OFFSET>(st, f, epi, m1, m2);
 }
@@ -1163,7 +1161,7 @@ int32_t launch_lm_head_q8(nc_model *m, int rows) {
 }
 
 // An int8 projection of the step: more than four rows take the tensor cores when the model has
-// its weights' tensor maps (NC_TC_I8=0 keeps them on the dp4a kernels).
+// its weights' tensor maps and NC_TC_I8=1; otherwise the batched dp4a kernel.
 int32_t model_i8(nc_model *m, const FusedI8Args &f, int pro, int epi, const CUtensorMap &m1, const CUtensorMap &m2) {
     if (m->tc_i8 && tc_i8_enabled() && f.g.m > PRO_NORM_ROWS && pro != PRO_NORM)
         return launch_i8_tc(m->stream, f, pro, epi, m1, m2);
@@ -1955,6 +1953,41 @@ extern "C" int32_t nc_qwen2_upload_quantize(nc_model *m, const char *name, const
     m->uploaded.insert(base + "@int8");
     m->uploaded.insert(base + "@scales");
     return NC_OK;
+}
+
+// Timing hook for benchmarks: `iters` eager steps over the same rows (a prompt of `rows` tokens of
+// slot[0] from position pos[0]: its KV positions are rewritten with the same values each time),
+// only the last row's token (argmax) produced; CUDA events on the model's stream around all of them.
+extern "C" int32_t nc_qwen2_step_timed(nc_model *m, int32_t rows, const int64_t *ids, const int32_t *slot,
+                                       const int32_t *pos, int32_t iters, float *ms) {
+    if (!m || !ids || !slot || !pos || !ms) return fail(NC_ERR_ARGUMENT, "null argument");
+    NC_TRY(check_ready(m));
+    bool fused;
+    NC_TRY(check_rows(m, rows, slot, pos, &fused));
+    if (iters <= 0) return fail(NC_ERR_ARGUMENT, "iters %d", iters);
+    CUDA_TRY(cudaSetDevice(m->dev));
+    cudaStream_t st = m->stream;
+    const int32_t last = rows - 1;
+    CUDA_TRY(cudaMemcpyAsync(m->ids, ids, rows * 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->slot, slot, rows * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->pos, pos, rows * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->logit_row, &last, 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemsetAsync(m->err, 0xff, sizeof(unsigned long long), st));
+    m->logit_identity = rows == 1;
+    cudaEvent_t a, b;
+    CUDA_TRY(cudaEventCreate(&a));
+    CUDA_TRY(cudaEventCreate(&b));
+    CUDA_TRY(cudaEventRecord(a, st));
+    int32_t status = NC_OK;
+    for (int i = 0; i < iters && status == NC_OK; ++i) status = enqueue_step(m, rows, 1, fused, true);
+    CUDA_TRY(cudaEventRecord(b, st));
+    CUDA_TRY(cudaEventSynchronize(b));
+    CUDA_TRY(cudaEventElapsedTime(ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    NC_TRY(status);
+    *ms /= (float)iters;
+    return model_faults(m);
 }
 
 // ---- the LM head + argmax without any allocation ---------------------------------------------

@@ -14,17 +14,19 @@
 // accumulate leaves 1.5 * 2^23 + Dp4 as a float and one subtraction recovers Dp4 exactly), the
 // in-order fmaf chains, _combine and the epilogue.
 //
-// Roles (18 warps, one CTA per SM, persistent over work items = 128 weight rows x T tokens):
+// Roles (18 warps, one CTA per SM, persistent over work items = 128 weight rows x 4 tokens):
 //  - warp 16 (producer): per 128-byte chunk one TMA tensor copy of the weight tile (128-byte
 //    swizzle, K-major) and the block-diagonal activation tile: the stages are zeroed once, and
 //    each chunk only its T * 32 nonzero words are stored, from quantized activations loaded
 //    four chunks ahead into registers; a proxy fence, then one arrive on the stage's mbarrier;
 //  - warp 17 lane 0 (MMA issuer): per chunk one MMA per group into a TMEM slot, tcgen05.commit to
 //    the stage's and the slot's barriers;
-//  - warps 0-15 (epilogue): warp w reads TMEM lanes 32 (w % 4).. (its rows) and the columns of
-//    tokens (w / 4) * T/4.. : 2 (T = 8) or 1 (T = 4) tokens x 8 lanes per group; it re-arms the
-//    slot with the 1.5 * 2^23 bits, releases it, and runs the chains; after the item's last chunk
-//    _combine, (sum - offset) * scale and the epilogue (bias / residual / SwiGLU + quantize).
+//  - warps 0-15 (epilogue): warp w reads TMEM lanes 32 (w % 4).. (its rows) and the 8 columns
+//    (lanes) of token w / 4 of every group of a chunk, all four groups before one wait; it re-arms
+//    the slot with the 1.5 * 2^23 bits, releases it, and runs the chains two accumulators at a time
+//    (packed float2 add and fma, each lane rounded as the scalar operation); after the item's last
+//    chunk _combine, (sum - offset) * scale and the epilogue (bias / residual / SwiGLU + quantize).
+//    The next item's block scales are loaded into registers while the current one runs.
 // Gate/up items hold 64 gate rows and the 64 up rows of the same outputs (TMEM lanes 0-63 and
 // 64-127), so SiLU(gate) * up and its block quantization stay in the CTA.  Every wait is bounded
 // (g_wait_cycles); a wait that gives up records a fault in g_attention_fault, stops the pipeline,
@@ -48,7 +50,7 @@ constexpr float I8TC_MAGIC_F = 12582912.0f;
 
 template <int T>
 struct I8Tc {
-    static_assert(T == 4 || T == 8, "tokens per item");
+    static_assert(T == 4, "tokens per item: one per epilogue warp of a sub-partition");
     static constexpr int N = 8 * T;                    // MMA N: (token, lane) columns of one group
     static constexpr int B_BYTES = N * CHUNK;          // one chunk of block-diagonal activations
     static constexpr int SLOT_COLS = 4 * N;            // one chunk's four groups
@@ -283,7 +285,8 @@ gemm_i8_tc_kernel(const FusedI8Args f, const __grid_constant__ CUtensorMap wmap,
         }
     } else {
         // ---- epilogue ----
-        const int sp = warp & 3, wq = warp >> 2;
+        static_assert(S::TPW == 1, "one token per epilogue thread");
+        const int sp = warp & 3, wq = warp >> 2;          // TMEM lanes 32 sp.., the item's token wq
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sp) << 16) + (uint32_t)(wq * S::COLS);
         // every slot starts armed with the 1.5 * 2^23 bits
         for (int slot = 0; slot < S::SLOTS; ++slot) {
@@ -296,70 +299,94 @@ gemm_i8_tc_kernel(const FusedI8Args f, const __grid_constant__ CUtensorMap wmap,
         if (lane == 0)
             for (int slot = 0; slot < S::SLOTS; ++slot) mbar_arrive(&tempty[slot]);
         const int et = t;                               // 0..511
+        constexpr int PFN = 2;                          // block scales per thread and item (T * blocks <= 1024)
+        float pf_xs[PFN], pf_off = 0.0f;
+        int pf_bs[PFN];
+        auto prefetch = [&](int it) {
+            if (it >= items) return;
+            const int t0 = (it / row_tiles) * T;
+#pragma unroll
+            for (int u = 0; u < PFN; ++u) {
+                const int i = et + u * I8TC_EPI_WARPS * 32;
+                if (i < T * blocks) {
+                    const int tt = i / blocks, b = i - tt * blocks;
+                    const int64_t src = (int64_t)min(t0 + tt, a.m - 1) * blocks + b;
+                    pf_xs[u] = __ldg(a.xs + src);
+                    if (PRO == PRO_OFFSET) pf_bs[u] = __ldg(f.bsums_in + src);
+                }
+            }
+            if (PRO == PRO_NONE && et < T) pf_off = __ldg(a.offset + min(t0 + et, a.m - 1));
+        };
+        prefetch(blockIdx.x);
+        const float2 neg_magic = make_float2(-I8TC_MAGIC_F, -I8TC_MAGIC_F);
         int q = 0;
         for (int it = blockIdx.x; it < items; it += gridDim.x) {
             const int rt = it % row_tiles, t0 = (it / row_tiles) * T;
-            // the item's block scales and offsets
-            for (int i = et; i < T * blocks; i += I8TC_EPI_WARPS * 32) {
-                const int tt = i / blocks, b = i - tt * blocks;
-                const int64_t src = (int64_t)min(t0 + tt, a.m - 1) * blocks + b;
-                const float sc = a.xs[src];
-                xs_s[tt * bpad + b] = sc;
-                if (PRO == PRO_OFFSET) term_s[tt * bpad + b] = fmul((float)f.bsums_in[src], sc);
+            // the item's block scales and offsets (loaded during the previous item)
+#pragma unroll
+            for (int u = 0; u < PFN; ++u) {
+                const int i = et + u * I8TC_EPI_WARPS * 32;
+                if (i < T * blocks) {
+                    const int tt = i / blocks, b = i - tt * blocks;
+                    xs_s[tt * bpad + b] = pf_xs[u];
+                    if (PRO == PRO_OFFSET) term_s[tt * bpad + b] = fmul((float)pf_bs[u], pf_xs[u]);
+                }
             }
-            if (PRO == PRO_NONE && et < T) offs_s[et] = a.offset[min(t0 + et, a.m - 1)];
+            if (PRO == PRO_NONE && et < T) offs_s[et] = pf_off;
             epi_bar();
+            // the offset: 128 * in-order sum over blocks of block sum * scale (read after the chunks)
             if (PRO == PRO_OFFSET && warp < T && lane == 0) offs_s[warp] = fmul(chain_sum(term_s + warp * bpad, blocks), 128.0f);
+            prefetch(it + gridDim.x);
 
-            float acc[S::TPW][32];
+            // accumulator pairs (8g + l, 8g + l + 1), l even
+            float2 acc2[16];
 #pragma unroll
-            for (int j = 0; j < S::TPW; ++j)
-#pragma unroll
-                for (int i = 0; i < 32; ++i) acc[j][i] = 0.0f;
-            bool ok = true;
+            for (int i = 0; i < 16; ++i) acc2[i] = make_float2(0.0f, 0.0f);
+            const float *xs_t = xs_s + wq * bpad;
             for (int c = 0; c < chunks; ++c, ++q) {
                 const int slot = q % S::SLOTS;
-                ok = mbar_wait_for(&tfull[slot], (unsigned)((q / S::SLOTS) & 1), limit) && !s_fail;
+                bool ok = mbar_wait_for(&tfull[slot], (unsigned)((q / S::SLOTS) & 1), limit) && !s_fail;
                 if (!__all_sync(0xffffffffu, ok)) {
-                    ok = false;
                     s_fail = 1;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t sa = lane_base + slot * S::SLOT_COLS;
-                // one token's eight lanes of one group at a time (8 TMEM columns)
+                const int groups = c < whole ? 4 : (K - c * CHUNK) / QBLOCK;
+                uint32_t d[4][8];
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                    if (g < groups) tmem_ld<8>(sa + g * S::N, d[g]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                    if (g < groups) tmem_st_magic<8>(sa + g * S::N);
                 if (c < whole) {
+                    const float4 sc4 = *reinterpret_cast<const float4 *>(xs_t + 4 * c);
+                    const float scg[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
-                        const int G = 4 * c + g;
+                        const float2 sc = make_float2(scg[g], scg[g]);
 #pragma unroll
-                        for (int j = 0; j < S::TPW; ++j) {
-                            uint32_t d[8];
-                            tmem_ld<8>(sa + g * S::N + 8 * j, d);
-                            const float sc = xs_s[(wq * S::TPW + j) * bpad + G];
-                            tmem_wait_ld();
-                            tmem_st_magic<8>(sa + g * S::N + 8 * j);
-#pragma unroll
-                            for (int l = 0; l < 8; ++l)
-                                acc[j][8 * g + l] =
-                                    __fmaf_rn(fsub(__uint_as_float(d[l]), I8TC_MAGIC_F), sc, acc[j][8 * g + l]);
+                        for (int l = 0; l < 8; l += 2) {
+                            const float2 v = __fadd2_rn(make_float2(__uint_as_float(d[g][l]), __uint_as_float(d[g][l + 1])),
+                                                        neg_magic);
+                            acc2[4 * g + l / 2] = __ffma2_rn(v, sc, acc2[4 * g + l / 2]);
                         }
                     }
                 } else {
                     // 32-byte groups past the last whole chunk: accumulators 0..7, group after group
-                    const int groups = (K - c * CHUNK) / QBLOCK;
-                    for (int g = 0; g < groups; ++g) {
-                        const int G = 4 * c + g;
 #pragma unroll
-                        for (int j = 0; j < S::TPW; ++j) {
-                            uint32_t d[8];
-                            tmem_ld<8>(sa + g * S::N + 8 * j, d);
-                            const float sc = xs_s[(wq * S::TPW + j) * bpad + G];
-                            tmem_wait_ld();
-                            tmem_st_magic<8>(sa + g * S::N + 8 * j);
+                    for (int g = 0; g < 4; ++g) {
+                        if (g < groups) {
+                            const float s1 = xs_t[4 * c + g];
+                            const float2 sc = make_float2(s1, s1);
 #pragma unroll
-                            for (int l = 0; l < 8; ++l)
-                                acc[j][l] = __fmaf_rn(fsub(__uint_as_float(d[l]), I8TC_MAGIC_F), sc, acc[j][l]);
+                            for (int l = 0; l < 8; l += 2) {
+                                const float2 v = __fadd2_rn(make_float2(__uint_as_float(d[g][l]), __uint_as_float(d[g][l + 1])),
+                                                            neg_magic);
+                                acc2[l / 2] = __ffma2_rn(v, sc, acc2[l / 2]);
+                            }
                         }
                     }
                 }
@@ -368,61 +395,63 @@ gemm_i8_tc_kernel(const FusedI8Args f, const __grid_constant__ CUtensorMap wmap,
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[slot]);
             }
-            // every epilogue warp must take the same barriers: agree on failure first
+            // every epilogue warp must take the same barriers: agree on failure first (this barrier
+            // also publishes the offsets)
             epi_bar();
             if (s_fail) break;
 
             // ---- _combine, dequantize, epilogue ----
-            const int lrow = 32 * sp + lane;                 // TMEM lane = row of the item
+            float acc[32];
 #pragma unroll
-            for (int j = 0; j < S::TPW; ++j) {
-                const int tl = wq * S::TPW + j, tok = t0 + tl;
-                const float sum = combine32(acc[j]);
-                if (!TWO) {
-                    const int row = rt * I8TC_ROWS + lrow;
-                    if (tok < a.m && row < a.n) {
-                        const float y = fmul(fsub(sum, offs_s[tl]), a.scales[row]);
-                        float out = y;
-                        if (EPI == EPI_BIAS) out = fadd(y, a.bias[row]);
-                        if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)tok * a.n + row], y);
-                        a.out[(int64_t)tok * a.n + row] = out;
-                    }
-                } else {
-                    const int i = rt * 64 + (lrow & 63);
-                    const bool up = lrow >= 64;
-                    const int ic = min(i, a.n - 1);
-                    const float y = fmul(fsub(sum, offs_s[tl]), up ? a.scales2[ic] : a.scales[ic]);
-                    if (up) ex_s[tl * 64 + (lrow - 64)] = y;
-                    else hq_s[tl * 64 + lrow] = y;
-                }
+            for (int i = 0; i < 16; ++i) {
+                acc[2 * i] = acc2[i].x;
+                acc[2 * i + 1] = acc2[i].y;
             }
-            if (TWO) {
+            const int lrow = 32 * sp + lane;                 // TMEM lane = row of the item
+            const int tl = wq, tok = t0 + tl;
+            const float sum = combine32(acc);
+            if (!TWO) {
+                const int row = rt * I8TC_ROWS + lrow;
+                if (tok < a.m && row < a.n) {
+                    const float y = fmul(fsub(sum, offs_s[tl]), a.scales[row]);
+                    float out = y;
+                    if (EPI == EPI_BIAS) out = fadd(y, a.bias[row]);
+                    if (EPI == EPI_RESIDUAL) out = fadd(a.residual[(int64_t)tok * a.n + row], y);
+                    a.out[(int64_t)tok * a.n + row] = out;
+                }
+            } else {
+                const int i = rt * 64 + (lrow & 63);
+                const bool up = lrow >= 64;
+                const int ic = min(i, a.n - 1);
+                const float y = fmul(fsub(sum, offs_s[tl]), up ? a.scales2[ic] : a.scales[ic]);
+                if (up) ex_s[tl * 64 + (lrow - 64)] = y;
+                else hq_s[tl * 64 + lrow] = y;
                 epi_bar();
-                for (int i = et; i < T * 64; i += I8TC_EPI_WARPS * 32) {
-                    const int tl = i / 64, r = i % 64, col = rt * 64 + r, tok = t0 + tl;
-                    const float out = swiglu(hq_s[i], ex_s[i], tab);
-                    if (EPI == EPI_SWIGLU && tok < a.m && col < a.n) a.out[(int64_t)tok * a.n + col] = out;
-                    hq_s[i] = out;
+                for (int i2 = et; i2 < T * 64; i2 += I8TC_EPI_WARPS * 32) {
+                    const int tl2 = i2 / 64, r = i2 % 64, col = rt * 64 + r, tok2 = t0 + tl2;
+                    const float out = swiglu(hq_s[i2], ex_s[i2], tab);
+                    if (EPI == EPI_SWIGLU && tok2 < a.m && col < a.n) a.out[(int64_t)tok2 * a.n + col] = out;
+                    hq_s[i2] = out;
                 }
                 if (EPI == EPI_SWIGLU_QUANT) {
                     epi_bar();
                     // one warp per (token, 32-row block)
                     for (int task = warp; task < T * 2; task += I8TC_EPI_WARPS) {
-                        const int tl = task >> 1, blk = task & 1, tok = t0 + tl, gb = rt * 2 + blk;
-                        if (tok < a.m && gb < a.n / QBLOCK) {
+                        const int tl2 = task >> 1, blk = task & 1, tok2 = t0 + tl2, gb = rt * 2 + blk;
+                        if (tok2 < a.m && gb < a.n / QBLOCK) {
                             int8_t qv;
                             int bsv;
-                            const float sc = quantize_block_warp(hq_s[tl * 64 + blk * QBLOCK + lane], &qv, &bsv);
-                            f.q_out[(int64_t)tok * a.n + gb * QBLOCK + lane] = qv;
+                            const float sc = quantize_block_warp(hq_s[tl2 * 64 + blk * QBLOCK + lane], &qv, &bsv);
+                            f.q_out[(int64_t)tok2 * a.n + gb * QBLOCK + lane] = qv;
                             if (lane == 0) {
-                                f.xs_out[(int64_t)tok * (a.n / QBLOCK) + gb] = sc;
-                                f.bsums_out[(int64_t)tok * (a.n / QBLOCK) + gb] = bsv;
+                                f.xs_out[(int64_t)tok2 * (a.n / QBLOCK) + gb] = sc;
+                                f.bsums_out[(int64_t)tok2 * (a.n / QBLOCK) + gb] = bsv;
                             }
                         }
                     }
                 }
+                epi_bar();                              // ex_s / hq_s are free for the next item
             }
-            epi_bar();                                  // the item's scales and outputs are consumed
         }
     }
 

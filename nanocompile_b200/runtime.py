@@ -112,6 +112,7 @@ def library() -> ctypes.CDLL:
             "nc_qwen2_decode_timed": ([_vp, _i32, _P32, _P64, _P32, _i32, _PF], _i32),
             "nc_qwen2_profile": ([_vp, _i32, _P32, _P64, _P32, _i32, _PF, _P32], _i32),
             "nc_qwen2_probe": ([_vp, _i32, _PF, _P32], _i32),
+            "nc_qwen2_step_timed": ([_vp, _i32, _P64, _P32, _P32, _i32, _PF], _i32),
         }
         for name, (args, res) in signatures.items():
             fn = getattr(L, name)
@@ -311,6 +312,17 @@ class DeviceModel:
         check(library().nc_qwen2_profile(self._h, first.size, _p(slot, _P32), _p(first, _P64), _p(start, _P32), steps,
                                          _p(ms, _PF), _p(n, _P32)))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KINDS) if n[i]}
+
+    def step_timed(self, ids: Sequence[int], slot: int, start: int, iters: int) -> float:
+        """Average device milliseconds of ``iters`` eager steps of ``ids`` at positions ``start..``
+        of ``slot`` (the last row's token only), timed with CUDA events on the model's stream."""
+        ids = np.ascontiguousarray(ids, np.int64)
+        slots = np.full(ids.size, slot, np.int32)
+        pos = np.arange(start, start + ids.size, dtype=np.int32)
+        ms = ctypes.c_float(0)
+        check(library().nc_qwen2_step_timed(self._h, ids.size, _p(ids, _P64), _p(slots, _P32), _p(pos, _P32), iters,
+                                            ctypes.byref(ms)))
+        return float(ms.value)
 
     def probe(self, on: bool) -> dict[str, tuple[float, int]]:
         """Start (``on``) or stop timing every launch of the following :meth:`step` calls; stopping

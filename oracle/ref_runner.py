@@ -71,6 +71,10 @@ class ReferenceModel:
         self._packs: dict[tuple[int, int], np.ndarray] = {}
         self.vocab = int(self.plan["buffers"][self.plan["outputs"]["logits"]]["shape"][-1][0][1])
 
+    def set_threads(self, threads: int) -> None:
+        """Threads of the reference's pool (its NANOCOMPILE_THREADS), the calling thread included."""
+        self.pool.nc_pool_set_threads(int(threads))
+
     def _packed(self, buffer: int, block: int) -> np.ndarray:
         key = (buffer, block)
         if key not in self._packs:

@@ -65,10 +65,11 @@ def test_tensor_core_projection_stops_on_a_short_wait_and_recovers(short_waits):
     assert np.array_equal(bits(args[0].numpy()), bits(expect))
 
 
-def test_batched_decode_step_fault_is_reported_and_the_retry_is_exact(short_waits):
-    """Eight sequences (the tensor-core projections): a decode with waits cut short fails with
+def test_batched_decode_step_fault_is_reported_and_the_retry_is_exact(short_waits, monkeypatch):
+    """Eight sequences on the tensor-core projections: a decode with waits cut short fails with
     KernelError; the same decode again, at the default limit, gives the oracle's tokens."""
     cuda = short_waits
+    monkeypatch.setenv("NC_TC_I8", "1")
     w = q.int8_projection_weights(synthetic_weights(SMALL, seed=3), SMALL)
     model = cuda.DeviceModel(SMALL, w, "int8", max_rows=8, slots=8, capacity=128)
     first, starts = [], []

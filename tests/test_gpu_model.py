@@ -196,6 +196,24 @@ def test_05b_batched_decode_is_the_references(reference, cuda, qwen05b_weights):
     assert np.array_equal(tokens, expected[:, 1:])
 
 
+def test_05b_batched_decode_on_tensor_core_projections(cuda, qwen05b_vnni_weights, monkeypatch):
+    """Configuration 5's first 16 steps with the tcgen05 kind::i8 projections (NC_TC_I8=1)."""
+    monkeypatch.setenv("NC_TC_I8", "1")
+    g = golden("batch")
+    past = int(g["past"])
+    model = cuda.DeviceModel(QWEN2_0_5B, qwen05b_vnni_weights, "int8", max_rows=64, slots=64, capacity=past + 32)
+    first = []
+    for b in range(64):
+        k, v, t = synthetic_cache(QWEN2_0_5B, b, past)
+        model.kv_write(b, 0, k, v)
+        first.append(t)
+    kinds = model.profile(first, list(range(64)), [past] * 64, 1)
+    tokens, _ = model.decode(first, list(range(64)), [past] * 64, 16)
+    assert np.array_equal(tokens.T, g["tokens"][:, 1:17])
+    assert "gate_up_projection" in kinds
+    model.close()
+
+
 @pytest.mark.parametrize("rows", [1, 3, 4])
 def test_05b_small_batched_decode_is_the_references(cuda, qwen05b_vnni_weights, rows):
     """A few of configuration 5's sequences at once: the persistent decode step (up to four rows)."""
