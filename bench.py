@@ -414,7 +414,8 @@ def run_prefill(cfg, weights, dev: int, iters: int) -> dict:
             "projection_int8_tops": round(proj_tops, 2) if proj_tops else None,
             "tensor_frac_of_nominal_int8": round(tops / INT8_DENSE_TOPS, 4),
             "projection_tensor_frac_of_nominal_int8": round(proj_tops / INT8_DENSE_TOPS, 4) if proj_tops else None,
-            "note": "useful ops 2*512*357.8M; the block-diagonal tcgen05 operand issues 8x that on the tensor pipe",
+            "note": "useful int8 ops 2*512*357.8M over the step time; the projections run on the dp4a kernels "
+                    "(the tcgen05 kind::i8 kernel, NC_TC_I8=1, is slower: profiles/gemm_i8_tc_kernel_bs64.md)",
             "kernel_shares": {k: round(v[0] / total, 3) for k, v in sorted(kinds.items(), key=lambda x: -x[1][0])}}
 
 
@@ -486,6 +487,65 @@ def run_phase6(args) -> dict:
             "speedup_median": round(statistics.median(per[best_ref]) / statistics.median(per["b200"]), 1)}
 
 
+def run_projections(rows: int, iters: int) -> dict:
+    """The batched int8 projections alone at the 0.5B model's shapes, each entry point timed with
+    CUDA events on the launching stream (after 3 untimed launches): the tensor-core kernel
+    (nc_matmul_i8_tc) against the default dp4a one (nc_matmul_i8_vnni; its SwiGLU form without the
+    quantized output). Random bytes: the time does not depend on the values."""
+    import ctypes
+
+    import torch
+
+    from nanocompile_b200 import runtime as rt
+
+    L = rt.library()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    rng = np.random.default_rng(0)
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    out = {}
+    for name, (n, k, epi, pro) in {"qkv_projection": (1152, 896, 1, 0), "o_projection": (896, 896, 2, 2),
+                                   "gate_up_projection": (4864, 896, 4, 0), "down_projection": (896, 4864, 2, 2)}.items():
+        xq = t(rng.integers(-127, 128, (rows, k), dtype=np.int8))
+        xs = t(np.abs(rng.standard_normal((rows, k // 32))).astype(np.float32))
+        off = t(rng.standard_normal(rows).astype(np.float32))
+        bs = t(rng.integers(-500, 500, (rows, k // 32), dtype=np.int32))
+        w, w2 = t(rng.integers(0, 256, (n, k), dtype=np.uint8)), t(rng.integers(0, 256, (n, k), dtype=np.uint8))
+        s1, s2 = (t(np.abs(rng.standard_normal(n)).astype(np.float32) * 1e-3) for _ in range(2))
+        y = torch.zeros((rows, n), dtype=torch.float32, device=dev)
+        extra = {1: t(rng.standard_normal(n).astype(np.float32)), 2: y, 4: w2}[epi]
+        qo = torch.zeros((rows, n), dtype=torch.int8, device=dev)
+        xo = torch.zeros((rows, n // 32), dtype=torch.float32, device=dev)
+        bo = torch.zeros((rows, n // 32), dtype=torch.int32, device=dev)
+        ptr = lambda x: x.data_ptr() if x is not None else None                      # noqa: E731
+        calls = {"tcgen05": (L.nc_matmul_i8_tc, [y, xq, xs, off, w, s1, extra, s2 if epi == 4 else None,
+                                                  bs if pro else None, qo, xo, bo], [rows, n, k, epi, pro, 0])}
+        if not pro:                                 # the dp4a entry point takes given offsets
+            e2 = 3 if epi == 4 else epi
+            calls["dp4a"] = (L.nc_matmul_i8_vnni, [y, xq, xs, off, w, s1, extra, s2 if e2 == 3 else None],
+                             [rows, n, k, e2])
+        out[name] = {}
+        for kind, (fn, p, sz) in calls.items():
+            pp = (ctypes.c_void_p * len(p))(*[ptr(x) for x in p])
+            ss = (ctypes.c_int64 * len(sz))(*sz)
+            st = ctypes.c_void_p(stream.cuda_stream)
+            for _ in range(3):
+                rt.check(fn(pp, ss, st))
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(iters):
+                rt.check(fn(pp, ss, st))
+            b.record()
+            torch.cuda.synchronize()
+            out[name][kind] = round(a.elapsed_time(b) * 1000 / iters, 2)
+    rt.device_faults()
+    return {"projections_us": out, "rows": rows, "iters": iters}
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -499,6 +559,8 @@ def main() -> int:
                         help="alternating-order A/B rounds of one decode step: this backend against the reference "
                              "at each thread count (JSON lines to --records)")
     parser.add_argument("--records", default=str(ROOT / "gpurun_out" / "phase6_results.jsonl"))
+    parser.add_argument("--projections", type=int, default=0, metavar="ROWS",
+                        help="time the batched int8 projection entry points alone at ROWS rows")
     parser.add_argument("--cpu-steps", type=int, default=8)
     parser.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (profiling runs only)")
     parser.add_argument("--past", type=int, default=PAST, help="cached positions at the first step (profiling runs only)")
@@ -508,6 +570,9 @@ def main() -> int:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.phase6:
         print(json.dumps(run_phase6(args)), flush=True)
+        return 0
+    if args.projections:
+        print(json.dumps(run_projections(args.projections, max(args.steps, 1))), flush=True)
         return 0
     if args.impl == "reference":
         line = run_reference(args)
