@@ -70,6 +70,13 @@ __device__ __forceinline__ float expf_exact(float x, const uint64_t *tab) {
 // stored already offset (u8 = w ^ 0x80), so one dp4a.u32.s32 gives the lane.  Seeding the
 // accumulator with the bits of 1.5 * 2^23 makes the result the float 12582912 + v exactly
 // (|v| <= 4 * 255 * 127 < 2^22), so int -> float is one exact subtraction, not a conversion.
+// The Dp4 lane as the float 1.5 * 2^23 + Dp4 (exact: |Dp4| < 2^22); subtracting 1.5 * 2^23 gives it.
+__device__ __forceinline__ float dp4_biased(uint32_t w_u8x4, uint32_t x_s8x4) {
+    int32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(w_u8x4), "r"(x_s8x4), "r"(0x4B400000));
+    return __int_as_float(d);
+}
+
 __device__ __forceinline__ float dp4_lane(uint32_t w_u8x4, uint32_t x_s8x4) {
     int32_t d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(w_u8x4), "r"(x_s8x4), "r"(0x4B400000));

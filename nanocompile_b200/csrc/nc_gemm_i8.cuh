@@ -132,13 +132,17 @@ __global__ void __launch_bounds__(GEMM_WARPS * 32, 2) gemm_i8_kernel(FusedI8Args
             if (lane == 0) offs_s[t] = fmul(chain_sum(term_s + t * bpad, blocks), 128.0f);
 
     // ---- the chains: chunk after chunk, D weight chunks in flight ----
-    float acc[NM][R][T];
+    // accumulator pairs of rows (2p, 2p + 1): the exact conversion and the fmaf of both run as one
+    // packed float2 add and one packed fma (each lane rounded as the scalar operation)
+    static_assert(R % 2 == 0, "rows are paired");
+    float2 acc[NM][R / 2][T];
 #pragma unroll
     for (int m = 0; m < NM; ++m)
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+        for (int r = 0; r < R / 2; ++r)
 #pragma unroll
-            for (int t = 0; t < T; ++t) acc[m][r][t] = 0.0f;
+            for (int t = 0; t < T; ++t) acc[m][r][t] = make_float2(0.0f, 0.0f);
+    const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
     const uint32_t *xw_s = reinterpret_cast<const uint32_t *>(xq_s) + lane;
     const float *sc_s = xs_s + (lane >> 3);
     for (int c0 = 0; c0 < chunks; c0 += D) {
@@ -163,11 +167,15 @@ __global__ void __launch_bounds__(GEMM_WARPS * 32, 2) gemm_i8_kernel(FusedI8Args
                 for (int t = 0; t < T; ++t) {
                     const uint32_t xw = xw_s[t * kw + c * 32];
                     const float sc = sc_s[t * bpad + 4 * c];
+                    const float2 scv = make_float2(sc, sc);
 #pragma unroll
                     for (int m = 0; m < NM; ++m)
 #pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            acc[m][r][t] = __fmaf_rn(dp4_lane(cur[m][r], xw), sc, acc[m][r][t]);
+                        for (int r = 0; r < R / 2; ++r) {
+                            const float2 v = __fadd2_rn(make_float2(dp4_biased(cur[m][2 * r], xw),
+                                                                    dp4_biased(cur[m][2 * r + 1], xw)), neg_magic);
+                            acc[m][r][t] = __ffma2_rn(v, scv, acc[m][r][t]);
+                        }
                 }
             }
         }
@@ -187,11 +195,15 @@ __global__ void __launch_bounds__(GEMM_WARPS * 32, 2) gemm_i8_kernel(FusedI8Args
             for (int t = 0; t < T; ++t) {
                 const uint32_t xw = xw_s[t * kw + wo];
                 const float sc = xs_s[t * bpad + (stride / QBLOCK) + k1];
+                const float2 scv = make_float2(sc, sc);
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
 #pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        acc[m][r][t] = __fmaf_rn(dp4_lane(tw[m][r], xw), sc, acc[m][r][t]);
+                    for (int r = 0; r < R / 2; ++r) {
+                        const float2 v = __fadd2_rn(make_float2(dp4_biased(tw[m][2 * r], xw),
+                                                                dp4_biased(tw[m][2 * r + 1], xw)), neg_magic);
+                        acc[m][r][t] = __ffma2_rn(v, scv, acc[m][r][t]);
+                    }
             }
         }
     }
@@ -203,7 +215,7 @@ __global__ void __launch_bounds__(GEMM_WARPS * 32, 2) gemm_i8_kernel(FusedI8Args
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int t = 0; t < T; ++t) v[(m * R + r) * T + t] = acc[m][r][t];
+            for (int t = 0; t < T; ++t) v[(m * R + r) * T + t] = (r & 1) ? acc[m][r / 2][t].y : acc[m][r / 2][t].x;
     butterfly_reduce<NACC>(v, lane);
     __syncthreads();   // offsets (PRO_OFFSET) are visible from here
 
