@@ -365,6 +365,7 @@ def run_bs1(cfg, model) -> dict:
     with ClockSampler(model.device) as clocks:
         ms = model.decode_timed([first], [0], [BS1_PROMPT], steps)
     profile = model.profile([first], [0], [512], 4)
+    phases = model.phase_times([first], [0], [512], 4)
     # the whole step against HBM: bytes a token must read (the layers' int8 weights and KV rows at
     # the workload's mean position, the LM head as read) over the measured time per token
     peak, source = measured_peaks()
@@ -383,7 +384,9 @@ def run_bs1(cfg, model) -> dict:
     return {"value": round(steps / (ms / 1000.0), 1), "unit": "tok/s", "ms_per_token": round(ms / steps, 4),
             "workload": f"batch 1: {BS1_PROMPT}-token prompt, then {steps} greedy decode steps (past "
                         f"{BS1_PROMPT}..{BS1_END - 1}) (configuration 3)",
-            "roofline": roofline(profile, cfg, 1, 512, "bs1"), "step_roofline": step, "clocks": clocks.summary()}
+            "roofline": roofline(profile, cfg, 1, 512, "bs1"), "step_roofline": step, "clocks": clocks.summary(),
+            "phases_us": {"past": 512, "note": "persistent kernel, per layer: microseconds from the layer's start to "
+                          "the last CTA reaching each event (globaltimer), mean over layers and 4 steps", **phases}}
 
 
 PREFILL = 512          # configuration 4

@@ -290,6 +290,18 @@ int32_t nc_qwen2_probe(nc_model *model, int32_t on, float *ms_per_kind, int32_t 
 int32_t nc_qwen2_profile(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
                          const int32_t *start, int32_t steps, float *ms_per_kind, int32_t *launches_per_kind);
 
+/* Phase table of the persistent decode kernel: `steps` eager decode steps (arguments as
+ * nc_qwen2_decode) with globaltimer stamps; us_per_event[NC_MK_EVENTS] gets, per event, the mean
+ * over layers and steps of the microseconds from the first CTA starting the layer to the last CTA
+ * reaching the event (-1: never reached).  Events: 0 layer start, 1 input words in, 2 input norm +
+ * quantization, 3 q/k/v rows out, 4 q/k/v words in (attention), 5 scores, 6 softmax, 7 attention
+ * out, 8 attention blocks in, 9 o rows out, 10 residual words in, 11 post norm, 12 gate/up rows
+ * staged, 13 SwiGLU blocks out, 14 SwiGLU blocks in, 15 down rows out.  NC_ERR_STATE when the
+ * persistent kernel does not serve `batch` rows of the model. */
+#define NC_MK_EVENTS 16
+int32_t nc_qwen2_phase_times(nc_model *model, int32_t batch, const int32_t *slot, const int64_t *first,
+                             const int32_t *start, int32_t steps, float *us_per_event);
+
 #ifdef __cplusplus
 }
 #endif

@@ -813,10 +813,12 @@ __device__ __forceinline__ void att_prefetch_k(const AttnItem &it, float *ring, 
 // scratch, ring 1024-byte aligned, kbar[2] / vbar[4] initialized mbarriers whose phases kpar /
 // vpar track (bit per stage), K chunks 0 and 1 already requested (att_prefetch_k). Warp 0's
 // lane c gets dimension ds*32 + c of the context in *acc. False when a wait gave up (then every
-// thread returns false).
+// thread returns false). With st set, thread 0 writes globaltimer stamps there: st[0] when the
+// scores are done, st[1] when the probabilities are.
 __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q, const float *kn, const float *vn, float *e,
                                              float *ring, uint64_t *kbar, uint64_t *vbar, unsigned &kpar, unsigned &vpar,
-                                             const uint64_t *tab, float *s_red, float *s_scal, float *acc_out) {
+                                             const uint64_t *tab, float *s_red, float *s_scal, float *acc_out,
+                                             unsigned long long *st = nullptr) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int len = it.len, nk = (len + ATB_CHUNK - 1) / ATB_CHUNK;
     float mx = __uint_as_float(0xff800000u);
@@ -852,6 +854,7 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
         }
     }
     // the ring now takes the V slice: four chunks in flight while the softmax runs
+    if (st && t == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st[0]));
     if (t == 0) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int ci = 0; ci < nk && ci < 4; ++ci) att_issue_v(it, ring, vbar, ci);
@@ -877,6 +880,7 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     const float shs = s_scal[1], rcp = s_scal[2];
     for (int j = t; j < len; j += ATT_THREADS) e[j] = fdiv_recip(e[j], shs, rcp);
     __syncthreads();
+    if (st && t == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st[1]));
     // P.V: warp 0's lanes own the slice's 32 dimensions, positions in order; element (row j,
     // column c) of a swizzled stage sits at j*32 + ((c/4) ^ (j%8))*4 + c%4
     float acc = 0.0f;

@@ -1005,6 +1005,7 @@ struct nc_model {
     unsigned long long *mk_xt = nullptr, *mk_qkvt = nullptr, *mk_aqt = nullptr, *mk_hqt = nullptr;   // tagged words
     int64_t mk_tagged_bytes = 0;    // the four tagged buffers, contiguous from mk_xt
     int mk_ctas = 0;                // one CTA per SM; 0: the kernel cannot serve this model
+    unsigned long long *mk_stamps = nullptr;   // phase stamps of the next launches, or null
     bool logit_identity = false;    // the step's logit rows are its rows 0..rows-1 (set per step)
 
     // activations and step state
@@ -1135,6 +1136,7 @@ int32_t launch_decode_mk(nc_model *m, int rows) {
     a.aqt = a.qkvt + (int64_t)MK_ROWS * Nqkv;
     a.hqt = a.aqt + (int64_t)MK_ROWS * (Hq / QBLOCK) * MK_BLOCK_WORDS;
     a.sync = m->mk_sync;
+    a.stamps = m->mk_stamps;
     const MkSmem L = mk_smem(a.nl, rows, H, std::max(H, std::max(Hq, a.I)), a.d, a.cap);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(m->mk_ctas);
@@ -1879,6 +1881,62 @@ extern "C" int32_t nc_qwen2_profile(nc_model *m, int32_t batch, const int32_t *s
             launches_per_kind[pm.first] += 1;
         }
     }
+    return model_faults(m);
+}
+
+extern "C" int32_t nc_qwen2_phase_times(nc_model *m, int32_t batch, const int32_t *slot, const int64_t *first,
+                                         const int32_t *start, int32_t steps, float *us_per_event) {
+    if (!us_per_event) return fail(NC_ERR_ARGUMENT, "null argument");
+    cudaGraphExec_t graph;
+    NC_TRY(decode_setup(m, batch, slot, first, start, steps, true, &graph));
+    if (!(m->c.quant == 1 && m->mk_ctas && batch <= MK_ROWS))
+        return fail(NC_ERR_STATE, "the persistent decode kernel does not serve %d rows of this model", batch);
+    const int G = m->mk_ctas, nl = (int)m->c.layers;
+    const size_t words = (size_t)G * nl * MK_EVENTS;
+    unsigned long long *dev = nullptr;
+    CUDA_TRY(cudaMalloc(&dev, words * 8));
+    std::vector<unsigned long long> host(words);
+    std::vector<double> sum(MK_EVENTS, 0.0);
+    std::vector<int> count(MK_EVENTS, 0);
+    cudaStream_t st = m->stream;
+    int32_t status = NC_OK;
+    m->logit_identity = true;
+    for (int s = 0; s < steps && status == NC_OK; ++s) {
+        if (cudaMemsetAsync(dev, 0, words * 8, st) != cudaSuccess) { status = fail(NC_ERR_CUDA, "clearing stamps"); break; }
+        m->mk_stamps = dev;
+        status = enqueue_step(m, batch, batch, true, true);
+        m->mk_stamps = nullptr;
+        if (status != NC_OK) break;
+        if (launch_k(advance_kernel, 1, 1024, 0, st, m->ids, m->pos, m->tokens, m->history, m->step, batch) != cudaSuccess) {
+            status = fail(NC_ERR_CUDA, "launching advance_kernel");
+            break;
+        }
+        if (cudaMemcpyAsync(host.data(), dev, words * 8, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess) {
+            status = fail(NC_ERR_CUDA, "reading stamps");
+            break;
+        }
+        // per layer and event: the last CTA that wrote it, from the first CTA to start the layer
+        for (int l = 0; l < nl; ++l) {
+            unsigned long long t0 = ~0ull;
+            for (int b = 0; b < G; ++b) {
+                const unsigned long long v = host[((size_t)b * nl + l) * MK_EVENTS];
+                if (v && v < t0) t0 = v;
+            }
+            if (t0 == ~0ull) continue;
+            for (int e = 0; e < MK_EVENTS; ++e) {
+                unsigned long long last = 0;
+                for (int b = 0; b < G; ++b) last = std::max(last, host[((size_t)b * nl + l) * MK_EVENTS + e]);
+                if (last >= t0) {
+                    sum[e] += (double)(last - t0) * 1e-3;
+                    count[e] += 1;
+                }
+            }
+        }
+    }
+    cudaFree(dev);
+    NC_TRY(status);
+    for (int e = 0; e < MK_EVENTS; ++e) us_per_event[e] = count[e] ? (float)(sum[e] / count[e]) : -1.0f;
     return model_faults(m);
 }
 

@@ -45,6 +45,12 @@ constexpr int MK_GU_LPR = 8;            // lanes per gate/up row: 4 rows per war
 constexpr int MK_NCH_DOWN = 40;         // chunks of an MLP-wide weight row (<= 5120)
 constexpr int MK_MAX_LAYERS = 48;       // (layer, phase) fits the tag's low byte
 constexpr int MK_BLOCK_WORDS = 10;      // a quantized block: 8 words of int8, its scale, its sum
+// Phase stamps (globaltimer, ns) a CTA writes per layer when MkArgs::stamps is set:
+//   0 layer start        1 input words in      2 input norm + quantization done   3 q/k/v rows out
+//   4 q/k/v words in (attention CTAs)          5 scores done      6 softmax done   7 attention out
+//   8 attention blocks in 9 o rows out         10 residual words in 11 post norm done
+//   12 gate/up rows staged 13 SwiGLU blocks out 14 SwiGLU blocks in 15 down rows out
+constexpr int MK_EVENTS = 16;
 
 __device__ unsigned int g_mk_fault;
 
@@ -71,6 +77,7 @@ struct MkArgs {
     unsigned long long *aqt;                  // tagged attention output blocks [MK_ROWS][Hq/32][10]
     unsigned long long *hqt;                  // tagged SwiGLU output blocks [MK_ROWS][I/32][10]
     unsigned int *sync;                       // [0] CTAs finished, [1] launch number
+    unsigned long long *stamps;               // [G][nl][MK_EVENTS] phase stamps, or null
 };
 
 // dynamic shared memory: the layer table | gains [2][H] | rows / squares [m][H] | quantized
@@ -127,6 +134,12 @@ __device__ __forceinline__ void mk_prefetch_l2(const void *p, int64_t bytes) {
         c += n;
         bytes -= n;
     }
+}
+
+__device__ __forceinline__ unsigned long long mk_now() {
+    unsigned long long v;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(v));
+    return v;
 }
 
 // Reads words addr(0) .. addr(n-1) until each carries tag, handing (index, value) to store; up to
@@ -337,6 +350,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
     const uint32_t launch = (a.sync[1] + 1u) & 0xffffffu;
     auto tag = [&](int l, int k) { return (launch << 8) | (uint32_t)(l * 5 + k); };   // k: 0 x after o, 1 x after down,
                                                                                    // 2 q/k/v, 3 attention, 4 SwiGLU
+    auto stamp = [&](int l, int ev) {
+        if (a.stamps && t == 0) a.stamps[((int64_t)b * a.nl + l) * MK_EVENTS + ev] = mk_now();
+    };
 
     // this CTA's rows of every projection
     int q0, q1, o0, o1, u0, u1;
@@ -408,6 +424,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
 
     for (int l = 0; l < a.nl; ++l) {
         const MkLayer &W = layers[l];
+        stamp(l, 0);
         float *base = W.cache + aslot * a.slot_stride;
         float *Kc = base + (int64_t)ag * a.cap * d;
         float *Vc = base + ((int64_t)a.kv + ag) * a.cap * d;
@@ -442,8 +459,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             });
             if (__syncthreads_or(!ok)) return;
         }
+        stamp(l, 1);
         cp_async_wait<0>();                                  // the gains (made visible by the norm's barriers)
         mk_norm_quant(m, H, a.eps, gain_in, xrow, sq, xq, xs, term, s_offs, s_inv);
+        stamp(l, 2);
         {
             const int row = q0 + warp;
             const bool ok = row < q1;
@@ -454,6 +473,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                           tag(l, 2));
             }
         }
+        stamp(l, 3);
         wo.load(W.wo + (int64_t)orow * Hq, Hq / CHUNK, lane, orow_ok);
         const float sc_o = orow_ok ? mk_ldf(W.so + orow) : 0.0f;
 
@@ -465,6 +485,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 return src + (which == 0 ? ah * d : (which == 1 ? (a.heads + ag) * d : (a.heads + a.kv + ag) * d)) + c;
             }, [&](int i, uint32_t v) { e[i] = __uint_as_float(v); });   // q | k | v as written, RoPE below
             if (__syncthreads_or(!ok)) return;
+            stamp(l, 4);
             for (int i = t; i < 3 * d; i += MK_THREADS) {
                 const int which = i / d, c = i % d;
                 if (which == 2) {
@@ -484,7 +505,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                     Vc[(int64_t)apos * d + c] = vn[c];
                 }
             float acc;
-            if (!att_item_tma(it, q, kn, vn, e, vring, s_kbar, s_vbar, kpar, vpar, tab, s_red, s_scal, &acc)) {
+            unsigned long long *ast = a.stamps ? a.stamps + ((int64_t)b * a.nl + l) * MK_EVENTS + 5 : nullptr;
+            if (!att_item_tma(it, q, kn, vn, e, vring, s_kbar, s_vbar, kpar, vpar, tab, s_red, s_scal, &acc, ast)) {
                 if (t == 0) atomicExch(&g_mk_fault, 1u);
                 return;
             }
@@ -496,11 +518,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 const float sc = quantize_block_warp(acc, &qv, &bs);
                 mk_put_block(a.aqt + ((int64_t)ar * (Hq / QBLOCK) + blk) * MK_BLOCK_WORDS, qv, sc, bs, tag(l, 3));
             }
+            stamp(l, 7);
         }
         const int lr = warp * (32 / MK_GU_LPR) + lane / MK_GU_LPR;     // this lane's gate/up row in a pass
 
         // ---- C: o rows with the residual add ----
         if (!mk_take_blocks(a.aqt, tag(l, 3), m, Hq, xq, xs, term, bsum)) return;
+        stamp(l, 8);
         {
             mk_offsets(term, m, Hq / QBLOCK, s_offs);
             float sum[MK_ROWS];
@@ -516,6 +540,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 }
             }
         }
+        stamp(l, 9);
         float sg[2], su[2];                                           // rows lr, lr + 32
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -532,7 +557,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             });
             if (__syncthreads_or(!ok)) return;
         }
+        stamp(l, 10);
         mk_norm_quant(m, H, a.eps, gain_post, xrow, sq, xq, xs, term, s_offs, s_inv);
+        stamp(l, 11);
         {
             const bool ok = mbar_wait_bounded(&s_gbar, gpar);
             gpar ^= 1u;
@@ -541,6 +568,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 return;
             }
         }
+        stamp(l, 12);
         {
             const int j = lane % MK_GU_LPR;
 #pragma unroll
@@ -567,11 +595,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 mk_put_block(a.hqt + ((int64_t)r * (I / QBLOCK) + u0 + blk) * MK_BLOCK_WORDS, qv, sc, bs, tag(l, 4));
             }
         }
+        stamp(l, 13);
         wd.load(W.wd + (int64_t)orow * I, I / CHUNK, lane, orow_ok);
         const float sc_d = orow_ok ? mk_ldf(W.sd + orow) : 0.0f;
 
         // ---- E: down rows with the residual add ----
         if (!mk_take_blocks(a.hqt, tag(l, 4), m, I, xq, xs, term, bsum)) return;
+        stamp(l, 14);
         {
             mk_offsets(term, m, I / QBLOCK, s_offs);
             float sum[MK_ROWS];
@@ -587,6 +617,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 }
             }
         }
+        stamp(l, 15);
         if (l + 1 < a.nl) {
             const MkLayer &N = layers[l + 1];
             const int row = q0 + warp;

@@ -111,6 +111,7 @@ def library() -> ctypes.CDLL:
             "nc_qwen2_decode": ([_vp, _i32, _P32, _P64, _P32, _i32, _i32, _P64, _PF], _i32),
             "nc_qwen2_decode_timed": ([_vp, _i32, _P32, _P64, _P32, _i32, _PF], _i32),
             "nc_qwen2_profile": ([_vp, _i32, _P32, _P64, _P32, _i32, _PF, _P32], _i32),
+            "nc_qwen2_phase_times": ([_vp, _i32, _P32, _P64, _P32, _i32, _PF], _i32),
             "nc_qwen2_probe": ([_vp, _i32, _PF, _P32], _i32),
             "nc_qwen2_step_timed": ([_vp, _i32, _P64, _P32, _P32, _i32, _PF], _i32),
         }
@@ -312,6 +313,23 @@ class DeviceModel:
         check(library().nc_qwen2_profile(self._h, first.size, _p(slot, _P32), _p(first, _P64), _p(start, _P32), steps,
                                          _p(ms, _PF), _p(n, _P32)))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KINDS) if n[i]}
+
+    PHASES = ("layer start", "input words in", "input norm", "q/k/v rows out", "q/k/v words in", "scores",
+              "softmax", "attention out", "attention blocks in", "o rows out", "residual words in", "post norm",
+              "gate/up staged", "SwiGLU out", "SwiGLU in", "down rows out")
+
+    def phase_times(self, first: Sequence[int], slot: Sequence[int], start: Sequence[int], steps: int
+                    ) -> dict[str, float]:
+        """The persistent decode kernel's phase table over ``steps`` eager decode steps:
+        microseconds from a layer's start to the last CTA reaching each event, averaged over layers
+        and steps (globaltimer stamps)."""
+        first = np.ascontiguousarray(first, np.int64)
+        slot = np.ascontiguousarray(slot, np.int32)
+        start = np.ascontiguousarray(start, np.int32)
+        us = np.zeros(len(self.PHASES), np.float32)
+        check(library().nc_qwen2_phase_times(self._h, first.size, _p(slot, _P32), _p(first, _P64), _p(start, _P32),
+                                             steps, _p(us, _PF)))
+        return {k: round(float(us[i]), 2) for i, k in enumerate(self.PHASES) if us[i] >= 0}
 
     def step_timed(self, ids: Sequence[int], slot: int, start: int, iters: int) -> float:
         """Average device milliseconds of ``iters`` eager steps of ``ids`` at positions ``start..``
