@@ -155,6 +155,7 @@ __device__ __forceinline__ float pv_chain(float acc, const float *p, int n, V &&
         float va[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) va[u] = vat(u);
+#pragma unroll 1
         for (; j + 16 <= n; j += 8) {
             const float4 b0 = *reinterpret_cast<const float4 *>(p + j + 8), b1 = *reinterpret_cast<const float4 *>(p + j + 12);
             float vb[8];
@@ -169,6 +170,7 @@ __device__ __forceinline__ float pv_chain(float acc, const float *p, int n, V &&
         acc = pv_add8(acc, a0, a1, va);
         j += 8;
     }
+#pragma unroll 1
     for (; j < n; ++j) acc = fadd(acc, fmul(p[j], vat(j)));
     return acc;
 }
@@ -825,6 +827,7 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     float4 qr[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) qr[c] = reinterpret_cast<const float4 *>(q)[c];
+#pragma unroll 1
     for (int ci = 0; ci < nk; ++ci) {
         const int s = ci & 1;
         const bool ok = mbar_wait_bounded(&kbar[s], (kpar >> s) & 1u);
@@ -869,6 +872,7 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     }
     __syncthreads();
     const float mh = s_scal[0];
+#pragma unroll 1
     for (int j = t; j < len; j += ATT_THREADS) e[j] = expf_exact(fsub(e[j], mh), tab);
     __syncthreads();
     if (t == 0) {
@@ -878,6 +882,7 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     }
     __syncthreads();
     const float shs = s_scal[1], rcp = s_scal[2];
+#pragma unroll 1
     for (int j = t; j < len; j += ATT_THREADS) e[j] = fdiv_recip(e[j], shs, rcp);
     __syncthreads();
     if (st && t == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st[1]));
@@ -887,6 +892,7 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     bool vok = true;
     if (warp == 0) {
         const int cl = lane & 3, cu = lane >> 2;
+#pragma unroll 1
         for (int ci = 0; ci < nk; ++ci) {
             const int s = ci & 3;
             vok = __all_sync(0xffffffffu, mbar_wait_bounded(&vbar[s], (vpar >> s) & 1u));

@@ -220,7 +220,8 @@ __device__ __forceinline__ void quantize_blocks_warp(const float *v, int8_t *q, 
     for (int u = 0; u < N; ++u) bsum[u] = __reduce_add_sync(0xffffffffu, (int)q[u]);
 }
 
-__device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bsum) {
+// Out of line: the persistent decode kernel calls it from two places every layer.
+__device__ __noinline__ float quantize_block_warp(float v, int8_t *q, int *bsum) {
     float scale;
     quantize_blocks_warp<1>(&v, q, &scale, bsum);
     return scale;
@@ -229,7 +230,9 @@ __device__ __forceinline__ float quantize_block_warp(float v, int8_t *q, int *bs
 // ---- in-order sums -------------------------------------------------------------------------
 // acc = acc + p[0] + p[1] + ... strictly left to right, by one thread.  Two 32-value register
 // buffers alternate: the next block's shared-memory loads are issued before the current
-// block's 32 dependent adds, so the chain runs at the add latency.  p must be 16-byte aligned.
+// block's 32 dependent adds (unconditionally: past the last block they reload it), so the chain
+// runs at the add latency.  p must be 16-byte aligned and readable up to the next multiple of 4
+// elements; the last n % 32 come as 16-byte loads, then their adds in order.
 __device__ __forceinline__ void add32(float &acc, const float4 *v) {
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -248,14 +251,14 @@ __device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.
     if (n32) {
 #pragma unroll
         for (int u = 0; u < 8; ++u) a[u] = p4[u];
+#pragma unroll 1
         for (; i + 64 <= n32; i += 64) {
 #pragma unroll
             for (int u = 0; u < 8; ++u) b[u] = p4[(i + 32) / 4 + u];
             add32(acc, a);
-            if (i + 64 < n32) {
+            const int na = min(i + 64, n32 - 32);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) a[u] = p4[(i + 64) / 4 + u];
-            }
+            for (int u = 0; u < 8; ++u) a[u] = p4[na / 4 + u];
             add32(acc, b);
         }
         if (i < n32) {
@@ -263,13 +266,17 @@ __device__ __forceinline__ float chain_sum(const float *p, int n, float acc = 0.
             i += 32;
         }
     }
-    if (i < n) {                        // the last n % 32: all loads first, then the adds in order
-        float tv[32];
+    if (i < n) {
+        const int nt = n - i;
 #pragma unroll
-        for (int u = 0; u < 32; ++u) tv[u] = i + u < n ? p[i + u] : 0.0f;
+        for (int u = 0; u < 8; ++u) b[u] = 4 * u < nt ? p4[i / 4 + u] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-        for (int u = 0; u < 32; ++u)
-            if (i + u < n) acc = fadd(acc, tv[u]);
+        for (int u = 0; u < 8; ++u) {
+            if (4 * u < nt) acc = fadd(acc, b[u].x);
+            if (4 * u + 1 < nt) acc = fadd(acc, b[u].y);
+            if (4 * u + 2 < nt) acc = fadd(acc, b[u].z);
+            if (4 * u + 3 < nt) acc = fadd(acc, b[u].w);
+        }
     }
     return acc;
 }

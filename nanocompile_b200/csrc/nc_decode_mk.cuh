@@ -128,6 +128,7 @@ __device__ __forceinline__ unsigned long long mk_ld(const unsigned long long *p)
 __device__ __forceinline__ void mk_prefetch_l2(const void *p, int64_t bytes) {
     // 16-byte aligned start and size (rows of a multiple of 128 bytes)
     const char *c = (const char *)p;
+#pragma unroll 1
     while (bytes > 0) {
         const int n = (int)(bytes < (1 << 20) ? bytes : (1 << 20));
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
@@ -147,6 +148,7 @@ __device__ __forceinline__ unsigned long long mk_now() {
 template <typename A, typename F>
 __device__ __forceinline__ bool mk_poll(int n, uint32_t tag, A &&addr, F &&store, long long limit = NC_DRAIN_CYCLES) {
     const long long t0 = clock64();
+#pragma unroll 1
     for (int base = threadIdx.x; base < n; base += 4 * MK_THREADS) {
         bool pend[4];
 #pragma unroll
@@ -175,6 +177,27 @@ __device__ __forceinline__ bool mk_poll(int n, uint32_t tag, A &&addr, F &&store
         }
     }
     return true;
+}
+
+// mk_poll over the contiguous words src[0..n), for the hand-overs of whole rows and of quantized
+// blocks. MK_TO_ROWS: word i is float x[i] -> rows[i] = x, squares[i] = x * x;
+// MK_TO_BLOCKS: ten words per quantized block rb -> four int8 each to q[rb * 32 ..], the scale to
+// scales[rb], the block sum to sums[rb].
+enum MkPollTo : int { MK_TO_ROWS = 0, MK_TO_BLOCKS = 1 };
+__device__ __forceinline__ bool mk_poll_into(const unsigned long long *src, int n, uint32_t tag, int to, float *rows,
+                                          float *squares, int8_t *q, float *scales, int *sums) {
+    return mk_poll(n, tag, [&](int i) { return src + i; }, [&](int i, uint32_t v) {
+        if (to == MK_TO_ROWS) {
+            const float f = __uint_as_float(v);
+            rows[i] = f;
+            squares[i] = fmul(f, f);
+        } else {
+            const int w = i % MK_BLOCK_WORDS, rb = i / MK_BLOCK_WORDS;
+            if (w < 8) reinterpret_cast<uint32_t *>(q)[(rb * QBLOCK) / 4 + w] = v;
+            else if (w == 8) scales[rb] = __uint_as_float(v);
+            else sums[rb] = (int)v;
+        }
+    });
 }
 
 // One warp's quantized block (lane = position) as ten tagged words: four int8 per word, the
@@ -273,6 +296,32 @@ __device__ __forceinline__ float mk_dot_smem(const uint8_t *wrow, const int8_t *
     return combine_lanes<APL>(acc);
 }
 
+// The gate and up rows of one SwiGLU output together (the same activations): both combined sums.
+template <int LPR>
+__device__ __forceinline__ void mk_dot2_smem(const uint8_t *grow, const uint8_t *urow, const int8_t *xq, const float *xs,
+                                             int chunks, int j, float *g, float *u) {
+    constexpr int BPL = 128 / LPR, APL = BPL / 4;
+    using SegT = typename Seg<BPL>::T;
+    float ag[APL], au[APL];
+#pragma unroll
+    for (int i = 0; i < APL; ++i) ag[i] = au[i] = 0.0f;
+    for (int c = 0; c < chunks; ++c) {
+        const int off = c * CHUNK + j * BPL;
+        uint32_t gv[APL], uv[APL], xv[APL];
+        Seg<BPL>::split(*reinterpret_cast<const SegT *>(grow + off), gv);
+        Seg<BPL>::split(*reinterpret_cast<const SegT *>(urow + off), uv);
+        Seg<BPL>::split(*reinterpret_cast<const SegT *>(xq + off), xv);
+        const float sc = xs[off / QBLOCK];
+#pragma unroll
+        for (int i = 0; i < APL; ++i) {
+            ag[i] = __fmaf_rn(dp4_lane(gv[i], xv[i]), sc, ag[i]);
+            au[i] = __fmaf_rn(dp4_lane(uv[i], xv[i]), sc, au[i]);
+        }
+    }
+    *g = combine_lanes<APL>(ag);
+    *u = combine_lanes<APL>(au);
+}
+
 // rms_norm (nanocompile/nn.py:34-38) of the m rows in xrow (squares in sq) with gain, then block
 // quantization (nanocompile/quantize.py:102-124) into xq / xs and the offsets.
 __device__ __forceinline__ void mk_norm_quant(int m, int H, float eps, const float *gain, float *xrow, const float *sq,
@@ -281,10 +330,9 @@ __device__ __forceinline__ void mk_norm_quant(int m, int H, float eps, const flo
     if (lane == 0 && warp < m)
         s_inv[warp] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(chain_sum(sq + warp * H, H), (float)H), eps)));
     __syncthreads();
-    for (int i = t; i < m * H; i += MK_THREADS) xrow[i] = fmul(fmul(xrow[i], s_inv[i / H]), gain[i % H]);
-    __syncthreads();
     for (int r = 0; r < m; ++r)
-        quantize_row_smem<4>(xrow + r * H, H, xq + r * H, xs + r * blocks, nullptr, term + r * blocks, warp, MK_WARPS, lane);
+        quantize_row_smem<4>(xrow + r * H, H, xq + r * H, xs + r * blocks, nullptr, term + r * blocks, warp, MK_WARPS, lane,
+                             gain, s_inv[r]);
     __syncthreads();
     if (lane == 0 && warp < m) offs[warp] = fmul(chain_sum(term + warp * blocks, blocks), 128.0f);
     __syncthreads();
@@ -295,13 +343,9 @@ __device__ __forceinline__ void mk_norm_quant(int m, int H, float eps, const flo
 __device__ __forceinline__ bool mk_take_blocks(const unsigned long long *src, uint32_t tag, int m, int k, int8_t *xq, float *xs,
                                                float *term, int *bsum) {
     const int t = threadIdx.x, blocks = k / QBLOCK;
-    const bool ok = mk_poll(m * blocks * MK_BLOCK_WORDS, tag, [&](int i) { return src + i; }, [&](int i, uint32_t v) {
-        const int w = i % MK_BLOCK_WORDS, rb = i / MK_BLOCK_WORDS;      // rb = r * blocks + b
-        if (w < 8) reinterpret_cast<uint32_t *>(xq)[(rb * QBLOCK) / 4 + w] = v;
-        else if (w == 8) xs[rb] = __uint_as_float(v);
-        else bsum[rb] = (int)v;
-    });
+    const bool ok = mk_poll_into(src, m * blocks * MK_BLOCK_WORDS, tag, MK_TO_BLOCKS, nullptr, nullptr, xq, xs, bsum);
     if (__syncthreads_or(!ok)) return false;
+#pragma unroll 1
     for (int i = t; i < m * blocks; i += MK_THREADS) term[i] = fmul((float)bsum[i], xs[i]);
     __syncthreads();
     return true;
@@ -322,6 +366,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
     __shared__ uint64_t tab[32];
     __shared__ float s_inv[MK_ROWS], s_offs[MK_ROWS], s_red[MK_WARPS];
     __shared__ float s_hout[MK_ROWS][2 * QBLOCK];
+    __shared__ float s_dot[MK_ROWS][MK_WARPS];
     __shared__ __align__(8) uint64_t s_kbar[2], s_vbar[4], s_gbar;
     __shared__ float s_scal[3];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31, b = blockIdx.x, G = gridDim.x;
@@ -433,9 +478,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         it.krow0 = W.row0 + aslot * a.slot_rows + (int64_t)ag * a.cap;
         it.vrow0 = W.row0 + aslot * a.slot_rows + (int64_t)(a.kv + ag) * a.cap;
         it.ds = ads; it.pos = apos; it.len = alen; it.own_new = true; it.scale = a.scale;
-        if (attn && t == 0) att_prefetch_k(it, vring, s_kbar);   // cached rows: earlier steps'
+        if (attn && t == 0) {                                    // cached rows: earlier steps'
+            att_prefetch_k(it, vring, s_kbar);
+            // the rest of the history towards L2, once per (row, KV head): K past the two staged
+            // chunks, and V, which is requested only when the scores are done
+            if (ah % group == 0 && ads == 0) {
+                if (alen > 2 * ATB_CHUNK) mk_prefetch_l2(Kc + (int64_t)2 * ATB_CHUNK * d, (int64_t)(alen - 2 * ATB_CHUNK) * d * 4);
+                mk_prefetch_l2(Vc, (int64_t)alen * d * 4);
+            }
+        }
         prefetch_layer(l + 1);
         if (!attn) stage_gu(W);
+#pragma unroll 1
         for (int i = t; i < H / 4; i += MK_THREADS) {        // the norms' gains, waited for before use
             cp_async16(gain_in + 4 * i, W.in_norm + 4 * i);
             cp_async16(gain_post + 4 * i, W.post_norm + 4 * i);
@@ -444,6 +498,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
 
         // ---- A: input norm + quantization, q/k/v rows with the bias ----
         if (l == 0) {
+#pragma unroll 1
             for (int i = t; i < m * H; i += MK_THREADS) {
                 const int64_t id = a.ids[i / H];
                 const float v = (id >= 0 && id < a.vocab) ? a.embed[id * H + i % H] : 0.0f;
@@ -452,11 +507,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             }
             __syncthreads();
         } else {
-            const bool ok = mk_poll(m * H, tag(l - 1, 1), [&](int i) { return a.xt + i; }, [&](int i, uint32_t v) {
-                const float f = __uint_as_float(v);
-                xrow[i] = f;
-                sq[i] = fmul(f, f);
-            });
+            const bool ok = mk_poll_into(a.xt, m * H, tag(l - 1, 1), MK_TO_ROWS, xrow, sq, nullptr, nullptr, nullptr);
             if (__syncthreads_or(!ok)) return;
         }
         stamp(l, 1);
@@ -466,6 +517,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         {
             const int row = q0 + warp;
             const bool ok = row < q1;
+#pragma unroll 1
             for (int r = 0; r < m; ++r) {
                 const float sum = wq.dot(xq + r * H, xs + r * (H / QBLOCK), H / CHUNK, lane);
                 if (ok && lane == 0)
@@ -486,6 +538,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             }, [&](int i, uint32_t v) { e[i] = __uint_as_float(v); });   // q | k | v as written, RoPE below
             if (__syncthreads_or(!ok)) return;
             stamp(l, 4);
+#pragma unroll 1
             for (int i = t; i < 3 * d; i += MK_THREADS) {
                 const int which = i / d, c = i % d;
                 if (which == 2) {
@@ -500,6 +553,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             }
             __syncthreads();
             if (ah % group == 0 && ads == 0)
+#pragma unroll 1
                 for (int c = t; c < d; c += MK_THREADS) {
                     Kc[(int64_t)apos * d + c] = kn[c];
                     Vc[(int64_t)apos * d + c] = vn[c];
@@ -527,15 +581,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         stamp(l, 8);
         {
             mk_offsets(term, m, Hq / QBLOCK, s_offs);
-            float sum[MK_ROWS];
-#pragma unroll
-            for (int r = 0; r < MK_ROWS; ++r)
-                if (r < m && orow_ok) sum[r] = wo.dot(xq + r * Hq, xs + r * (Hq / QBLOCK), Hq / CHUNK, lane);
+            if (orow_ok) {                              // one copy of the dot: rows in a loop
+#pragma unroll 1
+                for (int r = 0; r < m; ++r) {
+                    const float v = wo.dot(xq + r * Hq, xs + r * (Hq / QBLOCK), Hq / CHUNK, lane);
+                    if (lane == 0) s_dot[r][warp] = v;
+                }
+            }
             __syncthreads();
 #pragma unroll
             for (int r = 0; r < MK_ROWS; ++r) {
                 if (r < m && orow_ok && lane == 0) {
-                    res[r] = fadd(res[r], fmul(fsub(sum[r], s_offs[r]), sc_o));
+                    res[r] = fadd(res[r], fmul(fsub(s_dot[r][warp], s_offs[r]), sc_o));
                     mk_st(a.xt + (int64_t)r * H + orow, __float_as_uint(res[r]), tag(l, 0));
                 }
             }
@@ -550,11 +607,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
 
         // ---- D: post-attention norm + quantization, gate/up blocks, SiLU * up, quantization ----
         {
-            const bool ok = mk_poll(m * H, tag(l, 0), [&](int i) { return a.xt + i; }, [&](int i, uint32_t v) {
-                const float f = __uint_as_float(v);
-                xrow[i] = f;
-                sq[i] = fmul(f, f);
-            });
+            const bool ok = mk_poll_into(a.xt, m * H, tag(l, 0), MK_TO_ROWS, xrow, sq, nullptr, nullptr, nullptr);
             if (__syncthreads_or(!ok)) return;
         }
         stamp(l, 10);
@@ -571,22 +624,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         stamp(l, 12);
         {
             const int j = lane % MK_GU_LPR;
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const int row = lr + 32 * p;
-                if (32 * p >= gun) break;                                 // the same in every lane
+            const int passes = gun > QBLOCK ? 2 : (gun > 0 ? 1 : 0);    // the same in every lane
+#pragma unroll 1
+            for (int pr = 0; pr < passes * m; ++pr) {                    // (pass, row) pairs
+                const int p = pr / m, r = pr % m, row = lr + 32 * p;
                 const uint8_t *grow = gus + (row < gun ? row : 0) * H, *urow = grow + 2 * QBLOCK * H;
-                for (int r = 0; r < m; ++r) {
-                    const float g = mk_dot_smem<MK_GU_LPR>(grow, xq + r * H, xs + r * (H / QBLOCK), H / CHUNK, j);
-                    const float u = mk_dot_smem<MK_GU_LPR>(urow, xq + r * H, xs + r * (H / QBLOCK), H / CHUNK, j);
-                    if (row < gun && j == 0) {
-                        const float off = s_offs[r];
-                        s_hout[r][row] = swiglu(fmul(fsub(g, off), sg[p]), fmul(fsub(u, off), su[p]), tab);
-                    }
+                float g, u;
+                mk_dot2_smem<MK_GU_LPR>(grow, urow, xq + r * H, xs + r * (H / QBLOCK), H / CHUNK, j, &g, &u);
+                if (row < gun && j == 0) {
+                    const float off = s_offs[r];
+                    s_hout[r][row] = swiglu(fmul(fsub(g, off), p ? sg[1] : sg[0]), fmul(fsub(u, off), p ? su[1] : su[0]), tab);
                 }
             }
             __syncthreads();
             const int ub = gun / QBLOCK;
+#pragma unroll 1
             for (int wb = warp; wb < m * ub; wb += MK_WARPS) {
                 const int r = wb / ub, blk = wb % ub;
                 int8_t qv;
@@ -604,15 +656,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         stamp(l, 14);
         {
             mk_offsets(term, m, I / QBLOCK, s_offs);
-            float sum[MK_ROWS];
-#pragma unroll
-            for (int r = 0; r < MK_ROWS; ++r)
-                if (r < m && orow_ok) sum[r] = wd.dot(xq + r * I, xs + r * (I / QBLOCK), I / CHUNK, lane);
+            if (orow_ok) {                              // one copy of the dot: rows in a loop
+#pragma unroll 1
+                for (int r = 0; r < m; ++r) {
+                    const float v = wd.dot(xq + r * I, xs + r * (I / QBLOCK), I / CHUNK, lane);
+                    if (lane == 0) s_dot[r][warp] = v;
+                }
+            }
             __syncthreads();
 #pragma unroll
             for (int r = 0; r < MK_ROWS; ++r) {
                 if (r < m && orow_ok && lane == 0) {
-                    res[r] = fadd(res[r], fmul(fsub(sum[r], s_offs[r]), sc_d));
+                    res[r] = fadd(res[r], fmul(fsub(s_dot[r][warp], s_offs[r]), sc_d));
                     mk_st(a.xt + (int64_t)r * H + orow, __float_as_uint(res[r]), tag(l, 1));
                 }
             }
@@ -630,14 +685,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
 
     // the final norm of row b (nanocompile/nn.py:34-38) for the LM head
     if (b < m) {
-        const bool ok = mk_poll(H, tag(a.nl - 1, 1), [&](int i) { return a.xt + (int64_t)b * H + i; }, [&](int i, uint32_t v) {
-            const float f = __uint_as_float(v);
-            xrow[i] = f;
-            sq[i] = fmul(f, f);
-        });
+        const bool ok = mk_poll_into(a.xt + (int64_t)b * H, H, tag(a.nl - 1, 1), MK_TO_ROWS, xrow, sq, nullptr, nullptr, nullptr);
         if (__syncthreads_or(!ok)) return;
         if (t == 0) s_inv[0] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(chain_sum(sq, H), (float)H), a.eps)));
         __syncthreads();
+#pragma unroll 1
         for (int i = t; i < H; i += MK_THREADS) a.normed[(int64_t)b * H + i] = fmul(fmul(xrow[i], s_inv[0]), a.final_norm[i]);
     }
     // the last CTA out advances the launch number

@@ -40,19 +40,27 @@ __global__ void gather_kernel(float *__restrict__ out, const int64_t *__restrict
 // ---- block quantization of a row held in shared memory --------------------------------------
 // Warp w quantizes blocks w, w + nwarps, ... (nanocompile/quantize.py:102-124), up to N of
 // them at once so their divisions overlap; writes xq / xs / block sums and leaves each block's
-// offset term float(sum_b) * scale_b in term[b].
+// offset term float(sum_b) * scale_b in term[b].  With gain set, the row is first normalized on
+// the way in, x * inv * gain (nanocompile/nn.py:34-38, the same two rounded products as a separate
+// pass), and the normalized values also go to normed (nullable).
 template <int N = 8>
 __device__ __forceinline__ void quantize_row_smem(const float *row, int n, int8_t *xq, float *xs, int32_t *bsums,
-                                                  float *term, int warp, int nwarps, int lane) {
+                                                  float *term, int warp, int nwarps, int lane,
+                                                  const float *gain = nullptr, float inv = 1.0f, float *normed = nullptr) {
     const int blocks = n / QBLOCK;
+#pragma unroll 1
     for (int b0 = warp; b0 < blocks; b0 += N * nwarps) {
         float v[N], scale[N];
         int8_t q[N];
         int bs[N];
 #pragma unroll
         for (int u = 0; u < N; ++u) {
-            const int b = b0 + u * nwarps;
-            v[u] = b < blocks ? row[b * QBLOCK + lane] : 0.0f;
+            const int b = b0 + u * nwarps, i = b * QBLOCK + lane;
+            v[u] = b < blocks ? row[i] : 0.0f;
+            if (gain && b < blocks) {
+                v[u] = fmul(fmul(v[u], inv), gain[i]);
+                if (normed) normed[i] = v[u];
+            }
         }
         quantize_blocks_warp<N>(v, q, scale, bs);
 #pragma unroll
@@ -101,29 +109,37 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
     __shared__ __align__(16) float s_term[256];
     const int b = blockIdx.x;
     // a thread requests four values of a row at once (one round trip per 1024 values)
-    auto stage = [&](float *dst, const float *src) {
+    // (and, with squares set, their squares x*x)
+    auto stage = [&](float *dst, const float *src, float *squares) {
         for (int i0 = threadIdx.x; i0 < n; i0 += 4 * NORM_THREADS) {
             float v[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) v[u] = i0 + u * NORM_THREADS < n ? src[i0 + u * NORM_THREADS] : 0.0f;
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-                if (i0 + u * NORM_THREADS < n) dst[i0 + u * NORM_THREADS] = v[u];
+                if (i0 + u * NORM_THREADS < n) {
+                    dst[i0 + u * NORM_THREADS] = v[u];
+                    if (squares) squares[i0 + u * NORM_THREADS] = fmul(v[u], v[u]);
+                }
         }
     };
     release_dependents();
-    stage(ws, w);
+    stage(ws, w, nullptr);
     wait_for_producer();
     const int64_t in_row = row_map ? row_map[b] : b;
-    stage(row, x + in_row * n);
+    stage(row, x + in_row * n, sq);
     __syncthreads();
-    rms_norm_smem(row, sq, ws, n, eps, &s_inv);
-    if (normed)
-        for (int i = threadIdx.x; i < n; i += NORM_THREADS) normed[(int64_t)b * n + i] = row[i];
-    if (!xq) return;
+    if (threadIdx.x == 0) s_inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(chain_sum(sq, n), (float)n), eps)));
+    __syncthreads();
+    const float inv = s_inv;
+    float *nrow = normed ? normed + (int64_t)b * n : nullptr;
+    if (!xq) {
+        for (int i = threadIdx.x; i < n; i += NORM_THREADS) nrow[i] = fmul(fmul(row[i], inv), ws[i]);
+        return;
+    }
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = n / QBLOCK;
     quantize_row_smem(row, n, xq + (int64_t)b * n, xs + (int64_t)b * blocks, bsums ? bsums + (int64_t)b * blocks : nullptr,
-                      s_term, warp, NORM_THREADS / 32, lane);
+                      s_term, warp, NORM_THREADS / 32, lane, ws, inv, nrow);
     __syncthreads();
     if (threadIdx.x == 0) offset[b] = fmul(chain_sum(s_term, blocks), 128.0f);
 }
