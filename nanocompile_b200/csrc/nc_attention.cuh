@@ -827,20 +827,30 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     float4 qr[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) qr[c] = reinterpret_cast<const float4 *>(q)[c];
+    // thread t reads row t of a staged K chunk: its 16-byte piece u of box b sits at
+    // b * 256 * 32 + t * 32 + ((u ^ (t % 8)) * 4) floats, one register per u
+    int koff[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) koff[u] = t * ATB_BOX + ((u ^ (t & 7)) << 2);
 #pragma unroll 1
     for (int ci = 0; ci < nk; ++ci) {
         const int s = ci & 1;
         const bool ok = mbar_wait_bounded(&kbar[s], (kpar >> s) & 1u);
         kpar ^= 1u << s;
         if (__syncthreads_or(!ok)) return false;
+        float *stage = ring + s * ATT_KSTAGE;
+        if (it.own_new && ci == nk - 1) {                 // the new key replaces row pos of the chunk
+            const int row = it.pos - ci * ATB_CHUNK;
+            for (int c = t; c < 64; c += ATT_THREADS) stage[staged_index<64, true>(row, c)] = kn[c];
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+        }
         const int j = ci * ATB_CHUNK + t;
         if (j < len) {
-            const float *stage = ring + s * ATT_KSTAGE;
-            const bool fresh = it.own_new && j == it.pos;
             float acc = 0.0f;
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
-                const float4 kv = fresh ? reinterpret_cast<const float4 *>(kn)[c] : staged_piece<64, true>(stage, t, c);
+                const float4 kv = *reinterpret_cast<const float4 *>(stage + (c >> 3) * ATB_CHUNK * ATB_BOX + koff[c & 7]);
                 acc = fadd(acc, fmul(qr[c].x, kv.x));
                 acc = fadd(acc, fmul(qr[c].y, kv.y));
                 acc = fadd(acc, fmul(qr[c].z, kv.z));
@@ -887,22 +897,46 @@ __device__ __forceinline__ bool att_item_tma(const AttnItem &it, const float *q,
     __syncthreads();
     if (st && t == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st[1]));
     // P.V: warp 0's lanes own the slice's 32 dimensions, positions in order; element (row j,
-    // column c) of a swizzled stage sits at j*32 + ((c/4) ^ (j%8))*4 + c%4
+    // column c) of a swizzled stage sits at j*32 + ((c/4) ^ (j%8))*4 + c%4, so row 8k + u of
+    // lane c is voff[u] + 256 k: eight registers, then immediate offsets over 32 positions
     float acc = 0.0f;
     bool vok = true;
     if (warp == 0) {
         const int cl = lane & 3, cu = lane >> 2;
+        int voff[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) voff[u] = u * ATB_BOX + ((cu ^ u) << 2) + cl;
 #pragma unroll 1
         for (int ci = 0; ci < nk; ++ci) {
             const int s = ci & 3;
             vok = __all_sync(0xffffffffu, mbar_wait_bounded(&vbar[s], (vpar >> s) & 1u));
             vpar ^= 1u << s;
             if (!vok) break;
-            const float *cv = ring + s * ATT_VSTAGE + cl;
+            const float *cv = ring + s * ATT_VSTAGE;
             const float *pp = e + ci * ATB_CHUNK;
             const int n = min(ATB_CHUNK, len - ci * ATB_CHUNK);
             const int stop = (it.own_new && ci == nk - 1) ? n - 1 : n;    // the new row comes from vn
-            acc = pv_chain(acc, pp, stop, [&](int j) { return cv[j * ATB_BOX + ((cu ^ (j & 7)) << 2)]; });
+            int j = 0;
+#pragma unroll 2
+            for (; j + 32 <= stop; j += 32) {
+                float v[32];
+                float4 pv[8];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[8 * k + u] = cv[j * ATB_BOX + k * 8 * ATB_BOX + voff[u]];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) pv[k] = *reinterpret_cast<const float4 *>(pp + j + 4 * k);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    acc = fadd(acc, fmul(pv[k].x, v[4 * k]));
+                    acc = fadd(acc, fmul(pv[k].y, v[4 * k + 1]));
+                    acc = fadd(acc, fmul(pv[k].z, v[4 * k + 2]));
+                    acc = fadd(acc, fmul(pv[k].w, v[4 * k + 3]));
+                }
+            }
+#pragma unroll 1
+            for (; j < stop; ++j) acc = fadd(acc, fmul(pp[j], cv[j * ATB_BOX + (((cu ^ (j & 7)) << 2) | cl)]));
             if (stop != n) acc = fadd(acc, fmul(pp[n - 1], vn[it.ds * ATB_BOX + lane]));
             __syncwarp();
             if (lane == 0 && ci + 4 < nk) {
