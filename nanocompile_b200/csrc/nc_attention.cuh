@@ -215,10 +215,9 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
     constexpr int SP = 2, SH = 4;                     // scores: positions x heads per thread
     constexpr int SROWS = ATB_CHUNK / SP;             // position groups of a chunk
     constexpr int S_THREADS = SROWS * ((G + SH - 1) / SH);
-    constexpr int PV_HEADS = 1;                       // P.V: (dimension pair, PV_HEADS heads)
-    constexpr int DP = D / 2, PV_THREADS = DP * ((G + PV_HEADS - 1) / PV_HEADS);
+    constexpr int DP = D / 2, PV_THREADS = DP * G;     // P.V: (dimension pair, one head)
     constexpr int QUADS = ATB_CHUNK / 4;              // exps: four positions of one head per item
-    static_assert(S_THREADS % 32 == 0 && S_THREADS <= ATB_THREADS, "scoring warps");
+    static_assert(S_THREADS % 32 == 0 && S_THREADS <= ATB_THREADS && SROWS % 8 == 0, "scoring warps");
     static_assert(ATB_THREADS - PV_THREADS >= 32, "threads left for the divisions");
     extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ uint64_t bars[ATB_STAGES];
@@ -351,6 +350,11 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
     float mx[SH];
 #pragma unroll
     for (int h = 0; h < SH; ++h) mx[h] = __uint_as_float(0xff800000u);
+    // TMA stages: piece c of row pq + i * SROWS sits at (c / 8) * CHUNK * BOX + i * SROWS * BOX +
+    // koff[c % 8] (the rows agree modulo 8), so the K loads take no index arithmetic
+    int koff[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) koff[u] = pq * ATB_BOX + ((u ^ (pq & 7)) << 2);
     int failed_at = -1;
     for (int ci = 0; ci < nk; ++ci) {
         const bool ok = ready(ci);
@@ -369,7 +373,12 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             for (int c = 0; c < PPR; ++c) {
                 float4 kr[SP];
 #pragma unroll
-                for (int i = 0; i < SP; ++i) kr[i] = staged_piece<D, TMA>(st, pq + i * SROWS, c);
+                for (int i = 0; i < SP; ++i) {
+                    if constexpr (TMA)
+                        kr[i] = *reinterpret_cast<const float4 *>(st + (c >> 3) * ATB_CHUNK * ATB_BOX + i * SROWS * ATB_BOX + koff[c & 7]);
+                    else
+                        kr[i] = staged_piece<D, TMA>(st, pq + i * SROWS, c);
+                }
 #pragma unroll
                 for (int h = 0; h < SH; ++h) {
                     const float4 x = reinterpret_cast<const float4 *>(q + (hb + h) * D)[c];
@@ -456,12 +465,14 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         __syncthreads();
     }
     {
-        // ---- probabilities @ V: thread (dimension pair, PV_HEADS heads), positions in order ----
-        // A warp takes 32 dimension pairs of one head: per position one 8-byte V load per thread
-        // and the head's probability as a broadcast, the loads of the next eight positions issued
-        // before the products of the current eight. The divisions e / sum of a chunk are made by
-        // the threads without P.V work while the P.V threads consume the chunk before it (chunk 0
-        // before the loop); the barrier that opens each chunk orders the two.
+        // ---- probabilities @ V: thread (dimension pair, one head), positions in order ----
+        // A warp takes the 32 dimension pairs of one head: per position one 8-byte V load per
+        // thread and the head's probability (a broadcast, four at a time); eight positions per
+        // step, the next step's loads issued before the current step's chains (two register sets
+        // in turn). Row u (mod 8) of a staged chunk keeps the thread's pair at voff[u] (the
+        // 128-byte swizzle), so the loads take no index arithmetic. The divisions e / sum of a
+        // chunk are made by the threads without P.V work while the P.V threads consume the chunk
+        // before it (chunk 0 before the loop); the barrier that opens each chunk orders the two.
         const bool pv = t < PV_THREADS;
         auto divide_chunk = [&](int ci) {
             if (pv || ci >= nk) return;
@@ -472,18 +483,17 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             }
         };
         divide_chunk(0);
-        const int dim = 2 * (t % DP), hq = PV_HEADS * (t / DP);
-        const float *pr[PV_HEADS];
-#pragma unroll
-        for (int i = 0; i < PV_HEADS; ++i) pr[i] = e + min(hq + i, G - 1) * cap4;   // past G: discarded
-        // where row k (mod 8) of a staged V chunk keeps this thread's two dimensions (adjacent)
+        const int dim = 2 * (t % DP), hq = min(t / DP, G - 1);       // past PV_THREADS: unused
+        const float *pr = e + hq * cap4;
         int voff[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) voff[k] = staged_index<D, TMA>(k, dim);
         constexpr int VROW8 = TMA ? 8 * ATB_BOX : 8 * D;  // floats from row j to row j + 8 (same box)
-        float acc[PV_HEADS][2];
-#pragma unroll
-        for (int i = 0; i < PV_HEADS; ++i) acc[i][0] = acc[i][1] = 0.0f;
+        float acc[2] = {0.0f, 0.0f};
+        struct Step {
+            float4 p[2];
+            float2 v[8];
+        };
         for (int ci = 0; ci < nk; ++ci) {
             const int idx = nk + ci;
             const bool ok = ready(idx);
@@ -495,51 +505,43 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             divide_chunk(ci + 1);
             if (pv) {
                 const int n = min(ATB_CHUNK, len - j0), n8 = n & ~7;
+                auto load = [&](int j, Step &x) {
+                    x.p[0] = *reinterpret_cast<const float4 *>(pr + j0 + j);
+                    x.p[1] = *reinterpret_cast<const float4 *>(pr + j0 + j + 4);
+                    const float *vr = st + (j / 8) * VROW8;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) x.v[k] = *reinterpret_cast<const float2 *>(vr + voff[k]);
+                };
+                auto step = [&](const Step &x) {
+                    const float pk[8] = {x.p[0].x, x.p[0].y, x.p[0].z, x.p[0].w, x.p[1].x, x.p[1].y, x.p[1].z, x.p[1].w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        acc[0] = fadd(acc[0], fmul(pk[k], x.v[k].x));
+                        acc[1] = fadd(acc[1], fmul(pk[k], x.v[k].y));
+                    }
+                };
                 int jj = 0;
                 if (n8) {
-                    float4 pc[PV_HEADS][2];
-                    float2 vc[8];
-                    auto load = [&](int j, float4 (&pd)[PV_HEADS][2], float2 (&vd)[8]) {
-#pragma unroll
-                        for (int i = 0; i < PV_HEADS; ++i) {
-                            pd[i][0] = *reinterpret_cast<const float4 *>(pr[i] + j0 + j);
-                            pd[i][1] = *reinterpret_cast<const float4 *>(pr[i] + j0 + j + 4);
-                        }
-                        const float *vr = st + (j / 8) * VROW8;
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) vd[k] = *reinterpret_cast<const float2 *>(vr + voff[k]);
-                    };
-                    load(0, pc, vc);
-                    for (; jj < n8; jj += 8) {
-                        float4 pn[PV_HEADS][2];
-                        float2 vx[8];
-                        load(min(jj + 8, n8 - 8), pn, vx);      // the last step reloads a step already made
-#pragma unroll
-                        for (int i = 0; i < PV_HEADS; ++i) {
-                            const float pk[8] = {pc[i][0].x, pc[i][0].y, pc[i][0].z, pc[i][0].w,
-                                                 pc[i][1].x, pc[i][1].y, pc[i][1].z, pc[i][1].w};
-#pragma unroll
-                            for (int k = 0; k < 8; ++k) {
-                                acc[i][0] = fadd(acc[i][0], fmul(pk[k], vc[k].x));
-                                acc[i][1] = fadd(acc[i][1], fmul(pk[k], vc[k].y));
-                            }
-                        }
-#pragma unroll
-                        for (int i = 0; i < PV_HEADS; ++i) {
-                            pc[i][0] = pn[i][0];
-                            pc[i][1] = pn[i][1];
-                        }
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) vc[k] = vx[k];
+                    Step A, B;
+                    load(0, A);
+#pragma unroll 1
+                    for (; jj + 16 <= n8; jj += 16) {
+                        load(jj + 8, B);
+                        step(A);
+                        load(min(jj + 16, n8 - 8), A);     // past the last step: a reload, unused
+                        step(B);
+                    }
+                    if (jj < n8) {
+                        step(A);
+                        jj += 8;
                     }
                 }
+#pragma unroll 1
                 for (; jj < n; ++jj) {
                     const float2 v = *reinterpret_cast<const float2 *>(st + staged_index<D, TMA>(jj, dim));
-#pragma unroll
-                    for (int i = 0; i < PV_HEADS; ++i) {
-                        acc[i][0] = fadd(acc[i][0], fmul(pr[i][j0 + jj], v.x));
-                        acc[i][1] = fadd(acc[i][1], fmul(pr[i][j0 + jj], v.y));
-                    }
+                    const float pj = pr[j0 + jj];
+                    acc[0] = fadd(acc[0], fmul(pj, v.x));
+                    acc[1] = fadd(acc[1], fmul(pj, v.y));
                 }
             }
         }
@@ -549,18 +551,9 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         const int width = a.heads * D;
         __syncthreads();
         if (pv) {
-#pragma unroll
-            for (int i = 0; i < PV_HEADS; ++i) {
-                const int h = hq + i;
-                if (h < G) {
-                    if (a.ctx) {
-                        a.ctx[(int64_t)r * width + (h0 + h) * D + dim] = acc[i][0];
-                        a.ctx[(int64_t)r * width + (h0 + h) * D + dim + 1] = acc[i][1];
-                    }
-                    q[h * D + dim] = acc[i][0];
-                    q[h * D + dim + 1] = acc[i][1];
-                }
-            }
+            const float2 o = make_float2(acc[0], acc[1]);
+            if (a.ctx) *reinterpret_cast<float2 *>(a.ctx + (int64_t)r * width + (h0 + hq) * D + dim) = o;
+            *reinterpret_cast<float2 *>(q + hq * D + dim) = o;
         }
         if (a.q_out) {
             __syncthreads();

@@ -138,8 +138,8 @@ norm_quant_kernel(float *__restrict__ normed, const float *__restrict__ x, const
         return;
     }
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, blocks = n / QBLOCK;
-    quantize_row_smem(row, n, xq + (int64_t)b * n, xs + (int64_t)b * blocks, bsums ? bsums + (int64_t)b * blocks : nullptr,
-                      s_term, warp, NORM_THREADS / 32, lane, ws, inv, nrow);
+    quantize_row_smem<4>(row, n, xq + (int64_t)b * n, xs + (int64_t)b * blocks, bsums ? bsums + (int64_t)b * blocks : nullptr,
+                         s_term, warp, NORM_THREADS / 32, lane, ws, inv, nrow);
     __syncthreads();
     if (threadIdx.x == 0) offset[b] = fmul(chain_sum(s_term, blocks), 128.0f);
 }
