@@ -18,8 +18,8 @@
 // costs one trip through L2 and there is no grid-wide barrier. A CTA's own o/down rows keep the
 // residual stream in registers. Every CTA loads the weights (and scales) of its next phase into
 // registers (gate/up: shared memory, by cp.async) before it starts waiting for that phase's inputs,
-// and asks L2 for its weights of the next layer at the start of each layer; attention's V slice
-// comes into shared memory by cp.async at the start of the layer.
+// and asks L2 for its weights of the next layer at the start of each layer; an attention CTA
+// requests its first two K chunks (TMA) and asks L2 for the rest of the K and V history there too.
 //
 // Every value is computed with the same float32 operations in the same order as the separate
 // kernels (norm_quant_kernel, gemv_i8_fused_kernel, attention_split_kernel), which follow
@@ -143,24 +143,28 @@ __device__ __forceinline__ unsigned long long mk_now() {
     return v;
 }
 
+constexpr int MK_POLL_WORDS = 4;
+
 // Reads words addr(0) .. addr(n-1) until each carries tag, handing (index, value) to store; up to
-// four words per thread are in flight together. False (and g_mk_fault set) when the wait gave up.
+// MK_POLL_WORDS words per thread are in flight together (a hand-over of up to
+// MK_POLL_WORDS * MK_THREADS words takes one round trip once the words are there). False (and
+// g_mk_fault set) when the wait gave up.
 template <typename A, typename F>
 __device__ __forceinline__ bool mk_poll(int n, uint32_t tag, A &&addr, F &&store, long long limit = NC_DRAIN_CYCLES) {
     const long long t0 = clock64();
 #pragma unroll 1
-    for (int base = threadIdx.x; base < n; base += 4 * MK_THREADS) {
-        bool pend[4];
+    for (int base = threadIdx.x; base < n; base += MK_POLL_WORDS * MK_THREADS) {
+        bool pend[MK_POLL_WORDS];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) pend[u] = base + u * MK_THREADS < n;
+        for (int u = 0; u < MK_POLL_WORDS; ++u) pend[u] = base + u * MK_THREADS < n;
         for (;;) {
-            unsigned long long v[4];
+            unsigned long long v[MK_POLL_WORDS];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < MK_POLL_WORDS; ++u)
                 if (pend[u]) v[u] = mk_ld(addr(base + u * MK_THREADS));
             bool any = false;
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < MK_POLL_WORDS; ++u)
                 if (pend[u]) {
                     if ((uint32_t)(v[u] >> 32) == tag) {
                         store(base + u * MK_THREADS, (uint32_t)v[u]);
