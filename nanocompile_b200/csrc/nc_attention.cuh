@@ -215,7 +215,7 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
     constexpr int SP = 2, SH = 4;                     // scores: positions x heads per thread
     constexpr int SROWS = ATB_CHUNK / SP;             // position groups of a chunk
     constexpr int S_THREADS = SROWS * ((G + SH - 1) / SH);
-    constexpr int DP = D / 2, PV_THREADS = DP * G;     // P.V: (dimension pair, one head)
+    constexpr int DP = D / 2, PV_THREADS = DP * ((G + 1) / 2);   // P.V: (dimension pair, two heads)
     constexpr int QUADS = ATB_CHUNK / 4;              // exps: four positions of one head per item
     static_assert(S_THREADS % 32 == 0 && S_THREADS <= ATB_THREADS && SROWS % 8 == 0, "scoring warps");
     static_assert(ATB_THREADS - PV_THREADS >= 32, "threads left for the divisions");
@@ -379,17 +379,27 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
                     else
                         kr[i] = staged_piece<D, TMA>(st, pq + i * SROWS, c);
                 }
+                // the eight chains advance component by component (x, y, z, w of the piece),
+                // so consecutive adds belong to different chains
+                float4 qx[SH];
 #pragma unroll
-                for (int h = 0; h < SH; ++h) {
-                    const float4 x = reinterpret_cast<const float4 *>(q + (hb + h) * D)[c];
+                for (int h = 0; h < SH; ++h) qx[h] = reinterpret_cast<const float4 *>(q + (hb + h) * D)[c];
 #pragma unroll
-                    for (int i = 0; i < SP; ++i) {
-                        acc[i][h] = fadd(acc[i][h], fmul(x.x, kr[i].x));
-                        acc[i][h] = fadd(acc[i][h], fmul(x.y, kr[i].y));
-                        acc[i][h] = fadd(acc[i][h], fmul(x.z, kr[i].z));
-                        acc[i][h] = fadd(acc[i][h], fmul(x.w, kr[i].w));
-                    }
-                }
+                for (int h = 0; h < SH; ++h)
+#pragma unroll
+                    for (int i = 0; i < SP; ++i) acc[i][h] = fadd(acc[i][h], fmul(qx[h].x, kr[i].x));
+#pragma unroll
+                for (int h = 0; h < SH; ++h)
+#pragma unroll
+                    for (int i = 0; i < SP; ++i) acc[i][h] = fadd(acc[i][h], fmul(qx[h].y, kr[i].y));
+#pragma unroll
+                for (int h = 0; h < SH; ++h)
+#pragma unroll
+                    for (int i = 0; i < SP; ++i) acc[i][h] = fadd(acc[i][h], fmul(qx[h].z, kr[i].z));
+#pragma unroll
+                for (int h = 0; h < SH; ++h)
+#pragma unroll
+                    for (int i = 0; i < SP; ++i) acc[i][h] = fadd(acc[i][h], fmul(qx[h].w, kr[i].w));
             }
 #pragma unroll
             for (int i = 0; i < SP; ++i) {
@@ -465,12 +475,13 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         __syncthreads();
     }
     {
-        // ---- probabilities @ V: thread (dimension pair, one head), positions in order ----
-        // A warp takes the 32 dimension pairs of one head: per position one 8-byte V load per
-        // thread and the head's probability (a broadcast, four at a time); eight positions per
-        // step, the next step's loads issued before the current step's chains (two register sets
-        // in turn). Row u (mod 8) of a staged chunk keeps the thread's pair at voff[u] (the
-        // 128-byte swizzle), so the loads take no index arithmetic. The divisions e / sum of a
+        // ---- probabilities @ V: thread (dimension pair, two heads), positions in order ----
+        // A warp takes the 32 dimension pairs of two heads: per position one 8-byte V load per
+        // thread (the row read once for both heads: with one head per warp, shared-memory
+        // wavefronts bounded this loop) and the two heads' probabilities (broadcasts, four at a
+        // time); eight positions per step, the next step's loads issued before the current
+        // step's chains (two register sets in turn). Row u (mod 8) of a staged chunk keeps the
+        // thread's pair at voff[u] (the 128-byte swizzle), so the loads take no index arithmetic. The divisions e / sum of a
         // chunk are made by the threads without P.V work while the P.V threads consume the chunk
         // before it (chunk 0 before the loop); the barrier that opens each chunk orders the two.
         const bool pv = t < PV_THREADS;
@@ -483,15 +494,15 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             }
         };
         divide_chunk(0);
-        const int dim = 2 * (t % DP), hq = min(t / DP, G - 1);       // past PV_THREADS: unused
-        const float *pr = e + hq * cap4;
+        const int dim = 2 * (t % DP), hq = 2 * (t / DP);            // heads hq, hq + 1 (if < G)
+        const float *pr0 = e + min(hq, G - 1) * cap4, *pr1 = e + min(hq + 1, G - 1) * cap4;
         int voff[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) voff[k] = staged_index<D, TMA>(k, dim);
         constexpr int VROW8 = TMA ? 8 * ATB_BOX : 8 * D;  // floats from row j to row j + 8 (same box)
-        float acc[2] = {0.0f, 0.0f};
+        float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
         struct Step {
-            float4 p[2];
+            float4 p[2][2];
             float2 v[8];
         };
         for (int ci = 0; ci < nk; ++ci) {
@@ -506,18 +517,29 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
             if (pv) {
                 const int n = min(ATB_CHUNK, len - j0), n8 = n & ~7;
                 auto load = [&](int j, Step &x) {
-                    x.p[0] = *reinterpret_cast<const float4 *>(pr + j0 + j);
-                    x.p[1] = *reinterpret_cast<const float4 *>(pr + j0 + j + 4);
+                    x.p[0][0] = *reinterpret_cast<const float4 *>(pr0 + j0 + j);
+                    x.p[0][1] = *reinterpret_cast<const float4 *>(pr0 + j0 + j + 4);
+                    x.p[1][0] = *reinterpret_cast<const float4 *>(pr1 + j0 + j);
+                    x.p[1][1] = *reinterpret_cast<const float4 *>(pr1 + j0 + j + 4);
                     const float *vr = st + (j / 8) * VROW8;
 #pragma unroll
                     for (int k = 0; k < 8; ++k) x.v[k] = *reinterpret_cast<const float2 *>(vr + voff[k]);
                 };
+                // the four chains (two heads x two dimensions) advance together, position by
+                // position, so each add has three others to hide its latency behind
                 auto step = [&](const Step &x) {
-                    const float pk[8] = {x.p[0].x, x.p[0].y, x.p[0].z, x.p[0].w, x.p[1].x, x.p[1].y, x.p[1].z, x.p[1].w};
+                    const float pk[2][8] = {{x.p[0][0].x, x.p[0][0].y, x.p[0][0].z, x.p[0][0].w,
+                                             x.p[0][1].x, x.p[0][1].y, x.p[0][1].z, x.p[0][1].w},
+                                            {x.p[1][0].x, x.p[1][0].y, x.p[1][0].z, x.p[1][0].w,
+                                             x.p[1][1].x, x.p[1][1].y, x.p[1][1].z, x.p[1][1].w}};
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
-                        acc[0] = fadd(acc[0], fmul(pk[k], x.v[k].x));
-                        acc[1] = fadd(acc[1], fmul(pk[k], x.v[k].y));
+                        const float m00 = fmul(pk[0][k], x.v[k].x), m01 = fmul(pk[0][k], x.v[k].y);
+                        const float m10 = fmul(pk[1][k], x.v[k].x), m11 = fmul(pk[1][k], x.v[k].y);
+                        acc[0][0] = fadd(acc[0][0], m00);
+                        acc[0][1] = fadd(acc[0][1], m01);
+                        acc[1][0] = fadd(acc[1][0], m10);
+                        acc[1][1] = fadd(acc[1][1], m11);
                     }
                 };
                 int jj = 0;
@@ -539,9 +561,11 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
 #pragma unroll 1
                 for (; jj < n; ++jj) {
                     const float2 v = *reinterpret_cast<const float2 *>(st + staged_index<D, TMA>(jj, dim));
-                    const float pj = pr[j0 + jj];
-                    acc[0] = fadd(acc[0], fmul(pj, v.x));
-                    acc[1] = fadd(acc[1], fmul(pj, v.y));
+                    const float p0 = pr0[j0 + jj], p1 = pr1[j0 + jj];
+                    acc[0][0] = fadd(acc[0][0], fmul(p0, v.x));
+                    acc[0][1] = fadd(acc[0][1], fmul(p0, v.y));
+                    acc[1][0] = fadd(acc[1][0], fmul(p1, v.x));
+                    acc[1][1] = fadd(acc[1][1], fmul(p1, v.y));
                 }
             }
         }
@@ -551,9 +575,14 @@ attention_batched_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap k
         const int width = a.heads * D;
         __syncthreads();
         if (pv) {
-            const float2 o = make_float2(acc[0], acc[1]);
-            if (a.ctx) *reinterpret_cast<float2 *>(a.ctx + (int64_t)r * width + (h0 + hq) * D + dim) = o;
-            *reinterpret_cast<float2 *>(q + hq * D + dim) = o;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                if (hq + i < G) {
+                    const float2 o = make_float2(acc[i][0], acc[i][1]);
+                    if (a.ctx) *reinterpret_cast<float2 *>(a.ctx + (int64_t)r * width + (h0 + hq + i) * D + dim) = o;
+                    *reinterpret_cast<float2 *>(q + (hq + i) * D + dim) = o;
+                }
+            }
         }
         if (a.q_out) {
             __syncthreads();
