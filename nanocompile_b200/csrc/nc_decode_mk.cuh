@@ -17,9 +17,10 @@
 // consumer reads the words it needs until every one carries the expected tag, so the hand-over
 // costs one trip through L2 and there is no grid-wide barrier. A CTA's own o/down rows keep the
 // residual stream in registers. Every CTA loads the weights (and scales) of its next phase into
-// registers (gate/up: shared memory, by cp.async) before it starts waiting for that phase's inputs,
-// and asks L2 for its weights of the next layer at the start of each layer; an attention CTA
-// requests its first two K chunks (TMA) and asks L2 for the rest of the K and V history there too.
+// registers (gate/up and down rows: shared memory, by bulk copies) before it starts waiting for
+// that phase's inputs, and asks L2 for its weights of the next layer at the start of each layer;
+// an attention CTA requests its first two K chunks (TMA) and asks L2 for the rest of the K and V
+// history there too.
 //
 // Every value is computed with the same float32 operations in the same order as the separate
 // kernels (norm_quant_kernel, gemv_i8_fused_kernel, attention_split_kernel), which follow
@@ -82,7 +83,8 @@ struct MkArgs {
 
 // dynamic shared memory: the layer table | gains [2][H] | rows / squares [m][H] | quantized
 // activations [m][max(H, Hq, I)] | block scales, terms, sums [m][blocks] | attention
-// probabilities [cap4] | V stages, later the gate/up rows | q/k/v [3][d] | cos/sin [d]
+// probabilities [cap4] | K / V stages, then the gate/up rows, then the down rows | q/k/v [3][d] |
+// cos/sin [d]
 struct MkSmem {
     int layers, gain, xrow, sq, xq, xs, term, bsum, e, vring, qkn, cs;
     int bytes;
@@ -362,7 +364,8 @@ __device__ __forceinline__ void mk_offsets(const float *term, int m, int blocks,
     if (warp == MK_WARPS - 1 && lane < m) offs[lane] = fmul(chain_sum(term + lane * blocks, blocks), 128.0f);
 }
 
-// NCH / NCHD: the chunks of a hidden-wide / MLP-wide weight row that a lane's registers hold.
+// NCH: the chunks of a hidden-wide weight row that a lane's registers hold (q/k/v and o rows);
+// NCHD bounds an MLP-wide row (the down rows come through shared memory).
 // kvmap: the KV arena as rows of d floats, 32 x 256 boxes with the 128-byte swizzle.
 template <int NCH, int NCHD>
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a, const __grid_constant__ CUtensorMap kvmap) {
@@ -371,7 +374,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
     __shared__ float s_inv[MK_ROWS], s_offs[MK_ROWS], s_red[MK_WARPS];
     __shared__ float s_hout[MK_ROWS][2 * QBLOCK];
     __shared__ float s_dot[MK_ROWS][MK_WARPS];
-    __shared__ __align__(8) uint64_t s_kbar[2], s_vbar[4], s_gbar;
+    __shared__ __align__(8) uint64_t s_kbar[2], s_vbar[4], s_gbar, s_dbar;
     __shared__ float s_scal[3];
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31, b = blockIdx.x, G = gridDim.x;
     const int H = a.H, I = a.I, m = a.m, d = a.d, Hq = a.heads * a.d, Nqkv = (a.heads + 2 * a.kv) * a.d;
@@ -391,9 +394,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         for (int s = 0; s < 2; ++s) mbar_init(&s_kbar[s], 1);
         for (int s = 0; s < 4; ++s) mbar_init(&s_vbar[s], 1);
         mbar_init(&s_gbar, 1);
+        mbar_init(&s_dbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    unsigned kpar = 0, vpar = 0, gpar = 0;              // mbarrier phases: K, V (warp 0), gate/up
+    unsigned kpar = 0, vpar = 0, gpar = 0, dpar = 0;    // mbarrier phases: K, V (warp 0), gate/up, down
     for (int i = t; i < a.nl * (int)sizeof(MkLayer) / 8; i += MK_THREADS)
         reinterpret_cast<uint64_t *>(layers)[i] = reinterpret_cast<const uint64_t *>(a.layers)[i];
     const uint32_t launch = (a.sync[1] + 1u) & 0xffffffu;
@@ -449,7 +453,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
         mk_prefetch_l2(W.wd + (int64_t)o0 * I, (int64_t)(o1 - o0) * I);
     };
     MkSlice<32, NCH> wq, wo;
-    MkSlice<32, NCHD> wd;
     uint8_t *gus = reinterpret_cast<uint8_t *>(vring);           // gate rows [64][H], then up rows
     auto stage_gu = [&](const MkLayer &W) {       // this CTA's gate/up rows: one bulk copy per matrix
         if (t != 0) return;
@@ -641,6 +644,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
                 }
             }
             __syncthreads();
+            // the gate/up rows are read: this CTA's down rows take their place, one bulk copy
+            // that lands while the SwiGLU blocks are handed over
+            if (t == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_expect_tx(&s_dbar, (unsigned)((o1 - o0) * I));
+                if (o1 > o0) bulk_copy_g2s(gus, W.wd + (int64_t)o0 * I, (unsigned)((o1 - o0) * I), &s_dbar);
+            }
             const int ub = gun / QBLOCK;
 #pragma unroll 1
             for (int wb = warp; wb < m * ub; wb += MK_WARPS) {
@@ -652,18 +662,25 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a
             }
         }
         stamp(l, 13);
-        wd.load(W.wd + (int64_t)orow * I, I / CHUNK, lane, orow_ok);
         const float sc_d = orow_ok ? mk_ldf(W.sd + orow) : 0.0f;
 
         // ---- E: down rows with the residual add ----
         if (!mk_take_blocks(a.hqt, tag(l, 4), m, I, xq, xs, term, bsum)) return;
         stamp(l, 14);
         {
+            {
+                const bool ok = mbar_wait_bounded(&s_dbar, dpar);
+                dpar ^= 1u;
+                if (__syncthreads_or(!ok)) {
+                    if (t == 0) atomicExch(&g_mk_fault, 1u);
+                    return;
+                }
+            }
             mk_offsets(term, m, I / QBLOCK, s_offs);
             if (orow_ok) {                              // one copy of the dot: rows in a loop
 #pragma unroll 1
                 for (int r = 0; r < m; ++r) {
-                    const float v = wd.dot(xq + r * I, xs + r * (I / QBLOCK), I / CHUNK, lane);
+                    const float v = mk_dot_smem<32>(gus + (int64_t)warp * I, xq + r * I, xs + r * (I / QBLOCK), I / CHUNK, lane);
                     if (lane == 0) s_dot[r][warp] = v;
                 }
             }
