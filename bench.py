@@ -564,6 +564,8 @@ def main() -> int:
     parser.add_argument("--records", default=str(ROOT / "gpurun_out" / "phase6_results.jsonl"))
     parser.add_argument("--projections", type=int, default=0, metavar="ROWS",
                         help="time the batched int8 projection entry points alone at ROWS rows")
+    parser.add_argument("--prefill-only", action="store_true",
+                        help="time configuration 4 alone (STEPS timed steps after 2) and print its object")
     parser.add_argument("--cpu-steps", type=int, default=8)
     parser.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (profiling runs only)")
     parser.add_argument("--past", type=int, default=PAST, help="cached positions at the first step (profiling runs only)")
@@ -576,6 +578,9 @@ def main() -> int:
         return 0
     if args.projections:
         print(json.dumps(run_projections(args.projections, max(args.steps, 1))), flush=True)
+        return 0
+    if args.prefill_only:
+        print(json.dumps(run_prefill(QWEN2_0_5B, synthetic_weights(QWEN2_0_5B, seed=0), 0, max(args.steps, 1))), flush=True)
         return 0
     if args.impl == "reference":
         line = run_reference(args)
