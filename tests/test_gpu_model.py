@@ -231,6 +231,30 @@ def test_05b_small_batched_decode_is_the_references(cuda, qwen05b_vnni_weights, 
     model.close()
 
 
+def test_persistent_step_phase_table(cuda, qwen05b_vnni_weights):
+    """The persistent step's globaltimer phase table: every phase boundary reached, in the
+    order the phases run, within one layer's time; the stamps leave the decoded tokens alone; a
+    batch the persistent kernel does not serve is refused."""
+    g = golden("batch")
+    past = int(g["past"])
+    model = cuda.DeviceModel(QWEN2_0_5B, qwen05b_vnni_weights, "int8", max_rows=8, slots=8, capacity=past + 64)
+    k, v, t = synthetic_cache(QWEN2_0_5B, 5, past)
+    model.kv_write(0, 0, k, v)
+    phases = model.phase_times([t], [0], [past], 2)
+    assert list(phases) == list(model.PHASES)
+    order = ["input words in", "input norm", "q/k/v rows out", "q/k/v words in", "scores", "softmax",
+             "attention out", "attention blocks in", "o rows out", "residual words in", "post norm",
+             "gate/up staged", "SwiGLU out", "SwiGLU in", "down rows out"]
+    times = [phases[name] for name in order]
+    assert all(0.0 <= a <= b for a, b in zip(times, times[1:])), phases
+    assert 0.0 < phases["down rows out"] < 1000.0
+    tokens, _ = model.decode([t], [0], [past], 8)
+    assert np.array_equal(tokens[:, 0], g["tokens"][5, 1:9])
+    with pytest.raises(cuda.InterpreterError, match="persistent decode kernel does not serve"):
+        model.phase_times([t] * 5, list(range(5)), [past] * 5, 1)
+    model.close()
+
+
 def test_05b_device_quantized_weights_decode_the_same(cuda, qwen05b_weights, qwen05b_vnni_weights):
     """float32 projections uploaded and quantized on the device give the host quantizer's bytes:
     the same 24 greedy tokens as the golden run."""
