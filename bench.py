@@ -418,7 +418,7 @@ def run_prefill(cfg, weights, dev: int, iters: int) -> dict:
             "tensor_frac_of_nominal_int8": round(tops / INT8_DENSE_TOPS, 4),
             "projection_tensor_frac_of_nominal_int8": round(proj_tops / INT8_DENSE_TOPS, 4) if proj_tops else None,
             "note": "useful int8 ops 2*512*357.8M over the step time; the projections run on the dp4a kernels "
-                    "(the tcgen05 kind::i8 kernel, NC_TC_I8=1, is slower: profiles/gemm_i8_tc_kernel_bs64.md)",
+                    "(the tcgen05 kind::i8 kernel, NC_TC_I8=1, measured slower)",
             "kernel_shares": {k: round(v[0] / total, 3) for k, v in sorted(kinds.items(), key=lambda x: -x[1][0])}}
 
 
