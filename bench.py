@@ -72,7 +72,18 @@ class RankGroup:
                 torch.cuda.set_device(self.local)
                 self.device = torch.device("cuda", self.local)
                 kwargs["device_id"] = self.device
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
+            # the communicators are made here, with the process's stdout pointed at stderr: the
+            # library may print a version banner, and rank 0's stdout must carry one JSON line
+            sys.stdout.flush()
+            saved = os.dup(1)
+            os.dup2(2, 1)
+            try:
+                dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
+                dist.barrier()
+            finally:
+                sys.stdout.flush()
+                os.dup2(saved, 1)
+                os.close(saved)
             self.dist = dist
             self.torch = torch
 
