@@ -991,6 +991,7 @@ struct nc_model {
     float *lm_xhi = nullptr, *lm_xlo = nullptr;   // the normed rows as pre-swizzled 64 x 32 tiles
     bool tc_head = false;
     float wmax = 0.0f;              // max |w| of the embedding (set when it is uploaded)
+    float wnorm = 0.0f;             // max over its rows of the row's 2-norm, rounded up (likewise)
     float *cand_val = nullptr, *cta_best = nullptr, *lm_delta = nullptr;
     int32_t *cand_idx = nullptr, *cand_cnt = nullptr;
     // the int8-prefiltered LM head (decode steps of up to LMQ_MAXM rows that need only the tokens)
@@ -1354,7 +1355,7 @@ int32_t enqueue_step(nc_model *m, int rows, int logit_rows, bool fused, bool tok
         la.xhi = m->lm_xhi; la.xlo = m->lm_xlo;
         const int ctas = (int)((c.vocab + LMT_ROWS - 1) / LMT_ROWS);
         CUDA_TRY(launch_k(lm_prep_kernel, logit_rows, 256, 0, st, m->lm_xhi, m->lm_xlo, m->lm_delta,
-                          (const float *)m->normed, H, m->wmax));
+                          (const float *)m->normed, H, m->wmax, m->wnorm));
         NC_TRY(check_launch("lm_prep_kernel"));
         CUDA_TRY(allow_smem(lm_head_tc_kernel, LMT_SMEM));
         CUDA_TRY(launch_k(lm_head_tc_kernel, dim3(ctas, (logit_rows + LMT_TOK - 1) / LMT_TOK), LMT_THREADS, LMT_SMEM,
@@ -1631,6 +1632,15 @@ extern "C" int32_t nc_qwen2_upload(nc_model *m, const char *name, const void *ho
             if (a > mx) mx = a;
         }
         m->wmax = mx;
+        // the largest row 2-norm, summed in double and rounded up to a float
+        double nmax = 0.0;
+        const int64_t hid = m->c.hidden, rows = bytes / 4 / hid;
+        for (int64_t r = 0; r < rows && mx == mx; ++r) {
+            double q = 0.0;
+            for (int64_t i = 0; i < hid; ++i) q += (double)w[r * hid + i] * (double)w[r * hid + i];
+            nmax = std::max(nmax, std::sqrt(q));
+        }
+        m->wnorm = mx == mx ? std::nextafter((float)nmax, INFINITY) : mx;
         if (m->tc_head) {
             lm_tiles_kernel<<<1184, 256, 0, m->stream>>>(m->lm_tiles, m->embed, (int)m->c.vocab, (int)m->c.hidden);
             NC_TRY(check_launch("lm_tiles_kernel"));

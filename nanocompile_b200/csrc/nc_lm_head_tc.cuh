@@ -24,7 +24,11 @@
 // per product |w x - approx| <= (2^-10 + 2^-21) |w||x| (w's dropped bits, x_lo's), and the two
 // float32 sums (the reference's in order, the tensor core's) add at most 2 K 2^-24 sum_k |w_k||x_k|;
 // with sum_k |w_k||x_k| <= max|w| sum_k |x_k|, delta = 2^-8 max(1, K/2048) max|w| sum_k |x_k|
-// covers twice the total. The best exact row is then within delta of the best approximation, so
+// covers twice the total. By Cauchy-Schwarz sum_k |w_k||x_k| <= ||w_row||_2 ||x||_2 as well, so
+// the margin takes the smaller of max|w| sum|x| and max_row ||w_row||_2 ||x||_2 (the latter with
+// a factor 1 + 2^-10 for the float32 sum of squares; the row norms come from the host in double,
+// rounded up): for weights without outliers the second is several times tighter, and every row it
+// leaves out needs no exact recheck. The best exact row is then within delta of the best approximation, so
 // it is always a candidate. A CTA whose candidates overflow its list, or that saw a NaN or +inf,
 // hands all of its rows to the pick kernel, which recomputes them exactly. A bounded wait that
 // gives up records a fault in g_attention_fault (the host turns it into an error) and also hands
@@ -134,15 +138,16 @@ __global__ void lm_tiles_kernel(float *__restrict__ dst, const float *__restrict
 // floats one 8 KB swizzled image) and its margin delta[m].
 __global__ void __launch_bounds__(256) lm_prep_kernel(float *__restrict__ xhi, float *__restrict__ xlo,
                                                       float *__restrict__ delta, const float *__restrict__ x, int k,
-                                                      float wmax) {
-    __shared__ float part[8];
+                                                      float wmax, float wnorm) {
+    __shared__ float part[8], part2[8];
     const int m = blockIdx.x, t = threadIdx.x, tb = m / LMT_TOK, r = m % LMT_TOK, kt_n = k / LMT_KT;
     release_dependents();
     wait_for_producer();
-    float acc = 0.0f;
+    float acc = 0.0f, acc2 = 0.0f;
     for (int c = t; c < k / 4; c += 256) {
         float4 v = *reinterpret_cast<const float4 *>(x + (int64_t)m * k + 4 * c);
         acc += fabsf(v.x) + fabsf(v.y) + fabsf(v.z) + fabsf(v.w);
+        acc2 += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         float4 lo = v;
         split_tf32(&v, &lo);
         const int kt = c / 8, u = c % 8;
@@ -150,13 +155,26 @@ __global__ void __launch_bounds__(256) lm_prep_kernel(float *__restrict__ xhi, f
         *reinterpret_cast<float4 *>(xhi + at) = v;
         *reinterpret_cast<float4 *>(xlo + at) = lo;
     }
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if ((t & 31) == 0) part[t / 32] = acc;
+    for (int o = 16; o > 0; o >>= 1) {
+        acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        acc2 += __shfl_xor_sync(0xffffffffu, acc2, o);
+    }
+    if ((t & 31) == 0) {
+        part[t / 32] = acc;
+        part2[t / 32] = acc2;
+    }
     __syncthreads();
     if (t == 0) {
-        float sum = 0.0f;
-        for (int i = 0; i < 8; ++i) sum += part[i];
-        delta[m] = 0x1p-8f * fmaxf(1.0f, (float)k / 2048.0f) * wmax * sum;
+        float sum = 0.0f, sq = 0.0f;
+        for (int i = 0; i < 8; ++i) {
+            sum += part[i];
+            sq += part2[i];
+        }
+        const float l1 = wmax * sum, l2 = wnorm * sqrtf(sq) * (1.0f + 0x1p-10f);
+        // fminf passes a NaN on only when both are NaN: keep the NaN (every row rechecked) when
+        // either bound is not a number
+        const float bound = (l1 != l1 || l2 != l2) ? l1 + l2 : fminf(l1, l2);
+        delta[m] = 0x1p-8f * fmaxf(1.0f, (float)k / 2048.0f) * bound;
     }
 }
 
