@@ -8,7 +8,7 @@
 //
 // What changes is the data movement, built for many rows sharing the GPU:
 //  * K and V chunks stream through a ring of shared-memory stages by TMA: a chunk is D/32 tensor
-//    copies of 128 rows x 128 bytes from one 2-D tensor map over the whole KV arena, with 128-byte
+//    copies of 256 rows x 128 bytes from one 2-D tensor map over the whole KV arena, with 128-byte
 //    swizzling, completion counted in bytes on an mbarrier. Many chunks are in flight per SM at no
 //    instruction cost, and the swizzle lets a thread read one whole K row without bank conflicts.
 //    Where no tensor map can describe the cache (its extent is not known, or the head dimension is
@@ -21,10 +21,10 @@
 //    rows and q pieces of four heads per step of four dimensions: eight chains).
 //  * The exps of chunk c + 1 are made by fifteen warps while warp 0 adds chunk c to the in-order
 //    sums of its G heads.
-//  * Probabilities are kept head-major ([8][cap]); a P.V warp takes one head, a thread two
-//    adjacent dimensions (two chains): one 8-byte V load and one broadcast probability per
-//    position, no padding head. V is read through offsets precomputed for the eight swizzle
-//    phases.
+//  * Probabilities are kept head-major ([8][cap]); a P.V warp takes two heads, a thread two
+//    adjacent dimensions of both (four chains): one 8-byte V load, read once for the two heads,
+//    and two broadcast probabilities per position. K and V are read through offsets precomputed
+//    for the eight swizzle phases.
 //  * The chunk holding the new position gets the new k / v row written into its stage, so the
 //    scores and P.V read one layout.
 //  * Decode streams the K history (cached by earlier steps) from before the wait on the previous

@@ -441,7 +441,7 @@ int32_t launch_attention_g(cudaStream_t st, const AttnArgs &a, int rows) {
     return check_launch("attention_kernel");
 }
 
-// A 2-D tensor map over a KV arena seen as rows of d floats (rows < 2^31): 128-row x 32-float
+// A 2-D tensor map over a KV arena seen as rows of d floats (rows < 2^31): 256-row x 32-float
 // boxes, 128-byte swizzle. cuTensorMapEncodeTiled comes from the driver through the runtime.
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
