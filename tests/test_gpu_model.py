@@ -196,6 +196,29 @@ def test_05b_batched_decode_is_the_references(reference, cuda, qwen05b_weights):
     assert np.array_equal(tokens, expected[:, 1:])
 
 
+def test_05b_batched_decode_logits_are_the_references(cuda, qwen05b_vnni_weights):
+    """Configuration 5's logits, not only its tokens: every row of the first and of the 64th batched
+    step has the SHA-1 of the reference's float32 logits (the step then takes the exact float32 LM
+    head, so this holds the 24 layers and the final norm of all 64 sequences to the bit)."""
+    import hashlib
+
+    g = golden("batch")
+    past = int(g["past"])
+    model = cuda.DeviceModel(QWEN2_0_5B, qwen05b_vnni_weights, "int8", max_rows=64, slots=64, capacity=past + 72)
+    first = []
+    for b in range(64):
+        k, v, t = synthetic_cache(QWEN2_0_5B, b, past)
+        model.kv_write(b, 0, k, v)
+        first.append(t)
+    for steps in (1, 64):
+        tokens, logits = model.decode(first, list(range(64)), [past] * 64, steps, want_logits=True)
+        assert np.array_equal(tokens.T, g["tokens"][:, 1:steps + 1])
+        for b in range(64):
+            digest = np.frombuffer(hashlib.sha1(np.ascontiguousarray(logits[b]).tobytes()).digest(), np.uint8)
+            assert np.array_equal(digest, g["sha1"][b, steps - 1]), (steps, b)
+    model.close()
+
+
 def test_05b_batched_decode_on_tensor_core_projections(cuda, qwen05b_vnni_weights, monkeypatch):
     """Configuration 5's first 16 steps with the tcgen05 kind::i8 projections (NC_TC_I8=1)."""
     monkeypatch.setenv("NC_TC_I8", "1")
