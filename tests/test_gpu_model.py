@@ -163,6 +163,18 @@ def test_05b_int8_vnni_step_logits_are_the_references(vnni_05b):
     assert np.array_equal(bits(g["samples"][47]), bits(lg[::1009]))
 
 
+def test_05b_int8_vnni_every_step_logits_through_the_device_cache(vnni_05b, cuda):
+    """All 993 steps of configuration 3 with the history in HBM (the persistent decode step for
+    the one-row steps): the SHA-1 of every step's float32 logits is the reference's."""
+    g = golden("qwen05b_vnni")
+    cache = cuda.new_device_cache(vnni_05b, 1100)
+    pending = list(g["prompt"])
+    for step in range(len(g["tokens"])):
+        lg = cache.forward(pending, last_only=True)[0]
+        assert np.array_equal(sha1(lg), g["sha1"][step]), step
+        pending = [int(g["tokens"][step])]
+
+
 def test_05b_prefill_512_is_the_references(vnni_05b, cuda):
     """Configuration 4: one step over 512 prompt tokens at past 0, host and device caches."""
     g = golden("prefill")
