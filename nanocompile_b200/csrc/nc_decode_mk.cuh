@@ -329,8 +329,10 @@ __device__ __forceinline__ void mk_dot2_smem(const uint8_t *grow, const uint8_t 
 }
 
 // rms_norm (nanocompile/nn.py:34-38) of the m rows in xrow (squares in sq) with gain, then block
-// quantization (nanocompile/quantize.py:102-124) into xq / xs and the offsets.
-__device__ __forceinline__ void mk_norm_quant(int m, int H, float eps, const float *gain, float *xrow, const float *sq,
+// quantization (nanocompile/quantize.py:102-124) into xq / xs and the offsets. Out of line: one
+// copy serves both norms of a layer, which keeps the per-layer loop's code near 110 KB (measured
+// 1.3% faster per token than two inlined copies).
+__device__ __noinline__ void mk_norm_quant(int m, int H, float eps, const float *gain, float *xrow, const float *sq,
                                               int8_t *xq, float *xs, float *term, float *offs, float *s_inv) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31, blocks = H / QBLOCK;
     if (lane == 0 && warp < m)
